@@ -1,0 +1,135 @@
+// Shared helpers for the single-source simulator core.
+//
+// Every simulation routine is written once as a __host__ __device__ function.
+// On the GPU one thread block (CTA) owns one environment and the PAR_FOR /
+// BARRIER macros spread an element loop across the block's threads with a
+// __syncthreads() between dependent phases. On the host the same source runs
+// serially for one environment per OpenMP thread. Routines therefore keep
+// per-element state in the environment's scratch arrays (shared memory on the
+// GPU), never in registers that must survive a barrier.
+#pragma once
+
+#include <cstdint>
+#include <cmath>
+
+#if defined(__CUDACC__)
+#define AD_HD __host__ __device__ __forceinline__
+#define AD_DEV __device__ __forceinline__
+#else
+#define AD_HD inline
+#define AD_DEV inline
+#endif
+
+#if defined(__CUDA_ARCH__)
+#define AD_TID ((int)threadIdx.x)
+#define AD_NT ((int)blockDim.x)
+#define PAR_FOR(i, n) for (int i = (int)threadIdx.x; i < (int)(n); i += (int)blockDim.x)
+#define BARRIER() __syncthreads()
+#define SERIAL_BEGIN if (threadIdx.x == 0) {
+#define SERIAL_END }
+#else
+#define AD_TID 0
+#define AD_NT 1
+#define PAR_FOR(i, n) for (int i = 0; i < (int)(n); ++i)
+#define BARRIER() ((void)0)
+#define SERIAL_BEGIN {
+#define SERIAL_END }
+#endif
+
+namespace ad {
+
+constexpr float kPi = 3.14159265358979323846f;
+constexpr float kTwoPi = 6.28318530717958647692f;
+constexpr float kG = 9.81f;
+constexpr float kInf = 1e30f;
+
+AD_HD float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi); }
+AD_HD float sgnf(float v) { return v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f); }
+AD_HD float sqr(float v) { return v * v; }
+AD_HD int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// Wrap an angle to [-pi, pi) with the floor-remainder convention used by the
+// simulator everywhere a heading is wrapped: remainder(a + pi, 2 pi) - pi.
+AD_HD float wrap_angle(float a) {
+  float r = fmodf(a + kPi, kTwoPi);
+  if (r < 0.f) r += kTwoPi;
+  return r - kPi;
+}
+
+// Signed shortest angular difference atan2(sin d, cos d).
+AD_HD float angle_diff(float a, float b) {
+  float d = a - b;
+  return atan2f(sinf(d), cosf(d));
+}
+
+struct V2 { float x, y; };
+struct V3 { float x, y, z; };
+
+AD_HD V3 cross3(V3 a, V3 b) {
+  return V3{a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x};
+}
+AD_HD float dot3(V3 a, V3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+AD_HD float norm3(V3 a) { return sqrtf(dot3(a, a)); }
+AD_HD float cross2(float ax, float ay, float bx, float by) { return ax * by - ay * bx; }
+
+// ---------------------------------------------------------------------------
+// Counter-based random numbers: Philox4x32-10 (Salmon, Moraes, Dror, Shaw,
+// "Parallel random numbers: as easy as 1, 2, 3", SC 2011). Each draw is a pure
+// function of (key, counter), so a kernel and its host twin produce identical
+// streams and inactive environments never perturb the draws of active ones.
+// ---------------------------------------------------------------------------
+AD_HD void mulhilo32(uint32_t a, uint32_t b, uint32_t& hi, uint32_t& lo) {
+  uint64_t p = (uint64_t)a * (uint64_t)b;
+  hi = (uint32_t)(p >> 32);
+  lo = (uint32_t)p;
+}
+
+struct U4 { uint32_t x, y, z, w; };
+
+AD_HD U4 philox4x32(U4 ctr, uint32_t k0, uint32_t k1) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u;
+  const uint32_t W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint32_t hi0, lo0, hi1, lo1;
+    mulhilo32(M0, ctr.x, hi0, lo0);
+    mulhilo32(M1, ctr.z, hi1, lo1);
+    ctr = U4{hi1 ^ ctr.y ^ k0, lo1, hi0 ^ ctr.w ^ k1, lo0};
+    k0 += W0;
+    k1 += W1;
+  }
+  return ctr;
+}
+
+// Uniform in [0, 1) with 24 bits of mantissa.
+AD_HD float u01(uint32_t v) { return (float)(v >> 8) * (1.0f / 16777216.0f); }
+
+// Box-Muller transform (Box & Muller 1958) of two uniforms into one normal.
+AD_HD float normal_from(uint32_t a, uint32_t b) {
+  float u1 = fmaxf(u01(a), 1e-7f);
+  float u2 = u01(b);
+  return sqrtf(-2.f * logf(u1)) * cosf(kTwoPi * u2);
+}
+
+// Stream identifiers keep the draw families of one tick disjoint.
+enum RngStream : uint32_t {
+  RNG_RESET = 1,
+  RNG_PERCEPTION = 2,
+  RNG_OPPONENT = 3,
+  RNG_LAUNCH = 4,
+  RNG_POLICY = 5,
+  RNG_DEFENSE = 6,
+};
+
+struct Rng {
+  uint32_t k0, k1;
+  // counter = (env, tick, stream, element)
+  AD_HD U4 draw(uint32_t env, uint32_t tick, uint32_t stream, uint32_t elem) const {
+    return philox4x32(U4{env, tick, stream, elem}, k0, k1);
+  }
+  AD_HD float uniform(uint32_t env, uint32_t tick, uint32_t stream, uint32_t elem) const {
+    return u01(draw(env, tick, stream, elem).x);
+  }
+};
+
+}  // namespace ad

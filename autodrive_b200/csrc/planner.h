@@ -1,0 +1,354 @@
+// Grid route planner for one (environment, robot) row.
+//
+// Reference behaviour (frc_defense/tensor_adstar.py:1108-1468): footprint-
+// inflated occupancy at the measured chassis heading, teammate/opponent
+// chassis inflation, blocked start/goal projection to a nearby free cell,
+// 8-connected cost-to-go by Jacobi Bellman sweeps with corner cutting blocked
+// and a bump traversal penalty, greedy descent extraction (<= 72 points),
+// line-of-sight shortcutting and a curvature/braking speed profile.
+//
+// On the GPU one CTA owns one route with the whole grid (occupancy + two value
+// buffers) in shared memory; the Bellman sweeps run until a sweep changes no
+// cell (block-wide vote) or the sweep budget is spent.
+#pragma once
+
+#include "game.h"
+
+namespace ad {
+
+struct PlanScratch {
+  uint8_t* blocked;   // [nx*ny]
+  float* value;       // [nx*ny]
+  float* value2;      // [nx*ny]
+  float* path;        // [kPathPoints*2]
+  float* tmp;         // [kPathPoints*2 + 4]
+  int* misc;          // [8]
+};
+
+AD_HD int cell_index(const SimParams& sp, int ix, int iy) { return ix * sp.plan_ny + iy; }
+AD_HD float cell_x(const SimParams& sp, int ix) { return ((float)ix + .5f) * sp.plan_res; }
+AD_HD float cell_y(const SimParams& sp, int iy) { return ((float)iy + .5f) * sp.plan_res; }
+
+AD_HD bool cell_on_bump(const SimParams& sp, float x, float y) {
+  for (int b = 0; b < sp.num_bumps; ++b) {
+    const Box& bx = sp.bumps[b];
+    if (fabsf(x - bx.cx) <= bx.hx && fabsf(y - bx.cy) <= bx.hy) return true;
+  }
+  return false;
+}
+
+// Segment sampled at half-cell spacing crosses no blocked cell.
+AD_HD bool grid_line_clear(const SimParams& sp, const uint8_t* blocked, float x0, float y0, float x1, float y1) {
+  float dx = x1 - x0, dy = y1 - y0;
+  int steps = (int)ceilf(fmaxf(fabsf(dx), fabsf(dy)) / (sp.plan_res * .5f));
+  steps = steps < 1 ? 1 : steps;
+  for (int k = 1; k <= steps; ++k) {
+    float f = (float)k / (float)steps;
+    int ix = clampi((int)floorf((x0 + dx * f) / sp.plan_res), 0, sp.plan_nx - 1);
+    int iy = clampi((int)floorf((y0 + dy * f) / sp.plan_res), 0, sp.plan_ny - 1);
+    if (blocked[cell_index(sp, ix, iy)]) return false;
+  }
+  return true;
+}
+
+struct PlanRequest {
+  float sx, sy, gx, gy, heading, length, width, speed, lat_mu, accel;
+  // perceived robot obstacles (x, y, radius), radius <= 0 disables a slot
+  float obst[kMaxRobots * 3];
+  int num_obst;
+};
+
+// Plan one route. Writes the persistent route state of row (e, r).
+AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanRequest& q, PlanScratch& ps) {
+  const int nx = sp.plan_nx, ny = sp.plan_ny, nc = nx * ny;
+  const size_t er = (size_t)e * sp.R + r;
+  // trench alignment hint: crossing a trench x-line from inside a clear opening
+  bool trench = false;
+  float heading = q.heading;
+  {
+    float lane_low = 0.f, lane_high = sp.field_width;
+    bool have = false;
+    float trench_x[2];
+    int tcount = 0;
+    // trench supports are the solid boxes whose y is not the field centre
+    for (int b = 0; b < sp.num_boxes; ++b) {
+      const Box& bx = sp.boxes[b];
+      bool support = fabsf(bx.cy - sp.field_width * .5f) > 1.5f && bx.hy < .3f && bx.hx > .5f;
+      if (!support) continue;
+      if (bx.cy < sp.field_width * .5f) lane_low = fmaxf(lane_low, bx.cy - bx.hy);
+      else lane_high = have ? fminf(lane_high, bx.cy + bx.hy) : bx.cy + bx.hy;
+      have = true;
+      bool seen = false;
+      for (int k = 0; k < tcount; ++k) seen = seen || fabsf(trench_x[k] - bx.cx) < 1e-3f;
+      if (!seen && tcount < 2) trench_x[tcount++] = bx.cx;
+    }
+    if (have) {
+      float lo = fminf(q.sx, q.gx), hi = fmaxf(q.sx, q.gx);
+      bool crosses = false;
+      for (int k = 0; k < tcount; ++k) crosses = crosses || (trench_x[k] >= lo && trench_x[k] <= hi);
+      float hw = q.width * .5f;
+      bool opening = (q.sy >= hw && q.sy <= lane_low - hw) || (q.sy >= lane_high + hw && q.sy <= sp.field_width - hw);
+      trench = crosses && opening;
+      if (trench) heading = q.gx >= q.sx ? 0.f : kPi;
+    }
+  }
+  // occupancy at the measured heading
+  const float ch = cosf(q.heading), sh = sinf(q.heading);
+  const float ac = fabsf(ch), as = fabsf(sh);
+  const float ex = (q.length * ac + q.width * as) * .5f, ey = (q.length * as + q.width * ac) * .5f;
+  const float mover = .5f * fminf(q.length, q.width);
+  PAR_FOR(c, nc) {
+    int ix = c / ny, iy = c % ny;
+    float x = cell_x(sp, ix), y = cell_y(sp, iy);
+    bool b = x < ex || x > sp.field_length - ex || y < ey || y > sp.field_width - ey;
+    for (int k = 0; k < sp.num_boxes && !b; ++k) {
+      const Box& bx = sp.boxes[k];
+      float dx = x - bx.cx, dy = y - bx.cy;
+      if (fabsf(dx) > bx.hx + ex || fabsf(dy) > bx.hy + ey) continue;
+      float fwd = dx * ch + dy * sh, lat = -dx * sh + dy * ch;
+      float sf = q.length * .5f + bx.hx * ac + bx.hy * as;
+      float sl = q.width * .5f + bx.hx * as + bx.hy * ac;
+      b = fabsf(fwd) <= sf && fabsf(lat) <= sl;
+    }
+    for (int k = 0; k < q.num_obst && !b; ++k) {
+      float rr = q.obst[k * 3 + 2];
+      if (!(rr > 0.f)) continue;
+      float cl = mover + rr;
+      b = sqr(x - q.obst[k * 3]) + sqr(y - q.obst[k * 3 + 1]) <= cl * cl;
+    }
+    ps.blocked[c] = b ? 1 : 0;
+  }
+  BARRIER();
+  SERIAL_BEGIN
+  // project blocked endpoints to the nearest free cell
+  float pts[4] = {q.sx, q.sy, q.gx, q.gy};
+  for (int k = 0; k < 2; ++k) {
+    int ix = clampi((int)floorf(pts[k * 2] / sp.plan_res), 0, nx - 1);
+    int iy = clampi((int)floorf(pts[k * 2 + 1] / sp.plan_res), 0, ny - 1);
+    if (!ps.blocked[cell_index(sp, ix, iy)]) continue;
+    float best = kInf;
+    int bc = -1;
+    for (int c = 0; c < nc; ++c) {
+      if (ps.blocked[c]) continue;
+      float d = sqr(cell_x(sp, c / ny) - pts[k * 2]) + sqr(cell_y(sp, c % ny) - pts[k * 2 + 1]);
+      if (d < best) {
+        best = d;
+        bc = c;
+      }
+    }
+    if (bc >= 0) {
+      pts[k * 2] = cell_x(sp, bc / ny);
+      pts[k * 2 + 1] = cell_y(sp, bc % ny);
+    }
+  }
+  ps.misc[0] = clampi((int)floorf(pts[0] / sp.plan_res), 0, nx - 1);
+  ps.misc[1] = clampi((int)floorf(pts[1] / sp.plan_res), 0, ny - 1);
+  ps.misc[2] = clampi((int)floorf(pts[2] / sp.plan_res), 0, nx - 1);
+  ps.misc[3] = clampi((int)floorf(pts[3] / sp.plan_res), 0, ny - 1);
+  ps.blocked[cell_index(sp, ps.misc[0], ps.misc[1])] = 0;
+  ps.blocked[cell_index(sp, ps.misc[2], ps.misc[3])] = 0;
+  ps.path[0] = pts[0];
+  ps.path[1] = pts[1];
+  ps.tmp[0] = pts[2];
+  ps.tmp[1] = pts[3];
+  SERIAL_END
+  BARRIER();
+  const int gcell = cell_index(sp, ps.misc[2], ps.misc[3]);
+  PAR_FOR(c, nc) { ps.value[c] = c == gcell ? 0.f : 1.e6f; }
+  BARRIER();
+  // Jacobi Bellman sweeps
+  const int dxs[8] = {1, -1, 0, 0, 1, 1, -1, -1};
+  const int dys[8] = {0, 0, 1, -1, 1, -1, 1, -1};
+  for (int sweep = 0; sweep < sp.plan_sweeps; ++sweep) {
+    int changed = 0;
+    PAR_FOR(c, nc) {
+      float cur = ps.value[c];
+      float best = cur;
+      if (!ps.blocked[c]) {
+        int ix = c / ny, iy = c % ny;
+        float bc = cell_on_bump(sp, cell_x(sp, ix), cell_y(sp, iy)) ? 1.f + sp.bump_cost : 1.f;
+        for (int k = 0; k < 8; ++k) {
+          int jx = ix + dxs[k], jy = iy + dys[k];
+          if (jx < 0 || jx >= nx || jy < 0 || jy >= ny) continue;
+          if (k >= 4 && (ps.blocked[cell_index(sp, jx, iy)] || ps.blocked[cell_index(sp, ix, jy)])) continue;
+          float cand = ps.value[cell_index(sp, jx, jy)] + (k >= 4 ? 1.41421356237f : 1.f) * bc;
+          best = fminf(best, cand);
+        }
+      } else {
+        best = 1.e6f;
+      }
+      ps.value2[c] = best;
+      if (best < cur) changed = 1;
+    }
+#if defined(__CUDA_ARCH__)
+    int any = __syncthreads_or(changed);
+#else
+    int any = changed;
+#endif
+    PAR_FOR(c, nc) { ps.value[c] = ps.value2[c]; }
+    BARRIER();
+    if (!any) break;
+  }
+  SERIAL_BEGIN
+  // greedy descent
+  int px = ps.misc[0], py = ps.misc[1];
+  const int gx = ps.misc[2], gy = ps.misc[3];
+  int len = 1;
+  for (int k = 1; k < kPathPoints; ++k) {
+    if (px == gx && py == gy) break;
+    float best = 1.e6f;
+    int bk = -1;
+    for (int m = 0; m < 8; ++m) {
+      int jx = px + dxs[m], jy = py + dys[m];
+      if (jx < 0 || jx >= nx || jy < 0 || jy >= ny) continue;
+      if (m >= 4 && (ps.blocked[cell_index(sp, jx, py)] || ps.blocked[cell_index(sp, px, jy)])) continue;
+      if (ps.blocked[cell_index(sp, jx, jy)]) continue;
+      float v = ps.value[cell_index(sp, jx, jy)];
+      if (v < best) {
+        best = v;
+        bk = m;
+      }
+    }
+    if (bk < 0 || !(best < ps.value[cell_index(sp, px, py)] - 1e-5f)) break;
+    px += dxs[bk];
+    py += dys[bk];
+    ps.path[len * 2] = cell_x(sp, px);
+    ps.path[len * 2 + 1] = cell_y(sp, py);
+    len++;
+  }
+  // snap the final point onto the resolved goal when the goal cell was reached
+  if (len > 1 && px == gx && py == gy) {
+    ps.path[(len - 1) * 2] = ps.tmp[0];
+    ps.path[(len - 1) * 2 + 1] = ps.tmp[1];
+  }
+  // line-of-sight shortcut: keep the farthest visible point from each anchor
+  int out = 0;
+  if (len > 1) {
+    int anchor = 0;
+    ps.tmp[2] = ps.path[0];
+    ps.tmp[3] = ps.path[1];
+    out = 1;
+    while (anchor < len - 1) {
+      int next = anchor + 1;
+      for (int k = len - 1; k > anchor + 1; --k) {
+        if (grid_line_clear(sp, ps.blocked, ps.path[anchor * 2], ps.path[anchor * 2 + 1], ps.path[k * 2],
+                            ps.path[k * 2 + 1])) {
+          next = k;
+          break;
+        }
+      }
+      ps.tmp[2 + out * 2] = ps.path[next * 2];
+      ps.tmp[2 + out * 2 + 1] = ps.path[next * 2 + 1];
+      out++;
+      anchor = next;
+    }
+  } else {
+    ps.tmp[2] = ps.path[0];
+    ps.tmp[3] = ps.path[1];
+    out = 1;
+  }
+  // densify long segments so the follower sees curvature at corners only
+  float* dst = w.p_path + er * kPathPoints * 2;
+  int n = 0;
+  for (int k = 0; k < out && n < kPathPoints; ++k) {
+    if (k > 0) {
+      float ax = ps.tmp[2 + (k - 1) * 2], ay = ps.tmp[2 + (k - 1) * 2 + 1];
+      float bx = ps.tmp[2 + k * 2], by = ps.tmp[2 + k * 2 + 1];
+      float seg = sqrtf(sqr(bx - ax) + sqr(by - ay));
+      int pieces = (int)ceilf(seg / (2.f * sp.plan_res));
+      for (int m = 1; m < pieces && n < kPathPoints - 1; ++m) {
+        float f = (float)m / (float)pieces;
+        dst[n * 2] = ax + (bx - ax) * f;
+        dst[n * 2 + 1] = ay + (by - ay) * f;
+        n++;
+      }
+    }
+    dst[n * 2] = ps.tmp[2 + k * 2];
+    dst[n * 2 + 1] = ps.tmp[2 + k * 2 + 1];
+    n++;
+  }
+  for (int k = n; k < kPathPoints; ++k) {
+    dst[k * 2] = dst[(n - 1) * 2];
+    dst[k * 2 + 1] = dst[(n - 1) * 2 + 1];
+  }
+  // a one-cell route from start==goal still counts as a single point
+  w.p_len[er] = len > 1 ? n : 1;
+  // speed profile: curvature caps then backward braking envelope
+  float* prof = w.p_profile + er * kPathPoints;
+  const float mu = fmaxf(q.lat_mu, .1f), acc = fmaxf(q.accel, .2f), vcap = fmaxf(q.speed, .1f);
+  const int L = w.p_len[er];
+  float station[kPathPoints];
+  station[0] = 0.f;
+  for (int k = 0; k < kPathPoints - 1; ++k)
+    station[k + 1] = station[k] + sqrtf(sqr(dst[(k + 1) * 2] - dst[k * 2]) + sqr(dst[(k + 1) * 2 + 1] - dst[k * 2 + 1]));
+  for (int k = 0; k < kPathPoints; ++k) {
+    float cap = vcap;
+    if (k > 0 && k < kPathPoints - 1) {
+      float ax = dst[k * 2] - dst[(k - 1) * 2], ay = dst[k * 2 + 1] - dst[(k - 1) * 2 + 1];
+      float bx = dst[(k + 1) * 2] - dst[k * 2], by = dst[(k + 1) * 2 + 1] - dst[k * 2 + 1];
+      float la = sqrtf(ax * ax + ay * ay), lb = sqrtf(bx * bx + by * by);
+      float ua = 1.f / fmaxf(la, 1e-6f), ub = 1.f / fmaxf(lb, 1e-6f);
+      float crs = ax * ua * by * ub - ay * ua * bx * ub, dt2 = ax * ua * bx * ub + ay * ua * by * ub;
+      float turn = fabsf(atan2f(crs, dt2));
+      float arc = fmaxf(.5f * (la + lb), 1e-4f);
+      float curv = turn / arc;
+      if (curv > 1e-6f) cap = fminf(vcap, fminf(sqrtf(mu * kG / curv), sp.steer_rate_limit / curv));
+    }
+    if (k == L - 1) cap = 0.f;
+    prof[k] = cap;
+  }
+  for (int k = 0; k < kPathPoints; ++k) {
+    float best = kInf;
+    for (int j = k; j < L; ++j) best = fminf(best, sqrtf(prof[j] * prof[j] + 2.f * acc * fmaxf(station[j] - station[k], 0.f)));
+    ps.tmp[k] = best;
+  }
+  for (int k = 0; k < kPathPoints; ++k) prof[k] = ps.tmp[k] < kInf ? ps.tmp[k] : vcap;
+  w.p_progress[er] = 0.f;
+  w.p_goal[er * 2] = dst[(L - 1) * 2];
+  w.p_goal[er * 2 + 1] = dst[(L - 1) * 2 + 1];
+  w.p_start[er * 2] = ps.path[0];
+  w.p_start[er * 2 + 1] = ps.path[1];
+  w.p_heading[er] = heading;
+  w.p_trench[er] = trench ? 1 : 0;
+  SERIAL_END
+  BARRIER();
+}
+
+// Build the planner request of row (e, r) from the controller state.
+AD_HD PlanRequest make_plan_request(World& w, const SimParams& sp, int e, int r) {
+  G g{w, sp, e};
+  PlanRequest q;
+  const float* p = g.ppose(r);
+  q.sx = p[0];
+  q.sy = p[1];
+  q.gx = w.c_target[g.er(r) * 2];
+  q.gy = w.c_target[g.er(r) * 2 + 1];
+  q.heading = p[2];
+  bool extended = sp.kind[r] == 1 || w.g_rlatch[g.er(r) * 8 + RL_INTAKE_COLLECTING];
+  q.length = g.param(r, RP_LENGTH) + (extended ? .6096f : 0.f);
+  q.width = g.param(r, RP_WIDTH);
+  q.speed = g.param(r, RP_SPEED);
+  q.lat_mu = g.param(r, RP_LATERAL_MU);
+  q.accel = g.param(r, RP_ACCEL);
+  // known teammates (estimated poses) plus the anonymous opponent track
+  q.num_obst = 0;
+  for (int m = 0; m < sp.R; ++m) {
+    if (sp.team[m] != sp.team[r] || m == r) continue;
+    const float* mp = g.ppose(m);
+    q.obst[q.num_obst * 3] = mp[0];
+    q.obst[q.num_obst * 3 + 1] = mp[1];
+    q.obst[q.num_obst * 3 + 2] = .5f * fminf(g.param(m, RP_LENGTH), g.param(m, RP_WIDTH));
+    q.num_obst++;
+  }
+  const size_t er = g.er(r);
+  const float* os = w.o_size + er * 3;
+  if (w.o_valid[er] && os[0] > 0.f && os[1] > 0.f && q.num_obst < kMaxRobots) {
+    q.obst[q.num_obst * 3] = w.o_pose[er * 3];
+    q.obst[q.num_obst * 3 + 1] = w.o_pose[er * 3 + 1];
+    q.obst[q.num_obst * 3 + 2] = .5f * fminf(os[0], os[1]);
+    q.num_obst++;
+  }
+  return q;
+}
+
+}  // namespace ad

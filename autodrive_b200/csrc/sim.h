@@ -1,0 +1,29 @@
+// Declarations shared by the simulation kernels and the Python bindings.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "planner.h"
+#include "rules.h"
+
+namespace ad {
+
+size_t tick_smem_bytes();
+size_t plan_smem_bytes(const SimParams& sp);
+void validate_params(const SimParams& sp);
+
+void launch_control(const World& w, const SimParams& sp, const int32_t* actions, cudaStream_t st);
+void launch_plan(const World& w, const SimParams& sp, int force, cudaStream_t st);
+void launch_tick(const World& w, const SimParams& sp, uint32_t tick, int run_game, int threads, cudaStream_t st);
+void launch_physics(const World& w, const SimParams& sp, int ticks, int threads, cudaStream_t st);
+void launch_observe(const World& w, const SimParams& sp, cudaStream_t st);
+void launch_perceive(const World& w, const SimParams& sp, int threads, cudaStream_t st);
+
+void host_control(World w, const SimParams& sp, const int32_t* actions);
+void host_plan(World w, const SimParams& sp, int force);
+void host_tick(World w, const SimParams& sp, uint32_t tick, int run_game);
+void host_physics(World w, const SimParams& sp, int ticks);
+void host_observe(World w, const SimParams& sp);
+void host_perceive(World w, const SimParams& sp);
+
+}  // namespace ad

@@ -1,0 +1,38 @@
+"""Build the sm_100a extension in place: ``python setup.py build_ext --inplace``."""
+import os
+
+from setuptools import find_packages, setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("autodrive_b200", "csrc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+ext = CUDAExtension(
+    name="autodrive_b200._C",
+    sources=[os.path.join(CSRC, f) for f in (
+        "bindings.cpp", "sim.cu", "policy_ops.cu", "comm_ops.cu")],
+    include_dirs=[os.path.join(HERE, CSRC)],
+    extra_compile_args={
+        "cxx": ["-O3", "-std=c++17"],
+        "nvcc": ARCH + ["-O3", "-lineinfo", "-std=c++17", "--use_fast_math",
+                        "--expt-relaxed-constexpr",
+                        "-Xptxas", "-v"] if os.environ.get("AD_PTXAS_VERBOSE") else
+                ARCH + ["-O3", "-lineinfo", "-std=c++17", "--use_fast_math",
+                        "--expt-relaxed-constexpr"],
+    },
+    extra_link_args=["-lcuda"],
+)
+
+setup(
+    name="autodrive-b200",
+    version="0.1.0",
+    packages=find_packages(include=["autodrive_b200*", "frc_defense*"]),
+    ext_modules=[ext],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    entry_points={"console_scripts": [
+        "frc-defense=frc_defense.tensor_training:main",
+        "frc-defense-tensor=frc_defense.tensor_training:main",
+        "frc-defense-dashboard=frc_defense.dashboard:main",
+    ]},
+)
