@@ -1,0 +1,125 @@
+"""Simulator micro-benchmarks (per-kernel device time, FUEL microbench).
+
+Examples::
+
+    python -m autodrive_b200.bench.sim_bench stages --envs 2048 --ticks 40
+    python -m autodrive_b200.bench.sim_bench fuel --envs 4096 --pieces 400 --ticks 1000
+
+``stages`` times the control / plan / tick / observe kernels of the 3v3
+environment separately with CUDA events (eager launches, after warm-up).
+``fuel`` is the FUEL-physics microbenchmark: worlds of spheres placed
+uniformly over the field with N(0, 1.5 m/s) planar velocities and six robots
+driving at up to 4.5 m/s, 10 substeps of 2 ms per tick, all ticks in one
+kernel with the state resident in shared memory.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def stages(args):
+    from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
+    dev = torch.device("cuda", 0)
+    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed, fuel_physics=not args.static)
+    if args.threads:
+        env.ws.sim.threads = args.threads
+    sim = env.ws.sim
+    for _ in range(args.warmup):
+        env.step_held(None, 20, use_graph=False)
+    torch.cuda.synchronize()
+    totals = {"control": 0., "plan": 0., "tick": 0., "observe": 0.}
+    for t in range(args.ticks):
+        for name, fn in (("control", lambda: sim.control(env._actions_buf)), ("plan", lambda: sim.plan(0)),
+                         ("tick", lambda: sim.tick(0, 1))):
+            a, b = _events()
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            totals[name] += a.elapsed_time(b)
+        if (t + 1) % 12 == 0:
+            a, b = _events()
+            a.record()
+            sim.observe()
+            b.record()
+            b.synchronize()
+            totals["observe"] += a.elapsed_time(b)
+    per_tick = {k: v / args.ticks for k, v in totals.items()}
+    total = sum(per_tick.values())
+    print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks,
+                      "ms_per_tick": per_tick, "env_ticks_per_s": args.envs / (total / 1e3),
+                      "threads": sim.threads}))
+
+
+def fuel(args):
+    from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
+    from autodrive_b200.sim.world import FuelPhysicsConfig
+    dev = torch.device("cuda", 0)
+    cfg = FuelPhysicsConfig(adaptive_substeps=False, substeps=10, broadphase="grid", contact_mode="fused",
+                            solver="jacobi", sleep=True)
+    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed, fuel_physics=cfg,
+                                fuel_count=max(args.pieces, 96))
+    if args.threads:
+        env.ws.sim.threads = args.threads
+    ws = env.ws
+    g = torch.Generator(device="cpu").manual_seed(args.seed)
+    n, P = args.envs, env.fuel_count
+    r = cfg.radius
+    active = torch.zeros((n, P), dtype=torch.uint8)
+    active[:, :args.pieces] = 1
+    x = r + torch.rand((n, P), generator=g) * (16.54 - 2 * r)
+    y = r + torch.rand((n, P), generator=g) * (8.07 - 2 * r)
+    vx = torch.randn((n, P), generator=g) * 1.5
+    vy = torch.randn((n, P), generator=g) * 1.5
+    ws["f_pos"][:, 0] = x.to(dev)
+    ws["f_pos"][:, 1] = y.to(dev)
+    ws["f_pos"][:, 2] = env._spawn_height(torch.stack((x, y), -1).to(dev))
+    ws["f_vel"].zero_()
+    ws["f_vel"][:, 0] = vx.to(dev)
+    ws["f_vel"][:, 1] = vy.to(dev)
+    ws["f_ang"].zero_()
+    ws["f_sleep"].zero_()
+    ws["f_active"].copy_(active.to(dev))
+    ws["f_owner"].fill_(-1)
+    heading = torch.rand((n, 6), generator=g) * 2 * math.pi
+    speed = torch.rand((n, 6), generator=g) * 4.5
+    cmd = torch.stack((speed * heading.cos(), speed * heading.sin(), torch.zeros_like(speed)), -1)
+    ws["c_command"].copy_(cmd.to(dev))
+    ws.sim.physics(args.warmup)
+    torch.cuda.synchronize()
+    a, b = _events()
+    a.record()
+    ws.sim.physics(args.ticks)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    print(json.dumps({"mode": "fuel", "envs": n, "pieces": args.pieces, "ticks": args.ticks,
+                      "substeps": 10, "ms_per_tick": ms / args.ticks,
+                      "env_ticks_per_s": n * args.ticks / (ms / 1e3),
+                      "finite": bool(torch.isfinite(ws["f_pos"]).all())}))
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("mode", choices=("stages", "fuel"))
+    p.add_argument("--envs", type=int, default=2048)
+    p.add_argument("--pieces", type=int, default=400)
+    p.add_argument("--ticks", type=int, default=40)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--threads", type=int, default=0)
+    p.add_argument("--static", action="store_true")
+    args = p.parse_args()
+    (stages if args.mode == "stages" else fuel)(args)
+
+
+if __name__ == "__main__":
+    main()
