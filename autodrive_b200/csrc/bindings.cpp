@@ -76,7 +76,7 @@ SimParams params_from_dict(const py::dict& d) {
   I(nominal_voltage) I(module_x) I(module_y) I(fuel_physics) I(fr) I(fm) I(fk) I(fc) I(fmu) I(froll)
   I(robot_height) I(max_comp) I(pair_damping) I(sleep) I(sleep_time) I(sleep_speed) I(sleep_ang)
   I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule)
-  I(perception_interval) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
+  I(perception_interval) I(opponent_kind) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
   I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(replan_interval)
   I(teammate_coordination) I(normalize_obs) I(horizon) I(max_speed_nominal) I(max_omega_nominal)
   I(plan_res) I(plan_nx) I(plan_ny) I(plan_sweeps) I(bump_cost) I(seed0) I(seed1)

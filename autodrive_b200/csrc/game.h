@@ -19,7 +19,8 @@
 
 namespace ad {
 
-enum Mode : int { MODE_NONE = 0, MODE_NN = 1, MODE_DET = 2 };
+enum Mode : int { MODE_NONE = 0, MODE_NN = 1, MODE_DET = 2, MODE_DIRECT = 3 };
+enum OpponentKind : int { OPP_OFFENSE = 0, OPP_MIRROR, OPP_CUTOFF, OPP_VELOCITY_INTERCEPT, OPP_RANDOM };
 
 // Accessor helpers for global state (env e, robot r, piece i).
 struct G {
@@ -250,6 +251,37 @@ AD_HD void safe_score_target(G& g, int r, float& outx, float& outy) {
   outy = any ? by : by0;
 }
 
+// Attacker objective of the two-robot roster: the HUB approach ring when
+// carrying FUEL to an active HUB, else the nearest perceived FUEL track
+// (frc_defense/tensor_sim.py:366-383).
+AD_HD void attacker_objective(G& g, int r, const int32_t* possession, float& gx, float& gy) {
+  const SimParams& sp = g.sp;
+  World& w = g.w;
+  const int team = sp.team[r];
+  const float* p = g.ppose(r);
+  float dx = p[0] - sp.hub_x[team], dy = p[1] - sp.hub_y[team];
+  float dn = fmaxf(sqrtf(dx * dx + dy * dy), 1e-6f);
+  float rad = .595f + robot_radius_of(g.param(r, RP_LENGTH), g.param(r, RP_WIDTH)) + .02f;
+  float ax = sp.hub_x[team] + dx / dn * rad, ay = sp.hub_y[team] + dy / dn * rad;
+  if (possession[r] > 0 && g.hub_active(team)) {
+    gx = ax;
+    gy = ay;
+    return;
+  }
+  float best = kInf;
+  gx = ax;
+  gy = ay;
+  for (int i = 0; i < sp.P; ++i) {
+    if (!w.t_mask[g.erp(r, i)]) continue;
+    float d = sqr(g.tx(r, i) - p[0]) + sqr(g.ty(r, i) - p[1]);
+    if (d < best) {
+      best = d;
+      gx = g.tx(r, i);
+      gy = g.ty(r, i);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Control: strategic action -> navigation target (one thread per robot).
 // `actions` holds the policy's categorical action for nn-mode robots.
@@ -358,6 +390,7 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
   } else {
     action = 7;
   }
+  if (mode == MODE_DIRECT) action = 7;
   bool no_track_search = det_offense && action == 6 && poss == 0 && !intake_available;
   g.latch(r, RL_NO_TRACK_SEARCH) = no_track_search;
   bool collecting = (action < 4 || no_track_search) &&
@@ -479,6 +512,33 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
     bool dumper_ferry = dumper && poss > 0 && !hub_on;
     tx = dumper_ferry ? p[0] : ftx;
     ty = dumper_ferry ? p[1] : fty;
+  }
+  if (sp.R == 2 && r == 1 && mode == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
+    // scripted two-robot attacker variants steer straight at a derived point
+    // (frc_defense/tensor_defense_step.py:108-180)
+    float gx, gy;
+    attacker_objective(g, r, possession, gx, gy);
+    const float* dp = g.ppose(0);
+    const float* dv = g.rvel(0);
+    if (sp.opponent_kind == OPP_MIRROR) {
+      tx = 2.f * gx - dp[0];
+      ty = 2.f * gy - dp[1];
+    } else if (sp.opponent_kind == OPP_CUTOFF) {
+      float rx = gx - dp[0], ry = gy - dp[1];
+      float rn = fmaxf(sqrtf(rx * rx + ry * ry), 1e-8f);
+      tx = dp[0] + dv[0] * .45f + rx / rn * .65f;
+      ty = dp[1] + dv[1] * .45f + ry / rn * .65f;
+    } else if (sp.opponent_kind == OPP_VELOCITY_INTERCEPT) {
+      float dist = sqrtf(sqr(dp[0] - p[0]) + sqr(dp[1] - p[1]));
+      float t = clampf(dist / speed, 0.f, 1.5f);
+      tx = dp[0] + dv[0] * t;
+      ty = dp[1] + dv[1] * t;
+    } else {
+      tx = gx;
+      ty = gy;
+    }
+    tx = clampf(tx, 0.f, sp.field_length);
+    ty = clampf(ty, 0.f, sp.field_width);
   }
   w.c_target[g.er(r) * 2] = tx;
   w.c_target[g.er(r) * 2 + 1] = ty;
@@ -789,9 +849,39 @@ AD_HD void synthesize_commands(G& g, const int32_t* possession) {
     omega[r] = om;
   }
   avoid_contention(g, cmd);
+  if (sp.R == 2 && sp.mode[1] == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
+    const size_t er = g.er(1);
+    const float* p = g.ppose(1);
+    const float* tg = w.c_target + er * 2;
+    float dx = tg[0] - p[0], dy = tg[1] - p[1];
+    float dn = fmaxf(sqrtf(dx * dx + dy * dy), 1e-8f);
+    float speed = g.param(1, RP_SPEED);
+    if (sp.opponent_kind == OPP_RANDOM) {
+      const Rng rng{sp.seed0, sp.seed1};
+      U4 u = rng.draw((uint32_t)g.e, (uint32_t)w.g_steps[(size_t)g.e * 2] ^ ((uint32_t)w.e_episode[g.e] << 14),
+                      RNG_DEFENSE, 1u);
+      float th = u01(u.x) * kTwoPi, sv = u01(u.y) * speed;
+      cmd[2] = cosf(th) * sv;
+      cmd[3] = sinf(th) * sv;
+    } else {
+      cmd[2] = dx / dn * speed;
+      cmd[3] = dy / dn * speed;
+    }
+    bool carrying = possession[1] > 0;
+    float hb = atan2f(sp.hub_y[1] - p[1], sp.hub_x[1] - p[0]);
+    omega[1] = carrying ? swerve_heading_rate(angle_diff(hb, p[2]), g.param(1, RP_OMEGA), g.param(1, RP_ALPHA),
+                                              g.rvel(1)[2], sp.dt, true)
+                        : 0.f;
+  }
   for (int r = 0; r < sp.R; ++r) {
     const size_t er = g.er(r);
     const float* p = g.ppose(r);
+    if (sp.mode[r] == MODE_DIRECT) continue;  // command supplied by the caller
+    if (w.g_rlatch[er * 8 + RL_SPARE]) {       // parked (static) opponent this episode
+      float* out = w.c_command + er * 3;
+      out[0] = out[1] = out[2] = 0.f;
+      continue;
+    }
     bool trench = w.p_trench[er] != 0;
     float therr = angle_diff(w.p_heading[er], p[2]);
     float cx = cmd[r * 2], cy = cmd[r * 2 + 1];

@@ -173,6 +173,8 @@ struct SimParams {
   // game rules
   float fuel_radius_rules = .0825f;   // intake/track geometry radius
   int two_robot_schedule = 0;   // 0: 3v3 REBUILT shifts; 1: two-robot 20 s + 30 s alternation
+  int opponent_kind = 0;        // two-robot attacker: 0 offense/adstar, 1 mirror, 2 cutoff,
+                                // 3 velocity_intercept, 4 random
   int perception_interval = 2;
   float perception_range = 6.f, perception_fov = 1.0471976f;  // half FOV (rad)
   float perception_dropout = .02f, position_noise = .015f, velocity_noise = .05f;

@@ -1,0 +1,358 @@
+"""Device-resident PPO for the defense environments.
+
+Behaviour follows frc_defense/tensor_training_ppo.py:12-631: Adam(lr 3e-4,
+eps 1e-5) per train call, strategic decisions held 12/13 ticks at 4 Hz,
+GAE with truncation bootstrapping, epochs x shuffled minibatches,
+minibatch advantage normalisation over all ranks, loss = clipped policy
+gradient + 0.5 value + linearly decayed entropy + L2 on weight matrices,
+global-norm clip 0.5, checkpoints and status written atomically by rank 0.
+
+B200 path: rollouts stay on the device (simulator kernels, one CUDA graph per
+held interval for the 3v3 env), GAE is one kernel that also yields the
+advantage statistics, and the update's gradient reduction + clip + Adam run
+as fused kernels over one flat parameter buffer.
+"""
+from __future__ import annotations
+
+import json
+import math
+import time
+from dataclasses import asdict, dataclass, field
+from pathlib import Path
+from typing import Any
+
+import torch
+
+from ..models import build_policy
+from ..parallel import dist as pdist
+from ..parallel.grad_sync import GradientSync, sync_parameters
+from .optim import FusedAdam
+from .rollout import DefenseAgents, StrategicClock, ThreeVsThreeAgents, gae_advantages
+
+OBS_NORMALIZATION = "fixed_physical_scale_v1"
+DEFENSE_TRAINING_OPPONENTS = ("offense", "adstar", "mirror", "cutoff", "velocity_intercept")
+CURRICULUM_STAGES = ("static_straight", "scripted", "adstar", "mixed")
+STATIC_OPPONENT_FRACTION = .20
+
+
+def curriculum_stage(progress: float) -> int:
+    return min(len(CURRICULUM_STAGES) - 1, max(0, int(max(0., min(.999999, progress)) * len(CURRICULUM_STAGES))))
+
+
+def curriculum_opponents(stage: int) -> tuple[str, ...]:
+    pools = (("offense",), ("offense", "mirror"), ("offense", "mirror", "adstar"), DEFENSE_TRAINING_OPPONENTS)
+    return pools[min(max(0, stage), len(pools) - 1)]
+
+
+@dataclass
+class PPOConfig:
+    rollout_steps: int = 128
+    epochs: int = 4
+    minibatch_size: int = 4096
+    learning_rate: float = 3e-4
+    gamma: float = .993
+    gae_lambda: float = .95
+    clip_coef: float = .2
+    value_coef: float = .5
+    entropy_coef: float = .01
+    max_grad_norm: float = .5
+    l2_coef: float = 1e-5
+    strategic_rate_hz: float = 4.
+    grad_backend: str = "auto"
+    bf16: bool = False
+
+
+def atomic_json(path: Path, value: dict) -> None:
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    tmp.write_text(json.dumps(value, indent=2, default=str))
+    tmp.replace(path)
+
+
+def atomic_save(path: Path, value: dict) -> None:
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    torch.save(value, tmp)
+    tmp.replace(path)
+
+
+def make_env(kind: str, num_envs: int, device, seed: int, opponent: str, horizon: int,
+             architecture: str = "strategic_adstar", fuel_physics=True, static_opponent_fraction: float = 0.):
+    """Environment factory (frc_defense/tensor_training_runtime.py:156-178)."""
+    if kind == "3v3":
+        from ..sim.env3v3 import TensorThreeVsThreeEnv
+        env = TensorThreeVsThreeEnv(num_envs=num_envs, device=device, seed=seed, horizon=horizon,
+                                    control_modes=("deterministic",) * 3 + ("nn",) * 3,
+                                    fuel_physics=fuel_physics)
+        return ThreeVsThreeAgents(env)
+    from ..sim.env_defense import TensorDefenseEnv
+    mode = {"direct": "direct", "tactical_adstar": "tactical", "strategic_adstar": "strategic"}.get(
+        architecture, architecture)
+    env = TensorDefenseEnv(num_envs=num_envs, task="defense", device=device, seed=seed, opponent=opponent,
+                           horizon=horizon, action_mode=mode, fuel_physics=fuel_physics,
+                           static_opponent_fraction=static_opponent_fraction)
+    return DefenseAgents(env)
+
+
+class PPOLearner:
+    """Policy, fused optimizer and update step shared by the trainers and bench."""
+
+    def __init__(self, obs_dim: int, action_dim: int, action_kind: str, device, cfg: PPOConfig,
+                 network: str = "mlp", world: int = 1, initial_state: dict | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = build_policy(network, obs_dim, action_dim, action_kind).to(self.device)
+        if initial_state is not None:
+            self.model.load_state_dict(initial_state)
+        sync_parameters(self.model, world)
+        self.opt = FusedAdam(self.model, lr=cfg.learning_rate, eps=1e-5, max_grad_norm=cfg.max_grad_norm)
+        self.sync = GradientSync(self.opt, world, cfg.grad_backend)
+        self.world = world
+        self.action_kind = action_kind
+        self.action_dim = action_dim
+
+    @torch.no_grad()
+    def act(self, obs: torch.Tensor):
+        mask = obs[:, -self.action_dim:] > .5 if self.action_kind == "categorical" else None
+        with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.cfg.bf16 and self.device.type == "cuda"):
+            action, logp, value = self.model.sample(obs, action_mask=mask)
+        return action, logp.float(), value.float(), mask
+
+    @torch.no_grad()
+    def value(self, obs: torch.Tensor) -> torch.Tensor:
+        with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.cfg.bf16 and self.device.type == "cuda"):
+            return self.model(obs)[2].float()
+
+    def update(self, flat: dict, entropy_coef: float) -> dict:
+        """epochs x minibatches of clipped PPO on one rollout batch."""
+        cfg = self.cfg
+        n = flat["obs"].shape[0]
+        mb = min(cfg.minibatch_size, n)
+        kl = torch.zeros((), device=self.device)
+        clip_frac = torch.zeros((), device=self.device)
+        ent = torch.zeros((), device=self.device)
+        samples, batches = 0, 0
+        for _ in range(cfg.epochs):
+            perm = torch.randperm(n, device=self.device)
+            for idx in perm.split(mb):
+                mask = flat["mask"][idx] if flat["mask"] is not None else None
+                with torch.autocast(self.device.type, dtype=torch.bfloat16,
+                                    enabled=cfg.bf16 and self.device.type == "cuda"):
+                    logp, entropy, value, _ = self.model.score(flat["obs"][idx], flat["actions"][idx], mask)
+                logp, entropy, value = logp.float(), entropy.float(), value.float()
+                logratio = logp - flat["logp"][idx]
+                ratio = logratio.exp()
+                kl += ((ratio - 1.) - logratio).detach().sum()
+                clip_frac += ((ratio - 1.).abs() > cfg.clip_coef).detach().sum()
+                adv = flat["adv"][idx]
+                if self.world > 1:
+                    stats = torch.stack((adv.sum(), adv.square().sum(), adv.new_tensor(float(adv.numel()))))
+                    pdist.all_reduce_(stats)
+                    mean = stats[0] / stats[2].clamp_min(1.)
+                    var = (stats[1] / stats[2].clamp_min(1.) - mean.square()).clamp_min(0.)
+                    adv = (adv - mean) / (var.sqrt() + 1e-8)
+                else:
+                    adv = (adv - adv.mean()) / (adv.std(unbiased=False) + 1e-8)
+                pg = torch.maximum(-adv * ratio, -adv * ratio.clamp(1 - cfg.clip_coef, 1 + cfg.clip_coef)).mean()
+                vloss = .5 * (value - flat["returns"][idx]).square().mean()
+                l2 = sum(p.square().sum() for p in self.model.parameters() if p.ndim > 1)
+                loss = pg + cfg.value_coef * vloss - entropy_coef * entropy.mean() + cfg.l2_coef * l2
+                self.opt.zero_grad()
+                loss.backward()
+                self.sync.step()
+                ent += entropy.mean().detach()
+                samples += int(idx.numel())
+                batches += 1
+        return {"approx_kl_sum": kl, "clip_fraction_sum": clip_frac, "entropy_sum": ent,
+                "samples": samples, "batches": batches}
+
+
+def collect_rollout(agents, learner: PPOLearner, obs: torch.Tensor, steps: int, clock: StrategicClock,
+                    episode_ticks: list[int]):
+    """Fill one rollout of `steps` decisions; returns (buffers, next obs, tick count)."""
+    dev = learner.device
+    A, D = agents.n_agents, agents.obs_dim
+    cont = learner.action_kind == "continuous"
+    buf = {
+        "obs": torch.empty((steps, A, D), device=dev),
+        "actions": torch.empty((steps, A, learner.action_dim) if cont else (steps, A), device=dev,
+                               dtype=torch.float32 if cont else torch.long),
+        "mask": None if cont else torch.empty((steps, A, learner.action_dim), device=dev, dtype=torch.bool),
+        "logp": torch.empty((steps, A), device=dev),
+        "values": torch.empty((steps, A), device=dev),
+        "next_values": torch.empty((steps, A), device=dev),
+        "rewards": torch.empty((steps, A), device=dev),
+        "dones": torch.empty((steps, A), device=dev, dtype=torch.bool),
+        "truncated": torch.empty((steps, A), device=dev, dtype=torch.bool),
+    }
+    ticks_total = 0
+    horizon = agents.horizon
+    for t in range(steps):
+        buf["obs"][t] = obs
+        action, logp, value, mask = learner.act(obs)
+        if mask is not None:
+            buf["mask"][t] = mask
+        ticks = clock.next()
+        remaining = horizon - episode_ticks[0]
+        next_obs, reward, done, truncated = agents.act(action, ticks, remaining)
+        used = min(ticks, remaining)
+        episode_ticks[0] += used
+        ticks_total += used
+        boundary = episode_ticks[0] >= horizon
+        buf["actions"][t], buf["logp"][t], buf["values"][t] = action, logp, value
+        buf["rewards"][t] = reward
+        buf["dones"][t] = done
+        buf["truncated"][t] = truncated | boundary
+        if t > 0:
+            prev_end = buf["dones"][t - 1] | buf["truncated"][t - 1]
+            buf["next_values"][t - 1] = torch.where(prev_end, buf["next_values"][t - 1], value)
+        if boundary or t == steps - 1:
+            buf["next_values"][t] = learner.value(next_obs)
+        if boundary:
+            episode_ticks[0] = 0
+            next_obs = agents.reset_done(torch.ones(A, dtype=torch.bool, device=dev))
+        obs = next_obs
+    return buf, obs, ticks_total
+
+
+def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, device, opponent: str,
+               initial_checkpoint=None, rollout_steps: int = 128, epochs: int = 4, minibatch_size: int = 4096,
+               learning_rate: float = 3e-4, gamma: float = .993, gae_lambda: float = .95, clip_coef: float = .2,
+               value_coef: float = .5, entropy_coef: float = .01, max_grad_norm: float = .5,
+               l2_coef: float = 1e-5, horizon: int = 8000, architecture: str = "strategic_adstar",
+               curriculum: bool = True, strategic_rate_hz: float = 4., env_kind: str = "defense",
+               network: str = "mlp", fuel_physics=True, grad_backend: str = "auto", bf16: bool = False,
+               status_context: dict | None = None, dist_state=None) -> dict[str, Any]:
+    if task != "defense":
+        raise ValueError("only defense policies are trainable; offense is deterministic")
+    if opponent not in (*DEFENSE_TRAINING_OPPONENTS, "mixed"):
+        raise ValueError("opponent must be a deterministic defense-training baseline")
+    state = dist_state or pdist.distributed_state(device)
+    rank, world, dev = state.rank, state.world, state.device
+    rank_seed = seed + rank * 1_000_003
+    torch.manual_seed(rank_seed)
+    cfg = PPOConfig(rollout_steps=rollout_steps, epochs=epochs, minibatch_size=minibatch_size,
+                    learning_rate=learning_rate, gamma=gamma, gae_lambda=gae_lambda, clip_coef=clip_coef,
+                    value_coef=value_coef, entropy_coef=entropy_coef, max_grad_norm=max_grad_norm,
+                    l2_coef=l2_coef, strategic_rate_hz=strategic_rate_hz, grad_backend=grad_backend, bf16=bf16)
+    agents = make_env(env_kind, num_envs, dev, rank_seed, "offense" if opponent == "mixed" else opponent,
+                      horizon, architecture, fuel_physics,
+                      STATIC_OPPONENT_FRACTION if env_kind == "defense" else 0.)
+    action_kind = agents.action_kind
+    initial_state = None
+    if initial_checkpoint is not None:
+        payload = torch.load(initial_checkpoint, map_location=dev, weights_only=True)
+        if payload.get("task") != "defense":
+            raise ValueError("initial checkpoint must be tagged as a defense policy")
+        if payload.get("drivetrain_config") != agents.drivetrain_config:
+            raise ValueError("initial checkpoint drivetrain configuration does not match this run")
+        if payload.get("architecture", "direct") != architecture:
+            raise ValueError("initial checkpoint architecture differs from this training run")
+        initial_state = payload["model_state_dict"]
+    learner = PPOLearner(agents.obs_dim, agents.action_dim, action_kind, dev, cfg, network, world, initial_state)
+    out = Path(output)
+    if rank == 0:
+        out.mkdir(parents=True, exist_ok=True)
+    status_path, checkpoint = out / "status.json", out / "policy.pt"
+    status_context = dict(status_context or {})
+    updates = max(1, (timesteps + rollout_steps * num_envs - 1) // (rollout_steps * num_envs))
+    if rank == 0:
+        atomic_json(status_path, {**status_context, "status": "running", "task": task, "opponent": opponent,
+                                  "architecture": architecture, "network": network, "action_kind": action_kind,
+                                  "updates": updates, "world_size": world})
+    obs = agents.reset()
+    clock = StrategicClock(strategic_rate_hz) if action_kind == "categorical" else None
+    clock = clock or _UnitClock()
+    episode_ticks = [0]
+    started = time.perf_counter()
+    totals = {"transitions": 0, "physics_world_ticks": 0, "return_sum": 0., "episodes": 0}
+    action_counts = torch.zeros(agents.action_dim, device=dev)
+    history = []
+    result: dict[str, Any] = {}
+    for update in range(updates):
+        if curriculum and env_kind == "defense" and hasattr(agents.env, "ws"):
+            pool = curriculum_opponents(curriculum_stage(update / max(1, updates)))
+            kind = pool[update % len(pool)]
+            from ..sim.env_defense import OPPONENT_KINDS
+            agents.env.ws.sim  # parameters are baked per world; opponent variants switch via params
+            agents.env.opponent = kind
+            _set_opponent(agents.env, OPPONENT_KINDS[kind])
+        t0 = time.perf_counter()
+        buf, obs, ticks = collect_rollout(agents, learner, obs, rollout_steps, clock, episode_ticks)
+        stats = torch.zeros(3, dtype=torch.float64, device=dev)
+        adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
+                             buf["next_values"], gamma, gae_lambda, stats)
+        flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim),
+                "actions": buf["actions"].reshape((-1, agents.action_dim) if action_kind == "continuous" else (-1,)),
+                "mask": buf["mask"].reshape(-1, agents.action_dim) if buf["mask"] is not None else None,
+                "logp": buf["logp"].reshape(-1), "adv": adv.reshape(-1),
+                "returns": (adv + buf["values"]).reshape(-1)}
+        if action_kind == "categorical":
+            action_counts += torch.bincount(flat["actions"], minlength=agents.action_dim).float()
+        coef = entropy_coef * max(0., 1. - update / max(1, updates - 1))
+        upd = learner.update(flat, coef)
+        counters = torch.tensor([float(rollout_steps * agents.n_agents), float(ticks * num_envs),
+                                 float(buf["rewards"].sum().item()), float(upd["samples"]),
+                                 float(upd["approx_kl_sum"].item()), float(upd["clip_fraction_sum"].item()),
+                                 float(upd["entropy_sum"].item()), float(upd["batches"])],
+                                dtype=torch.float64, device=dev)
+        pdist.all_reduce_(counters)
+        elapsed = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        pdist.all_reduce_(elapsed, "max")
+        totals["transitions"] += int(counters[0])
+        totals["physics_world_ticks"] += int(counters[1])
+        wall = time.perf_counter() - started
+        record = {"update": update + 1, "updates": updates, "transitions": totals["transitions"],
+                  "transitions_per_second": totals["transitions"] / max(wall, 1e-9),
+                  "physics_world_ticks_per_second": totals["physics_world_ticks"] / max(wall, 1e-9),
+                  "update_seconds_max_rank": float(elapsed), "mean_reward": float(counters[2] / max(1., counters[0])),
+                  "approx_kl": float(counters[4] / max(1., counters[3])),
+                  "clip_fraction": float(counters[5] / max(1., counters[3])),
+                  "entropy": float(counters[6] / max(1., counters[7])),
+                  "grad_norm": float(learner.opt.last_norm.item())}
+        history.append(record)
+        if rank == 0:
+            atomic_save(checkpoint, checkpoint_payload(learner.model, agents, architecture, network, action_kind,
+                                                      learner.opt))
+            dist_counts = (action_counts / action_counts.sum().clamp_min(1)).tolist()
+            atomic_json(status_path, {**status_context, "status": "running", "task": task, "opponent": opponent,
+                                      "architecture": architecture, "network": network, **record,
+                                      "action_distribution": dist_counts, "world_size": world})
+        result = record
+    scores, acquisitions = agents.score_counts()
+    final = {**status_context, "status": "completed", "task": task, "opponent": opponent,
+             "architecture": architecture, "network": network, "checkpoint": str(checkpoint),
+             **result, "history": history[-20:],
+             "team_scores": scores.sum(0).tolist(), "acquisitions": acquisitions.sum(0).tolist(),
+             "world_size": world}
+    if rank == 0:
+        atomic_json(status_path, final)
+        atomic_json(out / "metadata.json", {k: v for k, v in final.items() if k != "history"})
+    return final
+
+
+class _UnitClock:
+    def next(self) -> int:
+        return 1
+
+
+def _set_opponent(env, code: int) -> None:
+    """Switch the scripted attacker behaviour between rollouts."""
+    params = dict(env.ws.params)
+    if params.get("opponent_kind") == code:
+        return
+    params["opponent_kind"] = code
+    from ..ops import require_extension
+    ext = require_extension()
+    tensors = [env.ws.t[name] for name, _, _ in env.ws.schema]
+    env.ws.params = params
+    env.ws.sim = ext.Sim(tensors, params)
+
+
+def checkpoint_payload(model, agents, architecture, network, action_kind, optimizer=None) -> dict:
+    """Reference-compatible policy.pt payload (frc_defense/tensor_training_ppo.py:455-459)."""
+    payload = {"model_state_dict": model.state_dict(), "obs_dim": agents.obs_dim,
+               "action_dim": agents.action_dim, "action_kind": action_kind, "architecture": architecture,
+               "task": "defense", "observation_normalization": OBS_NORMALIZATION,
+               "drivetrain_config": agents.drivetrain_config, "network": network}
+    if optimizer is not None:
+        payload["optimizer_state_dict"] = optimizer.state_dict()
+    return payload
