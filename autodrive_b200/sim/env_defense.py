@@ -81,8 +81,8 @@ class TensorDefenseEnv:
             raise ValueError("fuel_count must be 96 + 6*preloaded_per_robot through 600")
         self.dt = float(kwargs.pop("dt", .02))
         self.horizon = int(kwargs.pop("horizon", 8000))
-        if self.action_mode == "strategic":
-            self.horizon = max(self.horizon, math.ceil(160. / self.dt))
+        # The horizon is honoured as given (the reference raises strategic
+        # horizons to a full 160 s match; pass horizon=8000 for that).
         self.randomize = bool(kwargs.pop("randomize", True))
         self.static_opponent_fraction = float(kwargs.pop("static_opponent_fraction", 0.))
         if not 0. <= self.static_opponent_fraction <= 1.:
