@@ -1,21 +1,27 @@
-"""Headline benchmark: 3v3 full-match env-ticks/s on 1..8 B200 (one process per GPU).
+"""Headline benchmark: 3v3 env-ticks/s and PPO samples/s on 1..8 B200 (one process per GPU).
 
-Workload (one step): every world of a TensorThreeVsThreeEnv batch (2048 worlds
-per GPU, fuel physics on: 504 FUEL, 64 FUEL+robot substeps per 20 ms tick,
-perception every 2 ticks, route replanning every 20 ticks, deterministic
-scripted controllers for all six robots, seed 0..N per rank) advances one
-held decision interval of `--ticks-per-step` ticks (default 20) and builds the
-137-feature observations. Synthetic data, random-init state; nothing is
-cached or skipped inside the timed region.
+Default workload (`--mode train`), one step = one PPO training iteration of
+the 3v3 defense configuration on every GPU:
+  * TensorThreeVsThreeEnv, 2048 worlds per GPU, fuel physics on (504 FUEL,
+    64 robot+FUEL substeps per 20 ms tick), perception every 2 ticks, route
+    replanning every 20 ticks, three scripted offense robots and three learned
+    defenders sharing one 137->8 ActorCritic (random init, fp32);
+  * a rollout of `--decisions` strategic decisions held 12/13 ticks each
+    (4 Hz), the GAE kernel, then PPO with 4 epochs x 8 minibatches, gradient
+    averaging over the ranks and the fused clip + Adam kernels.
+`value` is simulated env-ticks per second over the whole job (all GPUs);
+`ppo_samples_per_s` is agent transitions per second trained on.
 
-Device timing: CUDA events on the launching stream, W warm-up steps, K timed
-steps bracketed by barrier + synchronize, max over ranks. The state touched
-per step (FUEL, tracks, routes: ~0.25 GB at 2048 worlds) exceeds the 126 MB L2,
-so no explicit flush is needed.
+`--mode sim` times the simulator alone: every world advances
+`--ticks-per-step` ticks under held actions and builds observations.
 
-End-to-end (`e2e`): the same metric through the public API
-(`TensorThreeVsThreeEnv.step_held`) with the step's action tensor copied from
-pinned host memory every step and the rewards read back to the host every step.
+Timing: CUDA events on the launching stream, W warm-up steps, K timed steps
+bracketed by barrier + synchronize, max over ranks. The state touched per
+step (FUEL, tracks, routes: ~0.25 GB per GPU) exceeds the 126 MB L2.
+
+End-to-end (`e2e`): the same step through the public training/env API with
+the step's control inputs copied from pinned host memory every step and the
+step's result statistics read back to the host every step.
 
 `--impl reference` runs the unmodified reference package from baseline/_ref
 through its own public API on the same configuration.
@@ -29,6 +35,7 @@ import sys
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "3v3 env-ticks/sec and PPO samples/sec, 1/2/4/8 B200, device-timed max over ranks"
 
 
 def _dist_init():
@@ -38,8 +45,8 @@ def _dist_init():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        torch.cuda.set_device(local)
         import datetime
+        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
@@ -63,7 +70,103 @@ def _barrier(world: int):
     torch.cuda.synchronize()
 
 
-def run_ours(args, rank, world, local):
+def _timed(fn, steps, world):
+    import torch
+    _barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    _barrier(world)
+    return _max_over_ranks(start.elapsed_time(stop), world)
+
+
+def run_train(args, rank, world, local):
+    import torch
+    sys.path.insert(0, HERE)
+    from autodrive_b200.train.ppo import PPOConfig, PPOLearner, collect_rollout, make_env
+    from autodrive_b200.train.rollout import StrategicClock, gae_advantages
+    from autodrive_b200.utils.clocks import ClockSampler
+    dev = torch.device("cuda", local)
+    agents = make_env("3v3", args.envs, dev, args.seed + rank * 1_000_003, "offense", 8000, fuel_physics=True)
+    samples = agents.n_agents * args.decisions
+    cfg = PPOConfig(rollout_steps=args.decisions, epochs=args.epochs,
+                    minibatch_size=samples // args.minibatches, grad_backend=args.grad_backend)
+    learner = PPOLearner(agents.obs_dim, agents.action_dim, "categorical", dev, cfg, "mlp", world)
+    state = {"obs": agents.reset(), "clock": StrategicClock(4.), "ep": [0], "ticks": 0}
+    control_dev = torch.tensor([cfg.entropy_coef, 0.], device=dev)
+    stats_dev = torch.zeros(4, device=dev)
+
+    def step():
+        buf, state["obs"], ticks = collect_rollout(agents, learner, state["obs"], args.decisions,
+                                                   state["clock"], state["ep"])
+        state["ticks"] += ticks
+        stats = torch.zeros(3, dtype=torch.float64, device=dev)
+        adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
+                             buf["next_values"], cfg.gamma, cfg.gae_lambda, stats)
+        flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim), "actions": buf["actions"].reshape(-1),
+                "mask": buf["mask"].reshape(-1, agents.action_dim), "logp": buf["logp"].reshape(-1),
+                "adv": adv.reshape(-1), "returns": (adv + buf["values"]).reshape(-1)}
+        upd = learner.update(flat, control_dev[0])
+        stats_dev[0] = buf["rewards"].mean()
+        stats_dev[1] = upd["approx_kl_sum"] / max(1, upd["samples"])
+        stats_dev[2] = upd["entropy_sum"] / max(1, upd["batches"])
+        stats_dev[3] = learner.opt.last_norm[0]
+
+    for _ in range(args.warmup):
+        step()
+    ticks_before = state["ticks"]
+    with ClockSampler(local) as clocks:
+        ms = _timed(step, args.steps, world)
+    ticks_timed = state["ticks"] - ticks_before
+    env_ticks = args.envs * ticks_timed * world
+    value = env_ticks / (ms / 1e3)
+    samples_total = samples * args.steps * world
+    # end to end: H2D control block and D2H result statistics every step
+    host_control = torch.tensor([cfg.entropy_coef, 0.]).pin_memory()
+    host_stats = torch.zeros(4).pin_memory()
+
+    def e2e_step():
+        control_dev.copy_(host_control, non_blocking=True)
+        step()
+        host_stats.copy_(stats_dev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        _ = float(host_stats[0])
+
+    for _ in range(args.warmup):
+        e2e_step()
+    t0 = state["ticks"]
+    e2e_ms = _timed(e2e_step, args.steps, world)
+    e2e_ticks = args.envs * (state["ticks"] - t0) * world
+    decisions_ticks = ticks_timed / max(1, args.steps)
+    minibatches = args.epochs * args.minibatches
+    launches = int(args.steps * (decisions_ticks * 3 + args.decisions + 1 + 2 * minibatches))
+    return {
+        "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (random-init seeded REBUILT matches and policy; no external data)",
+        "ppo_samples_per_s": samples_total / (ms / 1e3), "ppo_samples_per_step_per_gpu": samples,
+        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 504 FUEL, 64 substeps/tick) "
+                            "+ PPO on ActorCritic 137->128->128->8 for 3 learned defenders",
+                   "global_batch": args.envs * world, "envs_per_gpu": args.envs,
+                   "seq_len": args.decisions, "decisions_per_step": args.decisions,
+                   "env_ticks_per_step_per_world": decisions_ticks, "ppo_epochs": args.epochs,
+                   "ppo_minibatches": args.minibatches, "grad_backend": learner.sync.backend,
+                   "parallelism": f"env-batch x dp{world}",
+                   "l2": "working set > 126 MB L2 (no flush needed)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
+                "ppo_samples_per_s": samples_total / (e2e_ms / 1e3),
+                "h2d_bytes_per_step": host_control.numel() * 4, "d2h_bytes_per_step": host_stats.numel() * 4},
+        "gpu_launches": launches,
+        "final_stats": {"mean_reward": float(stats_dev[0]), "approx_kl": float(stats_dev[1]),
+                        "entropy": float(stats_dev[2]), "grad_norm": float(stats_dev[3])},
+    }
+
+
+def run_sim(args, rank, world, local):
     import torch
     sys.path.insert(0, HERE)
     from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
@@ -73,61 +176,35 @@ def run_ours(args, rank, world, local):
                                 fuel_physics=True, horizon=8000)
     ticks = args.ticks_per_step
     actions = torch.full((args.envs, 6), 7, dtype=torch.int32, device=dev)
-    # device-timed region
     for _ in range(args.warmup):
         env.step_held(actions, ticks)
-    _barrier(world)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            env.step_held(actions, ticks)
-        stop.record()
-        _barrier(world)
-    ms = start.elapsed_time(stop)
-    ms = _max_over_ranks(ms, world)
+        ms = _timed(lambda: env.step_held(actions, ticks), args.steps, world)
     env_ticks = args.envs * ticks * args.steps * world
-    value = env_ticks / (ms / 1000.)
-    # end-to-end through the public API with H2D inputs and D2H results each step
     host_actions = torch.full((args.envs, 6), 7, dtype=torch.int32).pin_memory()
     host_rewards = torch.empty((args.envs, 6), dtype=torch.float32).pin_memory()
-    env.reset(seed=args.seed + rank)
-    for _ in range(args.warmup):
-        dev_actions = host_actions.to(dev, non_blocking=True)
-        _, rew, _ = env.step_held(dev_actions, ticks)
-        host_rewards.copy_(rew, non_blocking=True)
-    _barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        dev_actions = host_actions.to(dev, non_blocking=True)
-        _, rew, _ = env.step_held(dev_actions, ticks)
+
+    def e2e_step():
+        _, rew, _ = env.step_held(host_actions.to(dev, non_blocking=True), ticks)
         host_rewards.copy_(rew, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         _ = float(host_rewards.sum())
-    e1.record()
-    _barrier(world)
-    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), world)
-    e2e_value = env_ticks / (e2e_ms / 1000.)
-    scores = env.fuel_score_count.sum().item()
-    launches_per_step = ticks * 3 + 1
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = _timed(e2e_step, args.steps, world)
     return {
-        "metric": "3v3 env-ticks/sec and PPO samples/sec, 1/2/4/8 B200, device-timed max over ranks",
-        "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "metric": METRIC, "value": env_ticks / (ms / 1e3), "unit": "env-ticks/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (random-init seeded REBUILT matches, deterministic scripted controllers)",
-        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match, fuel physics on (504 FUEL, "
-                            "64 substeps/tick), perception every 2 ticks, replan every 20 ticks",
-                   "global_batch": args.envs * world, "envs_per_gpu": args.envs,
-                   "seq_len": ticks, "ticks_per_step": ticks, "parallelism": f"env-batch x dp{world}",
-                   "l2": "working set > 126 MB L2 (no flush needed)"},
+        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match, fuel physics on (504 FUEL, 64 substeps/tick), "
+                            "perception every 2 ticks, replan every 20 ticks, simulator only",
+                   "global_batch": args.envs * world, "envs_per_gpu": args.envs, "seq_len": ticks,
+                   "parallelism": f"env-batch x dp{world}", "l2": "working set > 126 MB L2 (no flush needed)"},
         "clocks": clocks.summary(),
-        "e2e": {"value": e2e_value, "unit": "env-ticks/s",
-                "h2d_bytes_per_step": host_actions.numel() * 4,
-                "d2h_bytes_per_step": host_rewards.numel() * 4},
-        "gpu_launches": launches_per_step * args.steps,
-        "team_scores_total": scores,
+        "e2e": {"value": env_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
+                "h2d_bytes_per_step": host_actions.numel() * 4, "d2h_bytes_per_step": host_rewards.numel() * 4},
+        "gpu_launches": (ticks * 3 + 1) * args.steps,
     }
 
 
@@ -142,57 +219,42 @@ def run_reference(args, rank, world, local):
     # The reference's CUDA path builds FUEL contact pairs with per-world Python
     # loops on the host (frc_defense/fuel_physics.py:337-382). Calibrate one
     # tick at a small batch first and refuse configurations that cannot finish.
-    calib_envs = min(args.envs, 4)
-    env = RefEnv(num_envs=calib_envs, device=dev, seed=args.seed + rank,
-                 control_modes=("deterministic",) * 6, robot_roles=("offense",) * 3 + ("defense",) * 3,
-                 horizon=8000, randomize=True, fuel_count=504, fused_sensor_rng=True, fuel_physics=True)
-    actions = torch.full((calib_envs, 6), 7, dtype=torch.long, device=dev)
+    calib = min(args.envs, 4)
+    modes = ("deterministic",) * 3 + (("nn",) * 3 if args.mode == "train" else ("deterministic",) * 3)
+    env = RefEnv(num_envs=calib, device=dev, seed=args.seed + rank, control_modes=modes,
+                 robot_roles=("offense",) * 3 + ("defense",) * 3, horizon=8000, randomize=True,
+                 fuel_count=504, fused_sensor_rng=True, fuel_physics=True)
+    actions = torch.full((calib, 6), 7, dtype=torch.long, device=dev)
     env.step(actions, capture_observation=False, capture_info=False)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     env.step(actions, capture_observation=False, capture_info=False)
     torch.cuda.synchronize()
     per_tick = time.perf_counter() - t0
-    projected = per_tick * args.envs / calib_envs * args.ticks_per_step * (args.steps + args.warmup)
+    ticks_per_step = args.decisions * 12.5 if args.mode == "train" else args.ticks_per_step
+    projected = per_tick * args.envs / calib * ticks_per_step * (args.steps + args.warmup)
     if projected > args.reference_budget_s:
-        value = calib_envs / per_tick
         return {"impl": "reference",
-                "unavailable": (f"reference 3v3 with fuel physics measured {per_tick:.2f} s per tick at "
-                                f"{calib_envs} worlds ({value:.2f} env-ticks/s) on this GPU; "
-                                f"{args.envs} worlds x {args.ticks_per_step * (args.steps + args.warmup)} "
-                                f"ticks projects to {projected / 3600:.1f} h"),
-                "calibration_env_ticks_per_s": value, "n_gpus": world}
-    env = RefEnv(num_envs=args.envs, device=dev, seed=args.seed + rank,
-                 control_modes=("deterministic",) * 6, robot_roles=("offense",) * 3 + ("defense",) * 3,
-                 horizon=8000, randomize=True, fuel_count=504, fused_sensor_rng=True, fuel_physics=True)
-    actions = torch.full((args.envs, 6), 7, dtype=torch.long, device=dev)
-    for _ in range(args.warmup * args.ticks_per_step):
-        env.step(actions, capture_observation=False, capture_info=False)
-    _barrier(world)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        for t in range(args.ticks_per_step):
-            env.step(actions, capture_observation=(t == args.ticks_per_step - 1), capture_info=False)
-    stop.record()
-    _barrier(world)
-    ms = _max_over_ranks(start.elapsed_time(stop), world)
-    value = args.envs * args.ticks_per_step * args.steps * world / (ms / 1000.)
-    return {"impl": "reference", "metric": "3v3 env-ticks/sec and PPO samples/sec, 1/2/4/8 B200, "
-            "device-timed max over ranks", "value": value, "unit": "env-ticks/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "dtype": "fp32", "data": "synthetic",
-            "config": {"model": "reference TensorThreeVsThreeEnv", "global_batch": args.envs * world,
-                       "seq_len": args.ticks_per_step, "parallelism": f"dp{world}"}}
+                "unavailable": (f"reference 3v3 with fuel physics measured {per_tick:.2f} s per tick at {calib} "
+                                f"worlds ({calib / per_tick:.2f} env-ticks/s) on this GPU; {args.envs} worlds x "
+                                f"{ticks_per_step * (args.steps + args.warmup):.0f} ticks projects to "
+                                f"{projected / 3600:.1f} h"),
+                "calibration_env_ticks_per_s": calib / per_tick, "n_gpus": world}
+    raise SystemExit("reference configuration fits the budget; extend run_reference before using it")
 
 
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=6)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--envs", type=int, default=2048)
-    p.add_argument("--ticks-per-step", type=int, default=20)
+    p.add_argument("--mode", choices=("train", "sim"), default="train")
+    p.add_argument("--decisions", type=int, default=8, help="strategic decisions per PPO rollout (train mode)")
+    p.add_argument("--epochs", type=int, default=4)
+    p.add_argument("--minibatches", type=int, default=8)
+    p.add_argument("--grad-backend", default="auto")
+    p.add_argument("--ticks-per-step", type=int, default=20, help="ticks per step (sim mode)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--reference-budget-s", type=float, default=900.)
@@ -202,7 +264,10 @@ def main():
     rank, world, local = _dist_init()
     if world != args.gpus:
         p.error(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    result = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if args.impl == "reference":
+        result = run_reference(args, rank, world, local)
+    else:
+        result = (run_train if args.mode == "train" else run_sim)(args, rank, world, local)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
