@@ -63,6 +63,8 @@ struct TickShared {
   int16_t slot[kMaxPieces];
   int16_t sorted[kMaxPieces];
   int32_t cell_start[kMaxGridCells + 1];
+  uint32_t awake_bits[kMaxGridCells / 32 + 1];  // grid cells holding an awake sphere
+  float rtrig[kMaxRobots * 4];                  // per robot: cos, sin, contact reach^2, unused
   float red[kRedSlots * 20];
   float red_out[20];
   float scal[8];
@@ -787,6 +789,16 @@ AD_HD int atomic_inc_cell(TickShared& s, int cell) {
 #endif
 }
 
+AD_HD void mark_awake_cell(TickShared& s, int cell) {
+#if defined(__CUDA_ARCH__)
+  atomicOr(&s.awake_bits[cell >> 5], 1u << (cell & 31));
+#else
+  s.awake_bits[cell >> 5] |= 1u << (cell & 31);
+#endif
+}
+
+AD_HD bool cell_awake(const TickShared& s, int cell) { return (s.awake_bits[cell >> 5] >> (cell & 31)) & 1u; }
+
 AD_HD void static_contact_fuel(TickShared& s, const SimParams& sp, int i, V3 n, float depth, bool valid,
                                float h) {
   if (!(valid && depth > 0.f && !s.sleep[i])) return;
@@ -836,12 +848,22 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   // uniform XY grid (counting sort)
   const int ncell = sp.grid_nx * sp.grid_ny;
   PAR_FOR(c, ncell + 1) { s.cell_start[c] = 0; }
+  PAR_FOR(c, ncell / 32 + 1) { s.awake_bits[c] = 0u; }
+  // per-robot heading trig and contact reach for the chassis contacts below
+  PAR_FOR(r, sp.R) {
+    const float th = s.pose[r * 3 + 2];
+    s.rtrig[r * 4 + 0] = cosf(th);
+    s.rtrig[r * 4 + 1] = sinf(th);
+    const float reach = .5f * sqrtf(sqr(rparam(s, r, RP_LENGTH)) + sqr(rparam(s, r, RP_WIDTH))) + sp.fr;
+    s.rtrig[r * 4 + 2] = reach * reach;
+  }
   BARRIER();
   PAR_FOR(i, P) {
     if (s.freem[i]) {
       int c = fuel_cell_of(sp, s.fpos[0][i], s.fpos[1][i]);
       s.cell[i] = (int16_t)c;
       s.slot[i] = (int16_t)atomic_inc_cell(s, c);
+      if (!s.sleep[i]) mark_awake_cell(s, c);
     }
   }
   BARRIER();
@@ -864,7 +886,14 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
       const bool sleep_i = s.sleep[i];
       const V3 vi = V3{s.fvel[0][i], s.fvel[1][i], s.fvel[2][i]};
       const V3 wi = V3{s.fang[0][i], s.fang[1][i], s.fang[2][i]};
-      for (int oy = -1; oy <= 1; ++oy) {
+      // a sleeping sphere only receives impulses from awake neighbours
+      bool scan = !sleep_i;
+      for (int oy = -1; oy <= 1 && !scan; ++oy)
+        for (int ox = -1; ox <= 1 && !scan; ++ox) {
+          int yy = cy + oy, xx = cx + ox;
+          if (yy >= 0 && yy < sp.grid_ny && xx >= 0 && xx < sp.grid_nx) scan = cell_awake(s, yy * sp.grid_nx + xx);
+        }
+      for (int oy = -1; oy <= 1 && scan; ++oy) {
         int yy = cy + oy;
         if (yy < 0 || yy >= sp.grid_ny) continue;
         for (int ox = -1; ox <= 1; ++ox) {
@@ -934,8 +963,9 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
       for (int r = 0; r < sp.R; ++r) {
         const float* rp = s.pose + r * 3;
         const float* rv = s.vel + r * 3;
-        float co = cosf(rp[2]), si = sinf(rp[2]);
         float dx = s.fpos[0][i] - rp[0], dy = s.fpos[1][i] - rp[1];
+        if (dx * dx + dy * dy > s.rtrig[r * 4 + 2]) continue;
+        const float co = s.rtrig[r * 4 + 0], si = s.rtrig[r * 4 + 1];
         float lx = co * dx + si * dy, ly = -si * dx + co * dy;
         float hl = .5f * rparam(s, r, RP_LENGTH), hw = .5f * rparam(s, r, RP_WIDTH);
         float n2x, n2y, dist;
@@ -985,7 +1015,9 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   SERIAL_END
   // terrain, floor, walls, field boxes, sleep
   PAR_FOR(i, P) {
-    if (s.freem[i]) {
+    // a sleeping sphere has zero velocity and takes no static impulse; it
+    // stays asleep (its sleep clock is irrelevant once asleep)
+    if (s.freem[i] && !s.sleep[i]) {
       float height, grade;
       bool on = bump_height(sp, s.fpos[0][i], s.fpos[1][i], height, grade);
       V3 n = V3{0.f, 0.f, 1.f};
@@ -1002,8 +1034,9 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
       static_contact_fuel(s, sp, i, V3{0.f, 1.f, 0.f}, sp.fr - s.fpos[1][i], true, h);
       static_contact_fuel(s, sp, i, V3{0.f, -1.f, 0.f}, s.fpos[1][i] + sp.fr - sp.field_width, true, h);
       const bool low = s.fpos[2][i] < sp.robot_height + sp.fr;
-      for (int b = 0; b < sp.num_boxes; ++b) {
+      for (int b = 0; b < sp.num_boxes && low; ++b) {
         const Box& bx = sp.boxes[b];
+        if (fabsf(s.fpos[0][i] - bx.cx) >= bx.hx + sp.fr || fabsf(s.fpos[1][i] - bx.cy) >= bx.hy + sp.fr) continue;
         float nx, ny, dist;
         box_normal2(s.fpos[0][i] - bx.cx, s.fpos[1][i] - bx.cy, bx.hx, bx.hy, nx, ny, dist);
         static_contact_fuel(s, sp, i, V3{nx, ny, 0.f}, sp.fr - dist, low, h);

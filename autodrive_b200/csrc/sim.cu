@@ -259,7 +259,7 @@ __global__ void observe_kernel(World w, SimParams sp) {
   observe_env(w, sp, e, poss);
 }
 
-__global__ void __launch_bounds__(512) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
+__global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
   extern __shared__ __align__(16) uint8_t smem[];
   TickShared& s = *reinterpret_cast<TickShared*>(smem);
   __shared__ int32_t poss[kMaxRobots];
@@ -301,7 +301,7 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
 
 // Fuel-only microbenchmark kernel: `ticks` ticks of robot + FUEL substeps
 // with the state resident in shared memory between ticks.
-__global__ void __launch_bounds__(512) physics_kernel(World w, SimParams sp, int ticks) {
+__global__ void __launch_bounds__(256, 3) physics_kernel(World w, SimParams sp, int ticks) {
   extern __shared__ __align__(16) uint8_t smem[];
   TickShared& s = *reinterpret_cast<TickShared*>(smem);
   const int e = blockIdx.x;
