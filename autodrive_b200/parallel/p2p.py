@@ -1,0 +1,74 @@
+"""Fused peer-memory all-reduce + clip + Adam for data-parallel training.
+
+Every rank re-homes its flat gradient and parameter buffers into one
+IPC-exported device region (`csrc/comm_ops.cu`); IPC handles are exchanged
+over the gloo control group. One cooperative kernel per optimizer step then
+reduce-scatters gradients with NVLink peer loads, all-reduces the shard norms
+for the global clip, applies Adam to the owned shard and all-gathers the new
+parameters with peer stores. Waits on peers are bounded: a rank that stops
+participating makes the others raise `PeerCommError` instead of hanging.
+
+Optimizer moments are kept for the owned shard only (ZeRO-1 layout), so an
+optimizer state saved from one rank covers that rank's shard.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import require_extension
+from . import dist as pdist
+
+
+class PeerCommError(RuntimeError):
+    pass
+
+
+class FusedAllReduceAdam:
+    def __init__(self, optimizer, max_wait_iters: int = 1 << 24, check_every: int = 1):
+        self.ext = require_extension()
+        self.opt = optimizer
+        grouped = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size() if grouped else 1
+        self.rank = dist.get_rank() if grouped else 0
+        flat = optimizer.flat
+        if flat.flat.device.type != "cuda":
+            raise RuntimeError("the peer-memory all-reduce needs CUDA ranks")
+        n = flat.flat.numel()
+        self.comm = self.ext.peer_comm_create(n, self.world, self.rank)
+        handle = self.ext.peer_comm_ipc_handle(self.comm)
+        handles = [handle]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle, group=pdist.control_group())
+        self.ext.peer_comm_open(self.comm, handles)
+        grad, param = self.ext.peer_comm_buffers(self.comm)
+        param.copy_(flat.flat)
+        grad.zero_()
+        flat.rehome(param, grad)
+        padded = self.comm.n_padded
+        self.m = torch.zeros(padded, device=param.device)
+        self.v = torch.zeros(padded, device=param.device)
+        self.max_wait_iters = int(max_wait_iters)
+        self.check_every = max(1, int(check_every))
+        self.steps = 0
+        torch.cuda.synchronize(param.device)
+        pdist.barrier()
+
+    def step(self) -> torch.Tensor:
+        opt = self.opt
+        opt.flat.sync_grads()
+        opt.step_count += 1
+        self.ext.peer_comm_step(self.comm, self.m, self.v, opt.last_norm, opt.step_count, opt.lr,
+                                opt.betas[0], opt.betas[1], opt.eps, opt.weight_decay, opt.max_grad_norm,
+                                self.max_wait_iters)
+        self.steps += 1
+        if self.steps % self.check_every == 0:
+            self.check()
+        return opt.last_norm
+
+    def check(self) -> None:
+        code = int(self.comm.status.item())
+        if code:
+            phase = {1: "gradients-ready", 2: "norm exchange", 4: "completion"}.get(code, str(code))
+            raise PeerCommError(f"peer all-reduce wait expired in the {phase} barrier on rank {self.rank}")

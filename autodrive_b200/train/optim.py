@@ -35,6 +35,16 @@ class FlatParameters:
             self.slices.append((offset, n))
             offset += n
 
+    def rehome(self, flat: torch.Tensor, grad: torch.Tensor) -> None:
+        """Move parameters and gradients into caller-provided flat buffers
+        (already holding the parameter values), e.g. peer-visible memory."""
+        if flat.numel() != self.flat.numel() or grad.numel() != self.grad.numel():
+            raise ValueError("rehome buffers must match the flat parameter count")
+        self.flat, self.grad = flat, grad
+        for p, (o, n) in zip(self.params, self.slices):
+            p.data = self.flat[o:o + n].view_as(p)
+            p.grad = self.grad[o:o + n].view_as(p)
+
     def zero_grad(self) -> None:
         self.grad.zero_()
         # autograd may have replaced a .grad with a fresh tensor; re-bind views
