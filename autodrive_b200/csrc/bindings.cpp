@@ -178,6 +178,7 @@ struct Sim {
 
 void register_policy_ops(py::module& m);
 void register_comm_ops(py::module& m);
+void register_policy_tc_ops(py::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200-native FRC REBUILT simulator kernels";
@@ -197,4 +198,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("cuda", [](const Sim& s) { return s.cuda; });
   register_policy_ops(m);
   register_comm_ops(m);
+  register_policy_tc_ops(m);
 }

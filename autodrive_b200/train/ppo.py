@@ -24,6 +24,7 @@ from typing import Any
 import torch
 
 from ..models import build_policy
+from ..ops import policy_tc
 from ..parallel import dist as pdist
 from ..parallel.grad_sync import GradientSync, sync_parameters
 from .optim import FusedAdam
@@ -60,6 +61,8 @@ class PPOConfig:
     strategic_rate_hz: float = 4.
     grad_backend: str = "auto"
     bf16: bool = False
+    # tcgen05 kernels for the 2 x 128 categorical policy on CUDA (act + update)
+    fused_policy: bool = True
 
 
 def atomic_json(path: Path, value: dict) -> None:
@@ -108,9 +111,25 @@ class PPOLearner:
         self.world = world
         self.action_kind = action_kind
         self.action_dim = action_dim
+        self.tc = None
+        if (cfg.fused_policy and self.device.type == "cuda" and not cfg.bf16
+                and policy_tc.supported(self.model)):
+            self.tc = policy_tc.TensorCorePolicy(self.model, self.opt.flat)
+        self.weights_version = 0
+        self._loss_stats = torch.zeros(5, device=self.device)
+
+    def weights_changed(self) -> None:
+        """Call after writing parameters outside the optimizer (checkpoint loads)."""
+        self.weights_version += 1
+
+    def _tc_ready(self):
+        self.tc.ensure_packed(self.weights_version)
+        return self.tc
 
     @torch.no_grad()
     def act(self, obs: torch.Tensor):
+        if self.tc is not None:
+            return self._tc_ready().act(obs)
         mask = obs[:, -self.action_dim:] > .5 if self.action_kind == "categorical" else None
         with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.cfg.bf16 and self.device.type == "cuda"):
             action, logp, value = self.model.sample(obs, action_mask=mask)
@@ -118,11 +137,15 @@ class PPOLearner:
 
     @torch.no_grad()
     def value(self, obs: torch.Tensor) -> torch.Tensor:
+        if self.tc is not None:
+            return self._tc_ready().act(obs, value_only=True)
         with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.cfg.bf16 and self.device.type == "cuda"):
             return self.model(obs)[2].float()
 
     def update(self, flat: dict, entropy_coef: float) -> dict:
         """epochs x minibatches of clipped PPO on one rollout batch."""
+        if self.tc is not None:
+            return self._update_tc(flat, entropy_coef)
         cfg = self.cfg
         n = flat["obs"].shape[0]
         mb = min(cfg.minibatch_size, n)
@@ -163,6 +186,40 @@ class PPOLearner:
                 batches += 1
         return {"approx_kl_sum": kl, "clip_fraction_sum": clip_frac, "entropy_sum": ent,
                 "samples": samples, "batches": batches}
+
+
+    def _update_tc(self, flat: dict, entropy_coef) -> dict:
+        """The update on the tensor-core kernels: per minibatch one fused
+        forward+backward, the partial-gradient reduction and the fused
+        clip + Adam; no autograd graph and no host synchronisation."""
+        cfg, tc = self.cfg, self._tc_ready()
+        tc.check()
+        n = flat["obs"].shape[0]
+        mb = min(cfg.minibatch_size, n)
+        batch = {"obs": flat["obs"].contiguous().float(), "actions": flat["actions"].reshape(-1).long().contiguous(),
+                 "mask": None if flat.get("mask") is None else flat["mask"].contiguous(),
+                 "logp": flat["logp"].contiguous().float(), "adv": flat["adv"].contiguous().float(),
+                 "returns": flat["returns"].contiguous().float()}
+        if torch.is_tensor(entropy_coef):
+            ent = entropy_coef.reshape(1).to(self.device, torch.float32)
+        else:
+            ent = torch.full((1,), float(entropy_coef), device=self.device)
+        stats = self._loss_stats
+        stats.zero_()
+        reduce = pdist.all_reduce_ if self.world > 1 else None
+        samples, batches = 0, 0
+        for _ in range(cfg.epochs):
+            perm = torch.randperm(n, device=self.device)
+            for idx in perm.split(mb):
+                tc.train_minibatch(batch, idx, ent, cfg.clip_coef, cfg.value_coef, cfg.l2_coef, stats, reduce)
+                self.sync.step()
+                self.weights_version += 1
+                tc.pack(self.weights_version)
+                samples += int(idx.numel())
+                batches += 1
+        tc._post_status()
+        return {"approx_kl_sum": stats[0], "clip_fraction_sum": stats[1], "entropy_sum": stats[2],
+                "policy_loss_sum": stats[3], "value_loss_sum": stats[4], "samples": samples, "batches": batches}
 
 
 def collect_rollout(agents, learner: PPOLearner, obs: torch.Tensor, steps: int, clock: StrategicClock,

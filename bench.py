@@ -98,17 +98,31 @@ def run_train(args, rank, world, local):
     control_dev = torch.tensor([cfg.entropy_coef, 0.], device=dev)
     stats_dev = torch.zeros(4, device=dev)
 
+    phases = {"on": False, "events": []}
+
+    def mark():
+        if phases["on"]:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            phases["events"][-1].append(ev)
+
     def step():
+        if phases["on"]:
+            phases["events"].append([])
+        mark()
         buf, state["obs"], ticks = collect_rollout(agents, learner, state["obs"], args.decisions,
                                                    state["clock"], state["ep"])
         state["ticks"] += ticks
+        mark()
         stats = torch.zeros(3, dtype=torch.float64, device=dev)
         adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
                              buf["next_values"], cfg.gamma, cfg.gae_lambda, stats)
         flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim), "actions": buf["actions"].reshape(-1),
                 "mask": buf["mask"].reshape(-1, agents.action_dim), "logp": buf["logp"].reshape(-1),
                 "adv": adv.reshape(-1), "returns": (adv + buf["values"]).reshape(-1)}
+        mark()
         upd = learner.update(flat, control_dev[0])
+        mark()
         stats_dev[0] = buf["rewards"].mean()
         stats_dev[1] = upd["approx_kl_sum"] / max(1, upd["samples"])
         stats_dev[2] = upd["entropy_sum"] / max(1, upd["batches"])
@@ -117,8 +131,17 @@ def run_train(args, rank, world, local):
     for _ in range(args.warmup):
         step()
     ticks_before = state["ticks"]
+    phases["on"] = True
     with ClockSampler(local) as clocks:
         ms = _timed(step, args.steps, world)
+    phases["on"] = False
+    torch.cuda.synchronize()
+    breakdown = {"rollout": 0., "gae": 0., "update": 0.}
+    for ev in phases["events"]:
+        breakdown["rollout"] += ev[0].elapsed_time(ev[1])
+        breakdown["gae"] += ev[1].elapsed_time(ev[2])
+        breakdown["update"] += ev[2].elapsed_time(ev[3])
+    breakdown = {k: round(v / max(1, len(phases["events"])), 3) for k, v in breakdown.items()}
     ticks_timed = state["ticks"] - ticks_before
     env_ticks = args.envs * ticks_timed * world
     value = env_ticks / (ms / 1e3)
@@ -141,7 +164,12 @@ def run_train(args, rank, world, local):
     e2e_ticks = args.envs * (state["ticks"] - t0) * world
     decisions_ticks = ticks_timed / max(1, args.steps)
     minibatches = args.epochs * args.minibatches
-    launches = int(args.steps * (decisions_ticks * 3 + args.decisions + 1 + 2 * minibatches))
+    # own kernels per step: control+plan+tick per tick, observe + policy act per decision, the
+    # bootstrap value, GAE, and per minibatch either (adv stats, fused fwd+bwd, partial reduce,
+    # sum-of-squares, Adam, weight pack) on the tensor-core path or (sum-of-squares, Adam)
+    per_mb = 6 if learner.tc is not None else 2
+    per_decision = 2 if learner.tc is not None else 1
+    launches = int(args.steps * (decisions_ticks * 3 + per_decision * args.decisions + 2 + per_mb * minibatches))
     return {
         "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -161,6 +189,8 @@ def run_train(args, rank, world, local):
                 "ppo_samples_per_s": samples_total / (e2e_ms / 1e3),
                 "h2d_bytes_per_step": host_control.numel() * 4, "d2h_bytes_per_step": host_stats.numel() * 4},
         "gpu_launches": launches,
+        "breakdown_ms_per_step": breakdown,
+        "policy_kernels": "tcgen05" if learner.tc is not None else "torch",
         "final_stats": {"mean_reward": float(stats_dev[0]), "approx_kl": float(stats_dev[1]),
                         "entropy": float(stats_dev[2]), "grad_norm": float(stats_dev[3])},
     }
