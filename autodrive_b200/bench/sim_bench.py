@@ -32,11 +32,25 @@ def stages(args):
     if args.threads:
         env.ws.sim.threads = args.threads
     sim = env.ws.sim
+    nn_slots = [i for i, m in enumerate(env.control_modes) if m == "nn"]
+    gen = torch.Generator(device=dev).manual_seed(args.seed)
+
+    def random_actions():
+        # uniformly random valid strategic action for every neural slot (an untrained policy)
+        full = torch.full((env.n, 6), 7, dtype=torch.int32, device=dev)
+        if nn_slots:
+            mask = env.ws["obs"][:, nn_slots, -8:] > .5
+            score = torch.rand(mask.shape, device=dev, generator=gen).masked_fill(~mask, -1.)
+            full[:, nn_slots] = score.argmax(-1).to(torch.int32)
+        return full
+
     for _ in range(args.warmup):
-        env.step_held(None, 20, use_graph=False)
+        env.step_held(random_actions() if args.actions == "random" else None, 20, use_graph=False)
     torch.cuda.synchronize()
     totals = {"control": 0., "plan": 0., "tick": 0., "observe": 0.}
     for t in range(args.ticks):
+        if args.actions == "random" and t % 12 == 0:
+            env._set_actions(random_actions())
         for name, fn in (("control", lambda: sim.control(env._actions_buf)), ("plan", lambda: sim.plan(0)),
                          ("tick", lambda: sim.tick(0, 1))):
             a, b = _events()
@@ -54,7 +68,27 @@ def stages(args):
             totals["observe"] += a.elapsed_time(b)
     per_tick = {k: v / args.ticks for k, v in totals.items()}
     total = sum(per_tick.values())
-    print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks,
+    phases = None
+    if args.phases:
+        from autodrive_b200.ops import require_extension
+        ext = require_extension()
+        ext.phase_profile_read()
+        ext.phase_profile_enable(True)
+        for _ in range(args.ticks):
+            sim.control(env._actions_buf)
+            sim.plan(0)
+            sim.tick(0, 1)
+        torch.cuda.synchronize()
+        ext.phase_profile_enable(False)
+        cyc = ext.phase_profile_read()
+        names = ("robot_swerve", "robot_sweep", "robot_contacts", "robot_tail", "fuel_integrate_clear",
+                 "fuel_grid", "fuel_pairs", "fuel_apply", "fuel_chassis", "fuel_static", "pre_substeps",
+                 "post_substeps")
+        total = max(1, sum(cyc))
+        phases = {n: round(c / total, 4) for n, c in zip(names, cyc)}
+    awake = (env.ws["f_active"].bool() & (env.ws["f_sleep"] == 0)).float().sum(-1).mean().item()
+    print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,
+                      "awake_fuel_per_world": awake, "phase_share": phases,
                       "ms_per_tick": per_tick, "env_ticks_per_s": args.envs / (total / 1e3),
                       "threads": sim.threads}))
 
@@ -117,6 +151,9 @@ def main():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--threads", type=int, default=0)
     p.add_argument("--static", action="store_true")
+    p.add_argument("--phases", action="store_true", help="stages: also report the tick kernel's per-phase cycle shares")
+    p.add_argument("--actions", choices=("held", "random"), default="held",
+                   help="stages: default held actions, or random valid strategic actions every 12 ticks")
     args = p.parse_args()
     (stages if args.mode == "stages" else fuel)(args)
 

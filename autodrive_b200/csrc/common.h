@@ -27,6 +27,17 @@
 #define BARRIER() __syncthreads()
 #define SERIAL_BEGIN if (threadIdx.x == 0) {
 #define SERIAL_END }
+// Opt-in per-phase cycle accounting of the tick kernel: thread 0 adds the
+// clock64() time since the previous mark to bucket k (marks sit right after
+// CTA barriers, so a bucket is that phase's share of the CTA's critical path).
+#define PHASE_MARK(s, k)                                        \
+  do {                                                          \
+    if ((s).prof_on && threadIdx.x == 0) {                      \
+      const unsigned long long t_ = clock64();                  \
+      (s).prof[(k)] += t_ - (s).prof_last;                      \
+      (s).prof_last = t_;                                       \
+    }                                                           \
+  } while (0)
 #else
 #define AD_TID 0
 #define AD_NT 1
@@ -34,6 +45,7 @@
 #define BARRIER() ((void)0)
 #define SERIAL_BEGIN {
 #define SERIAL_END }
+#define PHASE_MARK(s, k) ((void)0)
 #endif
 
 namespace ad {

@@ -68,6 +68,10 @@ struct TickShared {
   float red[kRedSlots * 20];
   float red_out[20];
   float scal[8];
+  // phase accounting (PHASE_MARK), thread 0 only
+  unsigned long long prof_last;
+  unsigned long long prof[12];
+  int32_t prof_on;
 };
 
 // ----------------------------------------------------------------------------
@@ -635,6 +639,7 @@ AD_HD void record_pair_events(TickShared& s, const SimParams& sp, World& w, int 
 AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, float h) {
   PAR_FOR(r, sp.R) { swerve_robot(s, sp, r, h); }
   BARRIER();
+  PHASE_MARK(s, 0);
   SERIAL_BEGIN
   s.eflag[0] = 0;
   s.eflag[1] = 0;
@@ -650,6 +655,7 @@ AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, 
     }
   }
   BARRIER();
+  PHASE_MARK(s, 1);
   for (int it = 0; it < sp.contact_iterations; ++it) {
     PAR_FOR(q, sp.Q) { robot_pair_compute(s, sp, q); }
     BARRIER();
@@ -671,6 +677,7 @@ AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, 
     }
     BARRIER();
   }
+  PHASE_MARK(s, 2);
   PAR_FOR(r, sp.R) {
     s.safety[r * 4 + 0] += 1;
     s.safety[r * 4 + 1] += s.rflag[r * 4 + RF_ROBOT_CONTACT] ? 1 : 0;
@@ -682,6 +689,7 @@ AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, 
   s.phys_time += (double)h;
   SERIAL_END
   BARRIER();
+  PHASE_MARK(s, 3);
 }
 
 // ----------------------------------------------------------------------------
@@ -858,6 +866,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
     s.rtrig[r * 4 + 2] = reach * reach;
   }
   BARRIER();
+  PHASE_MARK(s, 4);
   PAR_FOR(i, P) {
     if (s.freem[i]) {
       int c = fuel_cell_of(sp, s.fpos[0][i], s.fpos[1][i]);
@@ -873,6 +882,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
     if (s.freem[i]) s.sorted[s.cell_start[(int)s.cell[i]] + (int)s.slot[i]] = (int16_t)i;
   }
   BARRIER();
+  PHASE_MARK(s, 5);
   // Jacobi pair contacts, each sphere computing the impulses that act on it
   float local_max[2] = {0.f, 0.f};
   const float I = .4f * sp.fm * sp.fr * sp.fr;
@@ -941,6 +951,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   }
   BARRIER();
   cta_max<2>(s, local_max);
+  PHASE_MARK(s, 6);
   // crowded piles share one Jacobi response scale per world
   const float scale = local_max[1] > 4.f ? fminf(.08f / fmaxf(local_max[0], .08f), 1.f) : 1.f;
   PAR_FOR(i, P) {
@@ -955,6 +966,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
     }
   }
   BARRIER();
+  PHASE_MARK(s, 7);
   // chassis contacts with reciprocal robot impulses
   float racc[18];
   for (int k = 0; k < 18; ++k) racc[k] = 0.f;
@@ -1006,6 +1018,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   }
   BARRIER();
   cta_sum<18>(s, racc);
+  PHASE_MARK(s, 8);
   SERIAL_BEGIN
   for (int r = 0; r < sp.R; ++r) {
     s.vel[r * 3 + 0] += racc[r * 3 + 0];
@@ -1063,6 +1076,7 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
     }
   }
   BARRIER();
+  PHASE_MARK(s, 9);
 }
 
 // Analytic terrain contact height for a ground-spawned sphere

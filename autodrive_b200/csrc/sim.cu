@@ -158,6 +158,7 @@ AD_HD void tick_env(World& w, const SimParams& sp, TickShared& s, int e, uint32_
     parked[k] = s.pose[k];
   }
   const float h = sp.dt / (float)sp.substeps;
+  PHASE_MARK(s, 10);
   for (int sub = 0; sub < sp.substeps; ++sub) {
     robot_substep(s, sp, w, e, h);
     if (sp.fuel_physics) fuel_substep(s, sp, h);
@@ -230,6 +231,7 @@ AD_HD void tick_env(World& w, const SimParams& sp, TickShared& s, int e, uint32_
   SERIAL_END
   store_fuel(s, w, sp, e);
   BARRIER();
+  PHASE_MARK(s, 11);
 }
 
 // Sensor update without physics (episode reset): fresh detections only.
@@ -259,13 +261,23 @@ __global__ void observe_kernel(World w, SimParams sp) {
   observe_env(w, sp, e, poss);
 }
 
+__device__ int g_prof_on = 0;
+__device__ unsigned long long g_prof[12];
+
 __global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
   extern __shared__ __align__(16) uint8_t smem[];
   TickShared& s = *reinterpret_cast<TickShared*>(smem);
   __shared__ int32_t poss[kMaxRobots];
   const int e = blockIdx.x;
   if (e >= sp.n || !w.active[e]) return;
+  if (threadIdx.x == 0) {
+    s.prof_on = g_prof_on;
+    for (int k = 0; k < 12; ++k) s.prof[k] = 0ull;
+    s.prof_last = clock64();
+  }
   tick_env(w, sp, s, e, tick, poss, run_game);
+  if (threadIdx.x == 0 && s.prof_on)
+    for (int k = 0; k < 12; ++k) atomicAdd(&g_prof[k], s.prof[k]);
 }
 
 __global__ void __launch_bounds__(512) perceive_kernel(World w, SimParams sp) {
@@ -328,6 +340,19 @@ static void check(cudaError_t err, const char* what) {
 }
 
 size_t tick_smem_bytes() { return sizeof(TickShared); }
+
+void phase_profile_enable(bool on) {
+  const int v = on ? 1 : 0;
+  check(cudaMemcpyToSymbol(g_prof_on, &v, sizeof(int)), "phase profile flag");
+}
+
+std::vector<unsigned long long> phase_profile_read() {
+  std::vector<unsigned long long> out(12, 0ull);
+  check(cudaMemcpyFromSymbol(out.data(), g_prof, sizeof(unsigned long long) * 12), "phase profile read");
+  std::vector<unsigned long long> zero(12, 0ull);
+  check(cudaMemcpyToSymbol(g_prof, zero.data(), sizeof(unsigned long long) * 12), "phase profile reset");
+  return out;
+}
 
 size_t plan_smem_bytes(const SimParams& sp) {
   const int nc = sp.plan_nx * sp.plan_ny;

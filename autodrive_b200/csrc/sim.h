@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <vector>
 
 #include "planner.h"
 #include "rules.h"
@@ -9,6 +10,8 @@
 namespace ad {
 
 size_t tick_smem_bytes();
+void phase_profile_enable(bool on);
+std::vector<unsigned long long> phase_profile_read();
 size_t plan_smem_bytes(const SimParams& sp);
 void validate_params(const SimParams& sp);
 
