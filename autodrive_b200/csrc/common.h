@@ -30,14 +30,17 @@
 // Opt-in per-phase cycle accounting of the tick kernel: thread 0 adds the
 // clock64() time since the previous mark to bucket k (marks sit right after
 // CTA barriers, so a bucket is that phase's share of the CTA's critical path).
-#define PHASE_MARK(s, k)                                        \
-  do {                                                          \
-    if ((s).prof_on && threadIdx.x == 0) {                      \
-      const unsigned long long t_ = clock64();                  \
-      (s).prof[(k)] += t_ - (s).prof_last;                      \
-      (s).prof_last = t_;                                       \
-    }                                                           \
+// `leader` is the thread that keeps the timeline (0: robot warp / whole CTA,
+// 32: FUEL warps while the two groups run concurrently).
+#define PHASE_MARK_BY(s, k, leader)                                 \
+  do {                                                              \
+    if ((s).prof_on && (int)threadIdx.x == (leader)) {              \
+      const unsigned long long t_ = clock64();                      \
+      (s).prof[(k)] += t_ - (s).prof_last[(leader) ? 1 : 0];        \
+      (s).prof_last[(leader) ? 1 : 0] = t_;                         \
+    }                                                               \
   } while (0)
+#define PHASE_MARK(s, k) PHASE_MARK_BY(s, k, 0)
 #else
 #define AD_TID 0
 #define AD_NT 1
@@ -45,8 +48,51 @@
 #define BARRIER() ((void)0)
 #define SERIAL_BEGIN {
 #define SERIAL_END }
+#define PHASE_MARK_BY(s, k, leader) ((void)0)
 #define PHASE_MARK(s, k) ((void)0)
 #endif
+
+// A set of threads of the CTA that runs one phase sequence on its own:
+// `rank` is this thread's index in the group, `size` the group's thread count,
+// `first` its first thread; `bar` selects the group barrier (0: the whole CTA,
+// -1: a single warp, >0: named barrier id). On the host every group is the one
+// serial caller (rank 0, size 1) and group barriers are no-ops.
+struct Group {
+  int rank, size, first, bar;
+};
+
+AD_HD Group group_all() {
+#if defined(__CUDA_ARCH__)
+  return Group{(int)threadIdx.x, (int)blockDim.x, 0, 0};
+#else
+  return Group{0, 1, 0, 0};
+#endif
+}
+
+AD_HD void group_sync(const Group& g) {
+#if defined(__CUDA_ARCH__)
+  if (g.bar == 0) __syncthreads();
+  else if (g.bar < 0) __syncwarp();
+  else asm volatile("bar.sync %0, %1;" :: "r"(g.bar), "r"(g.size) : "memory");
+#else
+  (void)g;
+#endif
+}
+
+#define GFOR(i, n, g) for (int i = (g).rank; i < (int)(n); i += (g).size)
+
+// Group-wide OR of a flag (also a group barrier). Only whole-CTA and
+// single-warp groups reduce; the host caller already holds the total.
+AD_HD bool group_any(const Group& g, bool v) {
+#if defined(__CUDA_ARCH__)
+  if (g.bar == 0) return __syncthreads_or(v) != 0;
+  __syncwarp();
+  return __any_sync(0xffffffffu, v) != 0;
+#else
+  (void)g;
+  return v;
+#endif
+}
 
 namespace ad {
 

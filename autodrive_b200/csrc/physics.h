@@ -62,15 +62,19 @@ struct TickShared {
   int16_t cell[kMaxPieces];
   int16_t slot[kMaxPieces];
   int16_t sorted[kMaxPieces];
-  int32_t cell_start[kMaxGridCells + 1];
-  uint32_t awake_bits[kMaxGridCells / 32 + 1];  // grid cells holding an awake sphere
+  int16_t work[kMaxPieces];                     // spheres that need pair contacts this substep
+  uint8_t listed[kMaxPieces];                   // sphere is on `work`
+  int32_t nwork;
+  uint32_t cmask;                               // robots with a chassis-FUEL contact this substep
+  alignas(16) int32_t cell_start[kMaxGridCells + 4];
+  alignas(16) uint32_t awake_bits[kMaxGridCells / 32 + 4];  // grid cells holding an awake sphere
   float rtrig[kMaxRobots * 4];                  // per robot: cos, sin, contact reach^2, unused
   float red[kRedSlots * 20];
   float red_out[20];
   float scal[8];
-  // phase accounting (PHASE_MARK), thread 0 only
-  unsigned long long prof_last;
-  unsigned long long prof[12];
+  // phase accounting (PHASE_MARK): [0] thread 0's timeline, [1] the FUEL warps' leader
+  unsigned long long prof_last[2];
+  unsigned long long prof[14];
   int32_t prof_on;
 };
 
@@ -102,6 +106,66 @@ AD_HD void cta_sum(TickShared& s, float (&v)[M]) {
 #else
   (void)s;
   (void)v;
+#endif
+}
+
+// Max over a thread group (warp-aligned); the group barrier replaces __syncthreads.
+template <int M>
+AD_HD void group_max(TickShared& s, float (&v)[M], const Group& g) {
+#if defined(__CUDA_ARCH__)
+  const int lane = threadIdx.x & 31, warp = g.rank >> 5;
+  const int warps = (g.size + 31) >> 5;
+#pragma unroll
+  for (int k = 0; k < M; ++k) {
+    float x = v[k];
+    for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+    if (lane == 0) s.red[warp * 20 + k] = x;
+  }
+  group_sync(g);
+  if (g.rank < M) {
+    float t = -kInf;
+    for (int w = 0; w < warps; ++w) t = fmaxf(t, s.red[w * 20 + g.rank]);
+    s.red_out[g.rank] = t;
+  }
+  group_sync(g);
+#pragma unroll
+  for (int k = 0; k < M; ++k) v[k] = s.red_out[k];
+  group_sync(g);
+#else
+  (void)s;
+  (void)v;
+  (void)g;
+#endif
+}
+
+// cta_sum restricted to the robots in `mask` (entries 3r..3r+2); the other
+// entries are left as they are (the caller's are zero).
+AD_HD void cta_sum_robots(TickShared& s, float (&v)[18], uint32_t mask) {
+#if defined(__CUDA_ARCH__)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int k = 0; k < 18; ++k) {
+    if (!((mask >> (k / 3)) & 1u)) continue;
+    float x = v[k];
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) s.red[warp * 20 + k] = x;
+  }
+  __syncthreads();
+  if (threadIdx.x < 18 && ((mask >> (threadIdx.x / 3)) & 1u)) {
+    float t = 0.f;
+    for (int w = 0; w < warps; ++w) t += s.red[w * 20 + threadIdx.x];
+    s.red_out[threadIdx.x] = t;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 18; ++k)
+    if ((mask >> (k / 3)) & 1u) v[k] = s.red_out[k];
+  __syncthreads();
+#else
+  (void)s;
+  (void)v;
+  (void)mask;
 #endif
 }
 
@@ -335,6 +399,171 @@ AD_HD void swerve_robot(TickShared& s, const SimParams& sp, int r, float h) {
   }
 }
 
+#if defined(__CUDA_ARCH__)
+// The four values one per module lane of a robot (lanes base..base+3) summed
+// in module order, as the serial routine adds them.
+__device__ __forceinline__ float module_sum(float v, int base) {
+  const float a = __shfl_sync(0xffffffffu, v, base);
+  const float b = __shfl_sync(0xffffffffu, v, base + 1);
+  const float c = __shfl_sync(0xffffffffu, v, base + 2);
+  const float d = __shfl_sync(0xffffffffu, v, base + 3);
+  return ((a + b) + c) + d;
+}
+
+__device__ __forceinline__ float module_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+// swerve_robot with the four modules of each robot on four lanes of one warp
+// (lane = 4 * robot + module; all 32 lanes call it, lanes past 4R only take
+// part in the shuffles). Per-module arithmetic is that of swerve_robot and
+// cross-module sums are added in module order.
+__device__ void swerve_robot_lanes(TickShared& s, const SimParams& sp, float h) {
+  const int lane = threadIdx.x & 31;
+  const bool active = lane < 4 * sp.R;
+  const int r = active ? (lane >> 2) : 0;
+  const int k = lane & 3;
+  const int base = lane & ~3;
+  float* pose = s.pose + r * 3;
+  float* vel = s.vel + r * 3;
+  float* ms = s.ms + r * 20;
+  const float L = rparam(s, r, RP_LENGTH), m = rparam(s, r, RP_MASS);
+  const float speed_limit = rparam(s, r, RP_SPEED), accel_limit = rparam(s, r, RP_ACCEL);
+  const float omega_limit = rparam(s, r, RP_OMEGA), alpha = rparam(s, r, RP_ALPHA);
+  const float ratio = rparam(s, r, RP_DRIVE_RATIO);
+  const float drive_limit = rparam(s, r, RP_DRIVE_CURRENT);
+  const float supply_limit = rparam(s, r, RP_DRIVE_SUPPLY);
+  const float robot_supply = rparam(s, r, RP_ROBOT_SUPPLY);
+  const float batt_r = rparam(s, r, RP_BATTERY_R);
+  const float lat_mu = rparam(s, r, RP_LATERAL_MU);
+  const float ground_mu = s.mu3[1];
+  const float th = pose[2];
+  const float c = cosf(th), sn = sinf(th);
+  const float mx = (k & 1) ? sp.module_x : -sp.module_x;
+  const float my = (k & 2) ? sp.module_y : -sp.module_y;
+  float wheel_h, wheel_g;
+  const bool on_bump = bump_height(sp, pose[0] + c * mx - sn * my, pose[1] + sn * mx + c * my, wheel_h, wheel_g);
+  const float h0 = __shfl_sync(0xffffffffu, wheel_h, base), h1 = __shfl_sync(0xffffffffu, wheel_h, base + 1);
+  const float h2 = __shfl_sync(0xffffffffu, wheel_h, base + 2), h3 = __shfl_sync(0xffffffffu, wheel_h, base + 3);
+  const float front = .5f * (h1 + h3);
+  const float rear = .5f * (h0 + h2);
+  const float pitch = atan2f(front - rear, L);
+  const float cg = 0.30f;
+  const float normal = fmaxf(m * kG * cosf(pitch) / 4.f -
+                             m * kG * cg * sinf(pitch) * sgnf(mx) / (2.f * fmaxf(L, 1e-6f)), 0.f);
+  const float* cmd = s.cmd + r * 3;
+  float bvx = c * cmd[0] + sn * cmd[1];
+  float bvy = -sn * cmd[0] + c * cmd[1];
+  float omega = clampf(cmd[2], -omega_limit, omega_limit);
+  float nrm = fmaxf(sqrtf(bvx * bvx + bvy * bvy), 1e-8f);
+  float scale = fminf(speed_limit / nrm, 1.f);
+  bvx *= scale;
+  bvy *= scale;
+  const float tdx = bvx - omega * my;
+  const float tdy = bvy + omega * mx;
+  float target = sqrtf(tdx * tdx + tdy * tdy);
+  const float tmax = module_max(target);
+  const float desat = fminf(speed_limit / fmaxf(tmax, 1e-8f), 1.f);
+  target *= desat;
+  float angle = atan2f(tdy, tdx);
+  float delta = wrap_angle(angle - ms[MS_ANGLE * 4 + k]);
+  if (fabsf(delta) > kPi / 2) {
+    angle += kPi;
+    target = -target;
+  }
+  angle = wrap_angle(angle);
+  delta = wrap_angle(angle - ms[MS_ANGLE * 4 + k]);
+  target *= fmaxf(cosf(delta), 0.f);
+  const float steer_target = clampf(8.f * delta, -sp.steer_rate_limit, sp.steer_rate_limit);
+  const float se = steer_target - ms[MS_STEER_RATE * 4 + k];
+  const float steer_current = fminf(2.f * fabsf(se), sp.steer_current_limit);
+  const float rate = clampf(ms[MS_STEER_RATE * 4 + k] + sgnf(se) * sp.steer_acceleration * steer_current /
+                                fmaxf(sp.steer_current_limit, 1e-6f) * h,
+                            -sp.steer_rate_limit, sp.steer_rate_limit);
+  const float new_angle = wrap_angle(ms[MS_ANGLE * 4 + k] + rate * h);
+  const float steer_sum = module_sum(steer_current, base);
+  const float res = sp.nominal_voltage / sp.stall_current;
+  const float stall = sp.free_speed_rpm * kTwoPi / 60.f;
+  const float kv = stall / (sp.nominal_voltage - res * sp.free_current);
+  const float kt = sp.stall_torque / sp.stall_current;
+  const float bus = fmaxf(sp.battery_voltage - s.current[r] * batt_r, 0.f);
+  const float motor_target = target / sp.wheel_radius * ratio;
+  const float actual = ms[MS_DRIVE_SPEED * 4 + k] / sp.wheel_radius * ratio;
+  const float duty = clampf(motor_target / stall + .8f * (motor_target - actual) / stall, -1.f, 1.f);
+  float amps = clampf((duty * bus - actual / kv) / res, -drive_limit, drive_limit);
+  float sup = fabsf(duty * amps);
+  amps *= fminf(supply_limit / fmaxf(sup, 1e-6f), 1.f);
+  float supply = fabsf(duty * amps);
+  const float supply_sum = module_sum(supply, base);
+  const float budget = fmaxf(robot_supply - steer_sum, 0.f);
+  const float cap = fminf(budget / fmaxf(supply_sum, 1e-6f), 1.f);
+  const float bvx0 = c * vel[0] + sn * vel[1];
+  const float bvy0 = -sn * vel[0] + c * vel[1];
+  const float vel2 = vel[2];
+  amps *= cap;
+  supply *= cap;
+  const float torque = kt * (amps - sp.free_current * sgnf(actual));
+  float force = torque * ratio * sp.motor_efficiency / sp.wheel_radius;
+  const float long_lim = ground_mu * normal;
+  force = fmaxf(fminf(force, long_lim), -long_lim);
+  const float ma = new_angle;
+  const float cma = cosf(ma), sma = sinf(ma);
+  const float mvx = bvx0 - vel2 * my;
+  const float mvy = bvy0 + vel2 * mx;
+  const float lat_v = -mvx * sma + mvy * cma;
+  const float lat_lim = lat_mu * normal;
+  float lat_f = fminf(fmaxf(-lat_v * m / (4.f * h), -lat_lim), lat_lim);
+  const float comb = sqrtf(sqr(force / fmaxf(long_lim, 1e-8f)) + sqr(lat_f / fmaxf(lat_lim, 1e-8f)));
+  const float fs = fmaxf(comb, 1.f);
+  force /= fs;
+  lat_f /= fs;
+  const float fx_d = force * cma, fy_d = force * sma;
+  const float fx_l = -lat_f * sma, fy_l = lat_f * cma;
+  const float fxd = module_sum(fx_d, base), fyd = module_sum(fy_d, base);
+  const float fxl = module_sum(fx_l, base), fyl = module_sum(fy_l, base);
+  const float torque_z = module_sum(mx * (fy_d + fy_l) - my * (fx_d + fx_l), base);
+  const float sup_total = module_sum(supply, base);
+  const float roll_n = module_sum(on_bump ? 0.0125f * normal : 0.f, base);
+  const float g0 = __shfl_sync(0xffffffffu, wheel_g, base), g1 = __shfl_sync(0xffffffffu, wheel_g, base + 1);
+  const float g2 = __shfl_sync(0xffffffffu, wheel_g, base + 2), g3 = __shfl_sync(0xffffffffu, wheel_g, base + 3);
+  // every lane of the robot has read what it needs from vel/current/ms above
+  __syncwarp();
+  if (active) {
+    ms[MS_STEER_RATE * 4 + k] = rate;
+    ms[MS_ANGLE * 4 + k] = new_angle;
+    ms[MS_CURRENT * 4 + k] = amps;
+    ms[MS_SUPPLY * 4 + k] = supply;
+  }
+  const float dax = fxd / m, day = fyd / m;
+  const float dscale = fminf(accel_limit / fmaxf(sqrtf(dax * dax + day * day), 1e-8f), 1.f);
+  const float ax = dax * dscale + fxl / m;
+  const float ay = day * dscale + fyl / m;
+  const float inertia = robot_inertia(s, r);
+  const float az = torque_z / inertia;
+  float vx = vel[0] + (c * ax - sn * ay) * h;
+  float vy = vel[1] + (sn * ax + c * ay) * h;
+  const float mean_grade = .25f * (g0 + g1 + g2 + g3);
+  const float rolling_accel = roll_n / m;
+  vx = vx + (-kG * mean_grade - rolling_accel * sgnf(vx)) * h;
+  const float vn = fmaxf(sqrtf(vx * vx + vy * vy), 1e-8f);
+  const float vs = fminf(speed_limit / vn, 1.f);
+  vx *= vs;
+  vy *= vs;
+  const float w = clampf(vel2 + clampf(az, -alpha, alpha) * h, -omega_limit, omega_limit);
+  __syncwarp();
+  if (active && k == 0) {
+    s.current[r] = sup_total + steer_sum;
+    vel[0] = vx;
+    vel[1] = vy;
+    vel[2] = w;
+  }
+  const float bx = c * vx + sn * vy, by = -sn * vx + c * vy;
+  if (active) ms[MS_DRIVE_SPEED * 4 + k] = (bx - w * my) * cosf(ma) + (by + w * mx) * sinf(ma);
+  __syncwarp();
+}
+#endif
+
 // Rigid impulse with Coulomb friction against a fixed surface at a contact
 // point (frc_defense/tensor_physics_collision.py:195-218).
 AD_HD void static_contact_impulse(TickShared& s, int r, float px, float py, float nx, float ny,
@@ -368,7 +597,8 @@ AD_HD void static_contact_impulse(TickShared& s, int r, float px, float py, floa
 
 // Sequential x-min, x-max, y-min, y-max wall contacts
 // (frc_defense/tensor_physics_collision.py:220-248).
-AD_HD void walls_robot(TickShared& s, const SimParams& sp, int r) {
+AD_HD bool walls_robot(TickShared& s, const SimParams& sp, int r) {
+  bool moved = false;
   float* pose = s.pose + r * 3;
   const float c = cosf(pose[2]), sn = sinf(pose[2]);
   const float hl = .5f * rparam(s, r, RP_LENGTH), hw = .5f * rparam(s, r, RP_WIDTH);
@@ -391,13 +621,15 @@ AD_HD void walls_robot(TickShared& s, const SimParams& sp, int r) {
     float py = pose[1] + sgnf(twx * ux + twy * uy) * uy * hl + sgnf(twx * vx + twy * vy) * vy * hw;
     static_contact_impulse(s, r, px, py, nx, ny, s.mu3[2]);
     s.rflag[r * 4 + RF_WALL_X + axis] = 1;
+    moved = true;
   }
+  return moved;
 }
 
 // Most-penetrating oriented-robot vs axis-aligned field box contact
 // (frc_defense/tensor_physics_collision.py:289-376).
-AD_HD void field_collision_robot(TickShared& s, const SimParams& sp, int r) {
-  if (sp.num_boxes == 0) return;
+AD_HD bool field_collision_robot(TickShared& s, const SimParams& sp, int r) {
+  if (sp.num_boxes == 0) return false;
   float* pose = s.pose + r * 3;
   const float* vel = s.vel + r * 3;
   const float c = cosf(pose[2]), sn = sinf(pose[2]);
@@ -432,7 +664,7 @@ AD_HD void field_collision_robot(TickShared& s, const SimParams& sp, int r) {
       }
     }
   }
-  if (best < 0) return;
+  if (best < 0) return false;
   const Box& bx = sp.boxes[best];
   float cnx[4], cny[4];
   int axis = -1;
@@ -470,6 +702,7 @@ AD_HD void field_collision_robot(TickShared& s, const SimParams& sp, int r) {
   static_contact_impulse(s, r, px, py, nx, ny, s.mu3[2]);
   s.rflag[r * 4 + RF_FIELD_CONTACT] = 1;
   s.eflag[0] = 1;  // world robot_contact includes static contacts (reference semantics)
+  return true;
 }
 
 // Robot pair q: SAT overlap, position correction split by inverse mass, and
@@ -479,6 +712,21 @@ AD_HD void robot_pair_compute(TickShared& s, const SimParams& sp, int q) {
   const int i = sp.pair_i[q], j = sp.pair_j[q];
   const float* pi = s.pose + i * 3;
   const float* pj = s.pose + j * 3;
+  {
+    // disjoint circumscribed circles: the rectangles cannot overlap (the SAT
+    // below would find a separating axis), so skip it
+    const float ddx = pj[0] - pi[0], ddy = pj[1] - pi[1];
+    const float reach = .5f * (sqrtf(sqr(rparam(s, i, RP_LENGTH)) + sqr(rparam(s, i, RP_WIDTH))) +
+                               sqrtf(sqr(rparam(s, j, RP_LENGTH)) + sqr(rparam(s, j, RP_WIDTH))));
+    if (ddx * ddx + ddy * ddy > reach * reach * 1.0002f + 1e-6f) {
+      s.pq_valid[q] = 0;
+      for (int k = 0; k < 6; ++k) s.pq_dv[q * 6 + k] = 0.f;
+      for (int k = 0; k < 4; ++k) s.pq_move[q * 4 + k] = 0.f;
+      s.pq_jn[q] = 0.f;
+      s.pq_jt[q] = 0.f;
+      return;
+    }
+  }
   const float ci = cosf(pi[2]), si = sinf(pi[2]), cj = cosf(pj[2]), sj = sinf(pj[2]);
   const float axx[4] = {ci, -si, cj, -sj};
   const float axy[4] = {si, ci, sj, cj};
@@ -634,17 +882,30 @@ AD_HD void record_pair_events(TickShared& s, const SimParams& sp, World& w, int 
   }
 }
 
-// One robot substep: swerve, swept integration with field contacts, then
-// contact_iterations rounds of pair/wall/field resolution.
-AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, float h) {
-  PAR_FOR(r, sp.R) { swerve_robot(s, sp, r, h); }
-  BARRIER();
-  PHASE_MARK(s, 0);
+// One robot substep: swerve, swept integration with field contacts, then up
+// to contact_iterations rounds of pair/wall/field resolution. Runs on thread
+// group `g` (one warp on the GPU while the FUEL warps work concurrently). A
+// round that finds no robot pair in contact and moves no robot off a wall or
+// field element leaves the state unchanged, so the remaining rounds (which
+// would repeat it exactly) are skipped. Ends by caching each robot's heading
+// trig and contact reach for the chassis-FUEL contacts.
+AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, float h, const Group& g) {
+#if defined(__CUDA_ARCH__)
+  if (g.bar < 0 && sp.R <= 8) {
+    swerve_robot_lanes(s, sp, h);
+  } else {
+    GFOR(r, sp.R, g) { swerve_robot(s, sp, r, h); }
+  }
+#else
+  GFOR(r, sp.R, g) { swerve_robot(s, sp, r, h); }
+#endif
+  group_sync(g);
+  PHASE_MARK_BY(s, 0, g.first);
   SERIAL_BEGIN
   s.eflag[0] = 0;
   s.eflag[1] = 0;
   SERIAL_END
-  PAR_FOR(r, sp.R) {
+  GFOR(r, sp.R, g) {
     for (int k = 0; k < 4; ++k) s.rflag[r * 4 + k] = 0;
     const float hs = h / (float)sp.sweep_steps;
     for (int step = 0; step < sp.sweep_steps; ++step) {
@@ -654,42 +915,51 @@ AD_HD void robot_substep(TickShared& s, const SimParams& sp, World& w, int env, 
       field_collision_robot(s, sp, r);
     }
   }
-  BARRIER();
-  PHASE_MARK(s, 1);
+  group_sync(g);
+  PHASE_MARK_BY(s, 1, g.first);
   for (int it = 0; it < sp.contact_iterations; ++it) {
-    PAR_FOR(q, sp.Q) { robot_pair_compute(s, sp, q); }
-    BARRIER();
-    SERIAL_BEGIN
-    bool any = false, opp = false;
-    for (int q = 0; q < sp.Q; ++q)
-      if (s.pq_valid[q]) {
-        any = true;
-        if (sp.team[sp.pair_i[q]] != sp.team[sp.pair_j[q]]) opp = true;
-      }
-    if (any) s.eflag[0] = 1;
-    if (opp) s.eflag[1] = 1;
-    record_pair_events(s, sp, w, env, h);
-    SERIAL_END
-    PAR_FOR(r, sp.R) {
-      robot_pair_apply(s, sp, r);
-      walls_robot(s, sp, r);
-      field_collision_robot(s, sp, r);
+    GFOR(q, sp.Q, g) { robot_pair_compute(s, sp, q); }
+    group_sync(g);
+    bool any = false;
+    for (int q = 0; q < sp.Q; ++q) any = any || s.pq_valid[q];
+    if (any) {
+      SERIAL_BEGIN
+      bool opp = false;
+      for (int q = 0; q < sp.Q; ++q)
+        if (s.pq_valid[q] && sp.team[sp.pair_i[q]] != sp.team[sp.pair_j[q]]) opp = true;
+      s.eflag[0] = 1;
+      if (opp) s.eflag[1] = 1;
+      record_pair_events(s, sp, w, env, h);
+      SERIAL_END
     }
-    BARRIER();
+    bool moved = false;
+    GFOR(r, sp.R, g) {
+      if (any) robot_pair_apply(s, sp, r);
+      moved = walls_robot(s, sp, r) || moved;
+      moved = field_collision_robot(s, sp, r) || moved;
+    }
+    group_sync(g);
+    moved = group_any(g, moved);
+    if (!any && !moved) break;
   }
-  PHASE_MARK(s, 2);
-  PAR_FOR(r, sp.R) {
+  PHASE_MARK_BY(s, 2, g.first);
+  GFOR(r, sp.R, g) {
     s.safety[r * 4 + 0] += 1;
     s.safety[r * 4 + 1] += s.rflag[r * 4 + RF_ROBOT_CONTACT] ? 1 : 0;
     s.safety[r * 4 + 2] += s.rflag[r * 4 + RF_FIELD_CONTACT] ? 1 : 0;
     s.safety[r * 4 + 3] += (s.rflag[r * 4 + RF_WALL_X] | s.rflag[r * 4 + RF_WALL_Y]) ? 1 : 0;
+    const float th = s.pose[r * 3 + 2];
+    s.rtrig[r * 4 + 0] = cosf(th);
+    s.rtrig[r * 4 + 1] = sinf(th);
+    const float reach = .5f * sqrtf(sqr(rparam(s, r, RP_LENGTH)) + sqr(rparam(s, r, RP_WIDTH))) + sp.fr;
+    s.rtrig[r * 4 + 2] = reach * reach;
   }
   SERIAL_BEGIN
   s.substep_index += 1;
   s.phys_time += (double)h;
   SERIAL_END
-  BARRIER();
-  PHASE_MARK(s, 3);
+  group_sync(g);
+  PHASE_MARK_BY(s, 3, g.first);
 }
 
 // ----------------------------------------------------------------------------
@@ -741,17 +1011,17 @@ AD_HD int fuel_cell_of(const SimParams& sp, float x, float y) {
 }
 
 // Exclusive scan of cell_start[0..n) in place; cell_start[n] = total.
-AD_HD void cta_exclusive_scan(TickShared& s, int n) {
+// Exclusive scan of cell_start[0..n) by a thread group; cell_start[n] = total.
+AD_HD void group_exclusive_scan(TickShared& s, int n, const Group& g) {
 #if defined(__CUDA_ARCH__)
-  // Each thread scans a contiguous chunk serially, then a block scan of chunk totals.
-  const int T = blockDim.x;
+  // each thread scans a contiguous chunk serially, then a scan of chunk totals
+  const int T = g.size;
   const int chunk = (n + T - 1) / T;
-  const int b = threadIdx.x * chunk;
+  const int b = g.rank * chunk;
   const int e = min(b + chunk, n);
   int sum = 0;
   for (int k = b; k < e; ++k) sum += s.cell_start[k];
-  // warp scan of per-thread sums
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = g.rank >> 5;
   int incl = sum;
   for (int o = 1; o < 32; o <<= 1) {
     int y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -759,8 +1029,8 @@ AD_HD void cta_exclusive_scan(TickShared& s, int n) {
   }
   int* wsum = reinterpret_cast<int*>(s.red);
   if (lane == 31) wsum[warp] = incl;
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  group_sync(g);
+  if (g.rank == 0) {
     int acc = 0;
     const int warps = (T + 31) >> 5;
     for (int w2 = 0; w2 < warps; ++w2) {
@@ -770,15 +1040,16 @@ AD_HD void cta_exclusive_scan(TickShared& s, int n) {
     }
     s.cell_start[n] = acc;
   }
-  __syncthreads();
+  group_sync(g);
   int run = wsum[warp] + incl - sum;
   for (int k = b; k < e; ++k) {
     int t = s.cell_start[k];
     s.cell_start[k] = run;
     run += t;
   }
-  __syncthreads();
+  group_sync(g);
 #else
+  (void)g;
   int acc = 0;
   for (int k = 0; k < n; ++k) {
     int t = s.cell_start[k];
@@ -806,6 +1077,31 @@ AD_HD void mark_awake_cell(TickShared& s, int cell) {
 }
 
 AD_HD bool cell_awake(const TickShared& s, int cell) { return (s.awake_bits[cell >> 5] >> (cell & 31)) & 1u; }
+
+AD_HD void push_work(TickShared& s, int i) {
+#if defined(__CUDA_ARCH__)
+  s.work[atomicAdd(&s.nwork, 1)] = (int16_t)i;
+#else
+  s.work[s.nwork++] = (int16_t)i;
+#endif
+}
+
+// A sleeping sphere only receives impulses from awake neighbours: it needs the
+// pair scan iff it is awake or one of its 3x3 cells holds an awake sphere.
+AD_HD bool needs_pair_scan(const TickShared& s, const SimParams& sp, int i) {
+  if (!s.sleep[i]) return true;
+  const int c = s.cell[i];
+  const int cx = c % sp.grid_nx, cy = c / sp.grid_nx;
+  for (int oy = -1; oy <= 1; ++oy) {
+    const int yy = cy + oy;
+    if (yy < 0 || yy >= sp.grid_ny) continue;
+    for (int ox = -1; ox <= 1; ++ox) {
+      const int xx = cx + ox;
+      if (xx >= 0 && xx < sp.grid_nx && cell_awake(s, yy * sp.grid_nx + xx)) return true;
+    }
+  }
+  return false;
+}
 
 AD_HD void static_contact_fuel(TickShared& s, const SimParams& sp, int i, V3 n, float depth, bool valid,
                                float h) {
@@ -835,11 +1131,13 @@ AD_HD void static_contact_fuel(TickShared& s, const SimParams& sp, int i, V3 n, 
 
 // One FUEL substep for the pieces marked free in s.freem
 // (frc_defense/fuel_physics.py:513-587).
-AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
+// FUEL phases that read no robot state (wake, integrate, grid, pair contacts,
+// Jacobi apply), run by thread group `g`.
+AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g) {
   const int P = sp.P;
   const float r2 = 2.f * sp.fr;
   // wake, gravity, explicit position update
-  PAR_FOR(i, P) {
+  GFOR(i, P, g) {
     if (s.freem[i]) {
       float vx = s.fvel[0][i], vy = s.fvel[1][i], vz = s.fvel[2][i];
       float wn = sqrtf(sqr(s.fang[0][i]) + sqr(s.fang[1][i]) + sqr(s.fang[2][i]));
@@ -855,19 +1153,25 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   }
   // uniform XY grid (counting sort)
   const int ncell = sp.grid_nx * sp.grid_ny;
-  PAR_FOR(c, ncell + 1) { s.cell_start[c] = 0; }
-  PAR_FOR(c, ncell / 32 + 1) { s.awake_bits[c] = 0u; }
-  // per-robot heading trig and contact reach for the chassis contacts below
-  PAR_FOR(r, sp.R) {
-    const float th = s.pose[r * 3 + 2];
-    s.rtrig[r * 4 + 0] = cosf(th);
-    s.rtrig[r * 4 + 1] = sinf(th);
-    const float reach = .5f * sqrtf(sqr(rparam(s, r, RP_LENGTH)) + sqr(rparam(s, r, RP_WIDTH))) + sp.fr;
-    s.rtrig[r * 4 + 2] = reach * reach;
+#if defined(__CUDA_ARCH__)
+  {
+    int4* cs = reinterpret_cast<int4*>(s.cell_start);
+    int4* ab = reinterpret_cast<int4*>(s.awake_bits);
+    const int4 z = make_int4(0, 0, 0, 0);
+    GFOR(c, (ncell + 1 + 3) / 4, g) { cs[c] = z; }
+    GFOR(c, (ncell / 32 + 1 + 3) / 4, g) { ab[c] = z; }
   }
-  BARRIER();
-  PHASE_MARK(s, 4);
-  PAR_FOR(i, P) {
+#else
+  GFOR(c, ncell + 1, g) { s.cell_start[c] = 0; }
+  GFOR(c, ncell / 32 + 1, g) { s.awake_bits[c] = 0u; }
+#endif
+  if (g.rank == 0) {
+    s.nwork = 0;
+    s.cmask = 0u;
+  }
+  group_sync(g);
+  PHASE_MARK_BY(s, 4, g.first);
+  GFOR(i, P, g) {
     if (s.freem[i]) {
       int c = fuel_cell_of(sp, s.fpos[0][i], s.fpos[1][i]);
       s.cell[i] = (int16_t)c;
@@ -875,43 +1179,44 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
       if (!s.sleep[i]) mark_awake_cell(s, c);
     }
   }
-  BARRIER();
-  cta_exclusive_scan(s, ncell);
-  BARRIER();
-  PAR_FOR(i, P) {
-    if (s.freem[i]) s.sorted[s.cell_start[(int)s.cell[i]] + (int)s.slot[i]] = (int16_t)i;
+  group_sync(g);
+  group_exclusive_scan(s, ncell, g);
+  GFOR(i, P, g) {
+    bool listed = false;
+    if (s.freem[i]) {
+      s.sorted[s.cell_start[(int)s.cell[i]] + (int)s.slot[i]] = (int16_t)i;
+      listed = needs_pair_scan(s, sp, i);
+      if (listed) push_work(s, i);
+    }
+    s.listed[i] = listed ? 1 : 0;
   }
-  BARRIER();
-  PHASE_MARK(s, 5);
-  // Jacobi pair contacts, each sphere computing the impulses that act on it
+  group_sync(g);
+  PHASE_MARK_BY(s, 5, g.first);
   float local_max[2] = {0.f, 0.f};
   const float I = .4f * sp.fm * sp.fr * sp.fr;
-  PAR_FOR(i, P) {
+  // Jacobi pair contacts over the work list, each sphere computing the
+  // impulses that act on it (spheres off the list receive none this substep)
+  const int nwork = s.nwork;
+  GFOR(k, nwork, g) {
+    const int i = s.work[k];
     float dvx = 0.f, dvy = 0.f, dvz = 0.f, dwx = 0.f, dwy = 0.f, dwz = 0.f;
     int deg = 0;
-    if (s.freem[i]) {
+    {
       const float px = s.fpos[0][i], py = s.fpos[1][i], pz = s.fpos[2][i];
       const int c = s.cell[i];
       const int cx = c % sp.grid_nx, cy = c / sp.grid_nx;
       const bool sleep_i = s.sleep[i];
       const V3 vi = V3{s.fvel[0][i], s.fvel[1][i], s.fvel[2][i]};
       const V3 wi = V3{s.fang[0][i], s.fang[1][i], s.fang[2][i]};
-      // a sleeping sphere only receives impulses from awake neighbours
-      bool scan = !sleep_i;
-      for (int oy = -1; oy <= 1 && !scan; ++oy)
-        for (int ox = -1; ox <= 1 && !scan; ++ox) {
-          int yy = cy + oy, xx = cx + ox;
-          if (yy >= 0 && yy < sp.grid_ny && xx >= 0 && xx < sp.grid_nx) scan = cell_awake(s, yy * sp.grid_nx + xx);
-        }
-      for (int oy = -1; oy <= 1 && scan; ++oy) {
+      for (int oy = -1; oy <= 1; ++oy) {
         int yy = cy + oy;
         if (yy < 0 || yy >= sp.grid_ny) continue;
         for (int ox = -1; ox <= 1; ++ox) {
           int xx = cx + ox;
           if (xx < 0 || xx >= sp.grid_nx) continue;
           int cc = yy * sp.grid_nx + xx;
-          for (int k = s.cell_start[cc]; k < s.cell_start[cc + 1]; ++k) {
-            int j = s.sorted[k];
+          for (int m = s.cell_start[cc]; m < s.cell_start[cc + 1]; ++m) {
+            int j = s.sorted[m];
             if (j == i) continue;
             float dx = px - s.fpos[0][j], dy = py - s.fpos[1][j], dz = pz - s.fpos[2][j];
             float d2 = dx * dx + dy * dy + dz * dz;
@@ -949,13 +1254,14 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
     local_max[0] = fmaxf(local_max[0], sqrtf(dvx * dvx + dvy * dvy + dvz * dvz));
     local_max[1] = fmaxf(local_max[1], (float)deg);
   }
-  BARRIER();
-  cta_max<2>(s, local_max);
-  PHASE_MARK(s, 6);
+  group_sync(g);
+  group_max<2>(s, local_max, g);
+  PHASE_MARK_BY(s, 6, g.first);
   // crowded piles share one Jacobi response scale per world
   const float scale = local_max[1] > 4.f ? fminf(.08f / fmaxf(local_max[0], .08f), 1.f) : 1.f;
-  PAR_FOR(i, P) {
-    if (s.freem[i]) {
+  GFOR(k, nwork, g) {
+    const int i = s.work[k];
+    {
       s.fvel[0][i] += s.dv[0][i] * scale;
       s.fvel[1][i] += s.dv[1][i] * scale;
       s.fvel[2][i] += s.dv[2][i] * scale;
@@ -965,11 +1271,18 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
       if (s.degree[i]) s.sleep[i] = 0;
     }
   }
-  BARRIER();
-  PHASE_MARK(s, 7);
-  // chassis contacts with reciprocal robot impulses
+  group_sync(g);
+  PHASE_MARK_BY(s, 7, g.first);
+}
+
+// FUEL phases coupled to the robots (chassis contacts with reciprocal robot
+// impulses), then terrain / walls / field boxes and sleep; whole CTA.
+AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
+  const int P = sp.P;
+  const float I = .4f * sp.fm * sp.fr * sp.fr;
   float racc[18];
   for (int k = 0; k < 18; ++k) racc[k] = 0.f;
+  uint32_t cmask = 0u;
   PAR_FOR(i, P) {
     if (s.freem[i]) {
       for (int r = 0; r < sp.R; ++r) {
@@ -1012,25 +1325,41 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
         racc[r * 3 + 0] -= imp.x / mr;
         racc[r * 3 + 1] -= imp.y / mr;
         racc[r * 3 + 2] -= (armx * imp.y - army * imp.x) / Ir;
+        cmask |= 1u << r;
         s.sleep[i] = 0;
+        if (!s.listed[i]) {
+          s.listed[i] = 1;
+          push_work(s, i);
+        }
       }
     }
   }
+#if defined(__CUDA_ARCH__)
+  cmask = __reduce_or_sync(0xffffffffu, cmask);
+  if ((threadIdx.x & 31) == 0 && cmask) atomicOr(&s.cmask, cmask);
+#else
+  s.cmask = cmask;
+#endif
   BARRIER();
-  cta_sum<18>(s, racc);
+  cmask = s.cmask;
+  if (cmask) cta_sum_robots(s, racc, cmask);
   PHASE_MARK(s, 8);
   SERIAL_BEGIN
   for (int r = 0; r < sp.R; ++r) {
+    if (!((cmask >> r) & 1u)) continue;
     s.vel[r * 3 + 0] += racc[r * 3 + 0];
     s.vel[r * 3 + 1] += racc[r * 3 + 1];
     s.vel[r * 3 + 2] += racc[r * 3 + 2];
   }
   SERIAL_END
-  // terrain, floor, walls, field boxes, sleep
-  PAR_FOR(i, P) {
+  // terrain, floor, walls, field boxes, sleep, for the awake spheres (all of
+  // them are on the work list: awake at binning, or woken by a chassis contact)
+  const int nwork = s.nwork;
+  PAR_FOR(k, nwork) {
+    const int i = s.work[k];
     // a sleeping sphere has zero velocity and takes no static impulse; it
     // stays asleep (its sleep clock is irrelevant once asleep)
-    if (s.freem[i] && !s.sleep[i]) {
+    if (!s.sleep[i]) {
       float height, grade;
       bool on = bump_height(sp, s.fpos[0][i], s.fpos[1][i], height, grade);
       V3 n = V3{0.f, 0.f, 1.f};
@@ -1077,6 +1406,34 @@ AD_HD void fuel_substep(TickShared& s, const SimParams& sp, float h) {
   }
   BARRIER();
   PHASE_MARK(s, 9);
+}
+
+// One physics substep of robots and FUEL. On the GPU (FUEL on, 256-thread
+// CTA) warp 0 advances the robots while the remaining warps run the FUEL
+// phases that do not read robot state; both groups meet at a CTA barrier
+// before the chassis contacts. Every value is produced by the same
+// operations in the same order as the serial host sequence.
+AD_HD void physics_substep(TickShared& s, const SimParams& sp, World& w, int env, float h) {
+#if defined(__CUDA_ARCH__)
+  if (sp.fuel_physics && blockDim.x == 256) {
+    if (threadIdx.x < 32) {
+      robot_substep(s, sp, w, env, h, Group{(int)threadIdx.x, 32, 0, -1});
+    } else {
+      if (s.prof_on && threadIdx.x == 32) s.prof_last[1] = clock64();
+      fuel_pre(s, sp, h, Group{(int)threadIdx.x - 32, 224, 32, 1});
+    }
+    __syncthreads();
+    PHASE_MARK_BY(s, 12, 0);
+    PHASE_MARK_BY(s, 13, 32);
+    fuel_post(s, sp, h);
+    return;
+  }
+#endif
+  robot_substep(s, sp, w, env, h, group_all());
+  if (sp.fuel_physics) {
+    fuel_pre(s, sp, h, group_all());
+    fuel_post(s, sp, h);
+  }
 }
 
 // Analytic terrain contact height for a ground-spawned sphere
