@@ -186,9 +186,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tick_smem_bytes", &tick_smem_bytes);
   m.def("phase_profile_enable", &phase_profile_enable, "turn the tick kernel's per-phase cycle counters on/off");
   m.def("phase_profile_read", &phase_profile_read,
-        "read and reset the per-phase cycle totals (summed over CTAs): robot swerve, robot sweep, robot "
-        "contacts, robot tail, fuel integrate+clear, fuel grid, fuel pairs, fuel apply, fuel chassis, "
-        "fuel static, pre-substep, post-substep");
+        "read and reset the 18 per-phase cycle totals (summed over CTAs): robot swerve, robot sweep, robot "
+        "contacts, robot tail, fuel integrate+clear, fuel scatter, fuel pairs, fuel apply, fuel chassis "
+        "reduction, fuel static, pre-substep, post-substep, robot-warp join wait, fuel-warps join wait, "
+        "fuel count, fuel scan, fuel chassis loop, unused");
   m.def("plan_smem_bytes", [](py::dict d) { return plan_smem_bytes(params_from_dict(d)); });
   py::class_<Sim>(m, "Sim")
       .def(py::init<std::vector<torch::Tensor>, py::dict>())

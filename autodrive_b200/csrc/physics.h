@@ -74,7 +74,7 @@ struct TickShared {
   float scal[8];
   // phase accounting (PHASE_MARK): [0] thread 0's timeline, [1] the FUEL warps' leader
   unsigned long long prof_last[2];
-  unsigned long long prof[14];
+  unsigned long long prof[18];
   int32_t prof_on;
 };
 
@@ -1012,41 +1012,60 @@ AD_HD int fuel_cell_of(const SimParams& sp, float x, float y) {
 
 // Exclusive scan of cell_start[0..n) in place; cell_start[n] = total.
 // Exclusive scan of cell_start[0..n) by a thread group; cell_start[n] = total.
+// On the GPU each warp owns a 128-cell-aligned segment and reads it as int4
+// (lane-consecutive, no bank conflicts): pass 1 sums the segment, pass 2 scans
+// it with a running carry that starts at the sum of the earlier segments.
 AD_HD void group_exclusive_scan(TickShared& s, int n, const Group& g) {
 #if defined(__CUDA_ARCH__)
-  // each thread scans a contiguous chunk serially, then a scan of chunk totals
-  const int T = g.size;
-  const int chunk = (n + T - 1) / T;
-  const int b = g.rank * chunk;
-  const int e = min(b + chunk, n);
-  int sum = 0;
-  for (int k = b; k < e; ++k) sum += s.cell_start[k];
-  const int lane = threadIdx.x & 31, warp = g.rank >> 5;
-  int incl = sum;
-  for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
+  const int lane = threadIdx.x & 31, warp = g.rank >> 5, warps = g.size >> 5;
+  const int seg = ((n + warps - 1) / warps + 127) & ~127;
+  const int b = warp * seg, e = min(b + seg, n);
+  int4* cs4 = reinterpret_cast<int4*>(s.cell_start);
   int* wsum = reinterpret_cast<int*>(s.red);
-  if (lane == 31) wsum[warp] = incl;
+  int tot = 0;
+  for (int c = b + lane * 4; c < e; c += 128) {
+    const int4 v = cs4[c >> 2];
+    tot += v.x + (c + 1 < e ? v.y : 0) + (c + 2 < e ? v.z : 0) + (c + 3 < e ? v.w : 0);
+  }
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  if (lane == 0) wsum[warp] = tot;
   group_sync(g);
-  if (g.rank == 0) {
-    int acc = 0;
-    const int warps = (T + 31) >> 5;
-    for (int w2 = 0; w2 < warps; ++w2) {
-      int t = wsum[w2];
-      wsum[w2] = acc;
-      acc += t;
+  int carry = 0, all = 0;
+  for (int w2 = 0; w2 < warps; ++w2) {
+    const int t = wsum[w2];
+    if (w2 < warp) carry += t;
+    all += t;
+  }
+  for (int c0 = b; c0 < b + seg; c0 += 128) {  // uniform trip count: every lane shuffles
+    const int c = c0 + lane * 4;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (c < e) {
+      v = cs4[c >> 2];
+      if (c + 1 >= e) v.y = 0;
+      if (c + 2 >= e) v.z = 0;
+      if (c + 3 >= e) v.w = 0;
     }
-    s.cell_start[n] = acc;
+    const int lsum = v.x + v.y + v.z + v.w;
+    int incl = lsum;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int base = carry + incl - lsum;
+    if (c < e) {
+      const int4 out = make_int4(base, base + v.x, base + v.x + v.y, base + v.x + v.y + v.z);
+      if (c + 3 < e) {
+        cs4[c >> 2] = out;
+      } else {
+        s.cell_start[c] = out.x;
+        if (c + 1 < e) s.cell_start[c + 1] = out.y;
+        if (c + 2 < e) s.cell_start[c + 2] = out.z;
+      }
+    }
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+    if (c0 + 128 >= e) break;
   }
-  group_sync(g);
-  int run = wsum[warp] + incl - sum;
-  for (int k = b; k < e; ++k) {
-    int t = s.cell_start[k];
-    s.cell_start[k] = run;
-    run += t;
-  }
+  if (g.rank == 0) s.cell_start[n] = all;
   group_sync(g);
 #else
   (void)g;
@@ -1078,11 +1097,20 @@ AD_HD void mark_awake_cell(TickShared& s, int cell) {
 
 AD_HD bool cell_awake(const TickShared& s, int cell) { return (s.awake_bits[cell >> 5] >> (cell & 31)) & 1u; }
 
-AD_HD void push_work(TickShared& s, int i) {
+// Append sphere i to the work list when `take` (warp-aggregated on the GPU:
+// one shared atomic per warp). Every lane of the warp must call it.
+AD_HD void push_work(TickShared& s, int i, bool take) {
 #if defined(__CUDA_ARCH__)
-  s.work[atomicAdd(&s.nwork, 1)] = (int16_t)i;
+  const unsigned m = __ballot_sync(0xffffffffu, take);
+  if (!m) return;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(m) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(&s.nwork, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (take) s.work[base + __popc(m & ((1u << lane) - 1u))] = (int16_t)i;
 #else
-  s.work[s.nwork++] = (int16_t)i;
+  if (take) s.work[s.nwork++] = (int16_t)i;
 #endif
 }
 
@@ -1090,8 +1118,9 @@ AD_HD void push_work(TickShared& s, int i) {
 // pair scan iff it is awake or one of its 3x3 cells holds an awake sphere.
 AD_HD bool needs_pair_scan(const TickShared& s, const SimParams& sp, int i) {
   if (!s.sleep[i]) return true;
-  const int c = s.cell[i];
-  const int cx = c % sp.grid_nx, cy = c / sp.grid_nx;
+  // the cell index of fuel_cell_of, without an integer division
+  const int cx = clampi((int)floorf(s.fpos[0][i] / sp.grid_cell), 0, sp.grid_nx - 1);
+  const int cy = clampi((int)floorf(s.fpos[1][i] / sp.grid_cell), 0, sp.grid_ny - 1);
   for (int oy = -1; oy <= 1; ++oy) {
     const int yy = cy + oy;
     if (yy < 0 || yy >= sp.grid_ny) continue;
@@ -1180,15 +1209,20 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
     }
   }
   group_sync(g);
+  PHASE_MARK_BY(s, 14, g.first);
   group_exclusive_scan(s, ncell, g);
-  GFOR(i, P, g) {
+  PHASE_MARK_BY(s, 15, g.first);
+  for (int b0 = 0; b0 < P; b0 += g.size) {  // uniform trip count (warp-aggregated push)
+    const int i = b0 + g.rank;
     bool listed = false;
-    if (s.freem[i]) {
-      s.sorted[s.cell_start[(int)s.cell[i]] + (int)s.slot[i]] = (int16_t)i;
-      listed = needs_pair_scan(s, sp, i);
-      if (listed) push_work(s, i);
+    if (i < P) {
+      if (s.freem[i]) {
+        s.sorted[s.cell_start[(int)s.cell[i]] + (int)s.slot[i]] = (int16_t)i;
+        listed = needs_pair_scan(s, sp, i);
+      }
+      s.listed[i] = listed ? 1 : 0;
     }
-    s.listed[i] = listed ? 1 : 0;
+    push_work(s, i, listed);
   }
   group_sync(g);
   PHASE_MARK_BY(s, 5, g.first);
@@ -1203,25 +1237,30 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
     int deg = 0;
     {
       const float px = s.fpos[0][i], py = s.fpos[1][i], pz = s.fpos[2][i];
-      const int c = s.cell[i];
-      const int cx = c % sp.grid_nx, cy = c / sp.grid_nx;
+      // neighbour rows: cells x-1..x+1 of a row are consecutive in the sorted order
+      const int cx = clampi((int)floorf(px / sp.grid_cell), 0, sp.grid_nx - 1);
+      const int cy = clampi((int)floorf(py / sp.grid_cell), 0, sp.grid_ny - 1);
+      const int x0 = cx > 0 ? cx - 1 : 0, x1 = cx + 1 < sp.grid_nx ? cx + 1 : sp.grid_nx - 1;
       const bool sleep_i = s.sleep[i];
       const V3 vi = V3{s.fvel[0][i], s.fvel[1][i], s.fvel[2][i]};
       const V3 wi = V3{s.fang[0][i], s.fang[1][i], s.fang[2][i]};
       for (int oy = -1; oy <= 1; ++oy) {
-        int yy = cy + oy;
+        const int yy = cy + oy;
         if (yy < 0 || yy >= sp.grid_ny) continue;
-        for (int ox = -1; ox <= 1; ++ox) {
-          int xx = cx + ox;
-          if (xx < 0 || xx >= sp.grid_nx) continue;
-          int cc = yy * sp.grid_nx + xx;
-          for (int m = s.cell_start[cc]; m < s.cell_start[cc + 1]; ++m) {
+        const int row = yy * sp.grid_nx;
+        if (sleep_i) {  // a sleeping sphere only interacts with awake ones
+          bool awake_row = false;
+          for (int xx = x0; xx <= x1; ++xx) awake_row = awake_row || cell_awake(s, row + xx);
+          if (!awake_row) continue;
+        }
+        {
+          const int m_end = s.cell_start[row + x1 + 1];
+          for (int m = s.cell_start[row + x0]; m < m_end; ++m) {
             int j = s.sorted[m];
-            if (j == i) continue;
+            if (j == i || (sleep_i && s.sleep[j])) continue;
             float dx = px - s.fpos[0][j], dy = py - s.fpos[1][j], dz = pz - s.fpos[2][j];
             float d2 = dx * dx + dy * dy + dz * dz;
             if (d2 >= r2 * r2) continue;
-            if (sleep_i && s.sleep[j]) continue;
             float d = sqrtf(d2);
             V3 n = d < 1e-12f ? V3{(j > i) ? 1.f : -1.f, 0.f, 0.f} : V3{dx / d, dy / d, dz / d};
             V3 ri = V3{-.5f * d * n.x, -.5f * d * n.y, -.5f * d * n.z};
@@ -1283,8 +1322,10 @@ AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
   float racc[18];
   for (int k = 0; k < 18; ++k) racc[k] = 0.f;
   uint32_t cmask = 0u;
-  PAR_FOR(i, P) {
-    if (s.freem[i]) {
+  for (int b0 = 0; b0 < P; b0 += AD_NT) {  // uniform trip count (warp-aggregated push)
+    const int i = b0 + AD_TID;
+    bool take = false;
+    if (i < P && s.freem[i]) {
       for (int r = 0; r < sp.R; ++r) {
         const float* rp = s.pose + r * 3;
         const float* rv = s.vel + r * 3;
@@ -1329,10 +1370,11 @@ AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
         s.sleep[i] = 0;
         if (!s.listed[i]) {
           s.listed[i] = 1;
-          push_work(s, i);
+          take = true;
         }
       }
     }
+    push_work(s, i, take);
   }
 #if defined(__CUDA_ARCH__)
   cmask = __reduce_or_sync(0xffffffffu, cmask);
@@ -1341,6 +1383,7 @@ AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
   s.cmask = cmask;
 #endif
   BARRIER();
+  PHASE_MARK(s, 16);
   cmask = s.cmask;
   if (cmask) cta_sum_robots(s, racc, cmask);
   PHASE_MARK(s, 8);

@@ -261,7 +261,7 @@ __global__ void observe_kernel(World w, SimParams sp) {
 }
 
 __device__ int g_prof_on = 0;
-__device__ unsigned long long g_prof[14];
+__device__ unsigned long long g_prof[18];
 
 __global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -271,12 +271,12 @@ __global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uin
   if (e >= sp.n || !w.active[e]) return;
   if (threadIdx.x == 0) {
     s.prof_on = g_prof_on;
-    for (int k = 0; k < 14; ++k) s.prof[k] = 0ull;
+    for (int k = 0; k < 18; ++k) s.prof[k] = 0ull;
     s.prof_last[0] = s.prof_last[1] = clock64();
   }
   tick_env(w, sp, s, e, tick, poss, run_game);
   if (threadIdx.x == 0 && s.prof_on)
-    for (int k = 0; k < 14; ++k) atomicAdd(&g_prof[k], s.prof[k]);
+    for (int k = 0; k < 18; ++k) atomicAdd(&g_prof[k], s.prof[k]);
 }
 
 __global__ void __launch_bounds__(512) perceive_kernel(World w, SimParams sp) {
@@ -345,10 +345,10 @@ void phase_profile_enable(bool on) {
 }
 
 std::vector<unsigned long long> phase_profile_read() {
-  std::vector<unsigned long long> out(14, 0ull);
-  check(cudaMemcpyFromSymbol(out.data(), g_prof, sizeof(unsigned long long) * 14), "phase profile read");
-  std::vector<unsigned long long> zero(14, 0ull);
-  check(cudaMemcpyToSymbol(g_prof, zero.data(), sizeof(unsigned long long) * 14), "phase profile reset");
+  std::vector<unsigned long long> out(18, 0ull);
+  check(cudaMemcpyFromSymbol(out.data(), g_prof, sizeof(unsigned long long) * 18), "phase profile read");
+  std::vector<unsigned long long> zero(18, 0ull);
+  check(cudaMemcpyToSymbol(g_prof, zero.data(), sizeof(unsigned long long) * 18), "phase profile reset");
   return out;
 }
 
