@@ -179,6 +179,7 @@ struct Sim {
 void register_policy_ops(py::module& m);
 void register_comm_ops(py::module& m);
 void register_policy_tc_ops(py::module& m);
+void register_tc_gemm_ops(py::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200-native FRC REBUILT simulator kernels";
@@ -205,4 +206,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_policy_ops(m);
   register_comm_ops(m);
   register_policy_tc_ops(m);
+  register_tc_gemm_ops(m);
 }

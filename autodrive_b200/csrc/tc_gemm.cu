@@ -1,0 +1,284 @@
+// General bf16 tensor-core GEMM for sm_100a: C[M,N] = A[M,K] * B[N,K]^T with
+// fp32 accumulation in TMEM and a fused bias + activation epilogue.
+//
+// Either operand may be stored K-major (row-major [rows][K]) or MN-major
+// (row-major [K][rows], i.e. the transpose), selected per call, so the three
+// GEMMs of a linear layer need no transposed copies:
+//   forward  Y  = X W^T      A = X  (K-major),  B = W  (K-major)
+//   dX       dX = dY W       A = dY (K-major),  B = W  (MN-major)
+//   dW       dW = dY^T X     A = dY (MN-major), B = X  (MN-major)
+//
+// One CTA per 128x128 output tile, 192 threads:
+//   warp 0  TMA producer: 2-D tiled loads (128-byte swizzle) of the A and B
+//           tiles of each 64-deep K step into a 4-stage shared-memory ring;
+//   warp 1  allocates 128 TMEM columns; one lane issues 4 tcgen05.mma per K
+//           step and commits each stage back to the producer, then signals
+//           the epilogue;
+//   warps 2-5 epilogue: tcgen05.ld of the fp32 accumulator rows, + bias,
+//           activation, fp32 or bf16 stores with bounds checks.
+// Out-of-range tile parts are zero-filled by the TMA unit. Every mbarrier
+// wait is bounded in wall-clock time; a wait that runs out sets a bit in a
+// device status word and the CTA drains and exits.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "tc_sm100.h"
+
+namespace py = pybind11;
+
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTileBytes = 128 * 128;        // one 128 x 64 bf16 operand tile
+constexpr uint32_t kStageBytes = 2 * kTileBytes;
+constexpr uint64_t kWaitNs = 2000000000ull;       // 2 s
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
+
+struct GemmArgs {
+  int M, N, K;
+  float* c_f32;
+  __nv_bfloat16* c_bf16;
+  int64_t ldc;
+  const float* bias;   // [N] or null
+  int act;             // 0 none, 1 tanh, 2 relu, 3 gelu (tanh form)
+  int accumulate;      // C += result (fp32 output only)
+  int* status;
+};
+
+__device__ __forceinline__ float apply_act(float x, int act) {
+  switch (act) {
+    case 1: return tanhf(x);
+    case 2: return fmaxf(x, 0.f);
+    case 3: {
+      const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+      return 0.5f * x * (1.f + tanhf(u));
+    }
+    default: return x;
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* misc = smem + kStages * kStageBytes;
+  const uint32_t full0 = tc::smem_u32(misc);             // kStages mbarriers
+  const uint32_t empty0 = full0 + 8 * kStages;           // kStages mbarriers
+  const uint32_t accbar = empty0 + 8 * kStages;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kStages + 1));
+  int* s_fail = reinterpret_cast<int*>(misc + 8 * (2 * kStages + 1) + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+  const int KT = (g.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(full0 + 8 * s, 1);
+      tc::mbar_init(empty0 + 8 * s, 1);
+    }
+    tc::mbar_init(accbar, 1);
+    tc::mbar_init_fence();
+    *s_fail = 0;
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_u32(s_tmem), 128);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kStages;
+      if (kt >= kStages && !tc::mbar_wait(empty0 + 8 * s, ((kt / kStages) - 1) & 1, kWaitNs)) {
+        atomicOr(g.status, 1);
+        atomicExch(s_fail, 1);
+        break;
+      }
+      if (*reinterpret_cast<volatile int*>(s_fail)) break;
+      const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
+      const uint32_t sb = sa + kTileBytes;
+      const uint32_t full = full0 + 8 * s;
+      tc::mbar_arrive_expect_tx(full, kStageBytes);
+      const int k0 = kt * kBK;
+      if (A_MN) {
+        tc::tma_load_2d(sa, &ta, m0, k0, full);
+        tc::tma_load_2d(sa + kTileBytes / 2, &ta, m0 + 64, k0, full);
+      } else {
+        tc::tma_load_2d(sa, &ta, k0, m0, full);
+      }
+      if (B_MN) {
+        tc::tma_load_2d(sb, &tb, n0, k0, full);
+        tc::tma_load_2d(sb + kTileBytes / 2, &tb, n0 + 64, k0, full);
+      } else {
+        tc::tma_load_2d(sb, &tb, k0, n0, full);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    const uint32_t id = tc::idesc_bf16(kBM, kBN, A_MN, B_MN);
+    bool ok = true;
+    for (int kt = 0; kt < KT && ok; ++kt) {
+      const int s = kt % kStages;
+      if (!tc::mbar_wait(full0 + 8 * s, (kt / kStages) & 1, kWaitNs)) {
+        atomicOr(g.status, 2);
+        atomicExch(s_fail, 1);
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
+      const uint32_t sb = sa + kTileBytes;
+#pragma unroll
+      for (int ks = 0; ks < kBK / 16; ++ks) {
+        const uint64_t da = A_MN ? tc::desc_mnmajor(sa, kBK, ks) : tc::desc_kmajor(sa, kBM, ks);
+        const uint64_t db = B_MN ? tc::desc_mnmajor(sb, kBK, ks) : tc::desc_kmajor(sb, kBN, ks);
+        tc::mma_bf16(tmem, da, db, id, kt > 0 || ks > 0);
+      }
+      tc::mma_commit(empty0 + 8 * s);   // stage free once these MMAs have read it
+    }
+    tc::mma_commit(accbar);             // accumulator complete (or nothing issued)
+  }
+
+  if (warp >= 2) {
+    // ---- epilogue ----
+    const bool got = tc::mbar_wait(accbar, 0, kWaitNs);
+    if (!got) atomicOr(g.status, 4);
+    tc::tc_fence_after();
+    const int q = warp & 3;
+    const int row = m0 + 32 * q + lane;
+    if (got && !*reinterpret_cast<volatile int*>(s_fail)) {
+#pragma unroll 1
+      for (int cc = 0; cc < kBN / 32; ++cc) {
+        float v[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
+        if (row < g.M) {
+          const int c0 = n0 + 32 * cc;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = c0 + i;
+            if (col < g.N) {
+              float x = v[i] + (g.bias ? g.bias[col] : 0.f);
+              x = apply_act(x, g.act);
+              const int64_t off = (int64_t)row * g.ldc + col;
+              if (g.c_f32) g.c_f32[off] = g.accumulate ? g.c_f32[off] + x : x;
+              else g.c_bf16[off] = __float2bfloat16_rn(x);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 128);
+  }
+}
+
+// 2-D bf16 tensor map over a row-major [rows][cols] matrix with row stride
+// `ld` elements; box = 64 columns x box_rows rows, 128-byte swizzle.
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+template <bool A_MN, bool B_MN>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
+    configured = true;
+  }
+  dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM);
+  tc_gemm_kernel<A_MN, B_MN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "tc_gemm launch failed");
+}
+
+// C = op(A) op(B)^T. `a_mn`: A is stored [K][M] (else [M][K]); `b_mn`: B is
+// stored [K][N] (else [N][K]). Storage row strides must be multiples of 8
+// elements and the base pointers 16-byte aligned (TMA rules).
+void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c,
+             c10::optional<torch::Tensor> bias, int64_t act, bool accumulate, torch::Tensor status) {
+  for (auto* t : {&a, &b, &c, &status})
+    TORCH_CHECK(t->is_cuda() && t->dim() >= 1, "tc_gemm operands must be CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
+              "tc_gemm operands must both be bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "tc_gemm takes 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "innermost dims must be contiguous");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "row strides must be multiples of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0, "operands must be 16-byte aligned");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "tc_gemm: inner dimensions differ");
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "tc_gemm: output must be [M, N]");
+  TORCH_CHECK(c.scalar_type() == torch::kFloat32 || c.scalar_type() == torch::kBFloat16, "output fp32 or bf16");
+  TORCH_CHECK(!accumulate || c.scalar_type() == torch::kFloat32, "accumulate needs an fp32 output");
+  TORCH_CHECK(status.scalar_type() == torch::kInt32, "status must be int32");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "tc_gemm dimensions too large");
+  if (M == 0 || N == 0) return;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.c_f32 = c.scalar_type() == torch::kFloat32 ? c.data_ptr<float>() : nullptr;
+  g.c_bf16 = c.scalar_type() == torch::kBFloat16 ? reinterpret_cast<__nv_bfloat16*>(c.data_ptr<at::BFloat16>()) : nullptr;
+  g.ldc = c.stride(0);
+  g.bias = nullptr;
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->is_cuda() && bias->scalar_type() == torch::kFloat32 && bias->numel() == N && bias->is_contiguous(),
+                "bias must be fp32 [N]");
+    g.bias = bias->data_ptr<float>();
+  }
+  g.act = (int)act;
+  g.accumulate = accumulate ? 1 : 0;
+  g.status = status.data_ptr<int>();
+  if (K == 0) {  // empty contraction: C = act(bias) (or unchanged when accumulating zero)
+    auto z = torch::zeros({M, N}, c.options().dtype(torch::kFloat32));
+    if (g.bias) z += *bias;
+    if (act == 1) z = z.tanh();
+    else if (act == 2) z = z.relu();
+    else if (act == 3) z = torch::gelu(z, "tanh");
+    if (accumulate) c.add_(z);
+    else c.copy_(z);
+    return;
+  }
+  // A: K-major [M][K] -> box 64 K x 128 rows; MN-major [K][M] -> box 64 M x 64 K rows
+  const CUtensorMap ta = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), kBK) : make_map(a.data_ptr(), M, K, a.stride(0), kBM);
+  const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), kBK) : make_map(b.data_ptr(), N, K, b.stride(0), kBN);
+  auto st = c10::cuda::getCurrentCUDAStream().stream();
+  if (!a_mn && !b_mn) launch<false, false>(ta, tb, g, st);
+  else if (!a_mn && b_mn) launch<false, true>(ta, tb, g, st);
+  else if (a_mn && !b_mn) launch<true, false>(ta, tb, g, st);
+  else launch<true, true>(ta, tb, g, st);
+}
+
+}  // namespace
+
+void register_tc_gemm_ops(py::module& m) {
+  m.def("tc_gemm", &tc_gemm, "bf16 tcgen05 GEMM C = op(A) op(B)^T (+bias, activation), TMA-fed, fp32 accumulate",
+        py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("c"), py::arg("bias"),
+        py::arg("act"), py::arg("accumulate"), py::arg("status"));
+}

@@ -1,0 +1,130 @@
+"""Linear layers on the sm_100a tensor-core GEMM (``csrc/tc_gemm.cu``).
+
+``TcLinear`` is a drop-in ``nn.Linear`` (same ``weight`` / ``bias`` parameters,
+same state-dict keys) whose forward and backward run as bf16 tcgen05 GEMMs
+with fp32 accumulation on CUDA:
+
+    forward  Y  = X W^T + b        (bias and tanh/relu fused in the epilogue)
+    dX       dY W                   (W read MN-major, no transpose)
+    dW       dY^T X                 (both read MN-major, no transpose)
+
+Inputs are rounded to bf16 and zero-padded to a multiple of 8 features (the
+TMA row-stride rule); parameters stay fp32 masters. On CPU the layer is
+``F.linear``. ``tensorize(module)`` swaps every ``nn.Linear`` of a module for
+a ``TcLinear`` sharing its parameters.
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from .ext import require_extension
+
+ACTS = {None: 0, "none": 0, "tanh": 1, "relu": 2}
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def _bf16_padded(x: torch.Tensor, cols: int, rows: int | None = None) -> torch.Tensor:
+    r = x.shape[0] if rows is None else rows
+    if x.dtype == torch.bfloat16 and x.shape[1] == cols and r == x.shape[0] and x.is_contiguous():
+        return x
+    out = torch.zeros((r, cols), dtype=torch.bfloat16, device=x.device)
+    out[:x.shape[0], :x.shape[1]] = x
+    return out
+
+
+class _Status:
+    tensors: dict = {}
+
+    @classmethod
+    def get(cls, device) -> torch.Tensor:
+        key = str(device)
+        if key not in cls.tensors:
+            cls.tensors[key] = torch.zeros(1, dtype=torch.int32, device=device)
+        return cls.tensors[key]
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, bias=None, act=None,
+         out: torch.Tensor | None = None, accumulate: bool = False, out_dtype=torch.float32) -> torch.Tensor:
+    """C = op(A) op(B)^T on the tensor cores; A is [M,K] (or [K,M] when a_mn),
+    B is [N,K] (or [K,N] when b_mn); both bf16 with row strides % 8 == 0."""
+    ext = require_extension()
+    m = a.shape[1] if a_mn else a.shape[0]
+    n = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    ext.tc_gemm(a, a_mn, b, b_mn, out, bias, ACTS[act], accumulate, _Status.get(a.device))
+    return out
+
+
+class _TcLinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, act):
+        out_f, in_f = weight.shape
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, in_f)
+        in_p, out_p = _pad8(in_f), _pad8(out_f)
+        xb = _bf16_padded(x2, in_p)
+        wb = _bf16_padded(weight.detach(), in_p, rows=out_p)
+        y = gemm(xb, wb[:out_f], bias=None if bias is None else bias.detach().float().contiguous(), act=act)
+        ctx.act = act
+        ctx.shapes = (in_f, out_f, in_p, out_p, lead)
+        ctx.has_bias = bias is not None
+        ctx.save_for_backward(xb, wb, y if act in ("tanh", "relu") else torch.empty(0, device=x.device))
+        return y.reshape(*lead, out_f).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, gy):
+        xb, wb, y = ctx.saved_tensors
+        in_f, out_f, in_p, out_p, lead = ctx.shapes
+        g = gy.reshape(-1, out_f).float()
+        if ctx.act == "tanh":
+            g = g * (1 - y * y)
+        elif ctx.act == "relu":
+            g = g * (y > 0)
+        gb = _bf16_padded(g, out_p)
+        gx = gw = gbias = None
+        if ctx.needs_input_grad[0]:
+            gx = gemm(gb, wb, b_mn=True)[:, :in_f].reshape(*lead, in_f)
+        if ctx.needs_input_grad[1]:
+            gw = gemm(gb, xb, a_mn=True, b_mn=True)[:out_f, :in_f]
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            gbias = g.sum(0)
+        return gx, gw, gbias, None
+
+
+class TcLinear(nn.Linear):
+    """nn.Linear on the tensor-core GEMM (CUDA), optional fused activation."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, act: str | None = None,
+                 device=None, dtype=None):
+        super().__init__(in_features, out_features, bias, device=device, dtype=dtype)
+        if act not in ACTS:
+            raise ValueError(f"activation must be one of {sorted(k for k in ACTS if k)}")
+        self.act = act
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.device.type != "cuda":
+            y = F.linear(x, self.weight, self.bias)
+            return torch.tanh(y) if self.act == "tanh" else (F.relu(y) if self.act == "relu" else y)
+        return _TcLinearFn.apply(x, self.weight, self.bias, self.act)
+
+
+def tensorize(module: nn.Module) -> nn.Module:
+    """Replace every nn.Linear in `module` (recursively) with a TcLinear that
+    shares its parameters. Returns the module."""
+    for name, child in list(module.named_children()):
+        if type(child) is nn.Linear:
+            tl = TcLinear.__new__(TcLinear)
+            nn.Module.__init__(tl)
+            tl.in_features, tl.out_features, tl.act = child.in_features, child.out_features, None
+            tl.weight = child.weight
+            tl.bias = child.bias
+            setattr(module, name, tl)
+        else:
+            tensorize(child)
+    return module

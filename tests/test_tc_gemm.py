@@ -1,0 +1,101 @@
+"""tcgen05 GEMM and TcLinear against plain PyTorch fp32 references."""
+import pytest
+import torch
+from torch import nn
+
+from autodrive_b200.ops.tc_linear import TcLinear, gemm, tensorize
+
+
+def _store(t: torch.Tensor) -> torch.Tensor:
+    """bf16 copy of a 2-D tensor in storage whose row stride is a multiple of 8."""
+    r, c = t.shape
+    buf = torch.zeros((r, (c + 7) // 8 * 8), dtype=torch.bfloat16, device=t.device)
+    buf[:, :c] = t
+    return buf[:, :c]
+
+
+def test_tc_linear_cpu_matches_linear():
+    torch.manual_seed(0)
+    lin = nn.Linear(13, 7)
+    tl = tensorize(nn.Sequential(lin))[0]
+    assert isinstance(tl, TcLinear) and tl.weight is lin.weight
+    x = torch.randn(5, 13)
+    assert torch.allclose(tl(x), x @ lin.weight.T + lin.bias)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("mnk", [(128, 128, 64), (300, 200, 152), (1000, 72, 1024), (64, 520, 40)])
+def test_gemm_majors_match_fp32(a_mn, b_mn, mnk):
+    m, n, k = mnk
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(n, k, device="cuda", generator=g)
+    ab, bb = a.bfloat16(), b.bfloat16()
+    ref = ab.float() @ bb.float().T
+    a_arg = _store(ab.T.contiguous()) if a_mn else _store(ab)
+    b_arg = _store(bb.T.contiguous()) if b_mn else _store(bb)
+    out = gemm(a_arg, b_arg, a_mn=a_mn, b_mn=b_mn)
+    torch.cuda.synchronize()
+    err = (out - ref).abs().max().item()
+    assert err < 1e-3 * max(1., ref.abs().max().item()), err
+
+
+@pytest.mark.gpu
+def test_gemm_epilogues():
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(257, 96, device="cuda", generator=g).bfloat16()
+    b = torch.randn(130, 96, device="cuda", generator=g).bfloat16()
+    bias = torch.randn(130, device="cuda", generator=g)
+    ref = a.float() @ b.float().T + bias
+    assert torch.allclose(gemm(a, b, bias=bias, act="tanh"), ref.tanh(), atol=2e-3)
+    assert torch.allclose(gemm(a, b, bias=bias, act="relu"), ref.relu(), atol=2e-3)
+    out16 = gemm(a, b, bias=bias, out_dtype=torch.bfloat16)
+    assert out16.dtype == torch.bfloat16 and torch.allclose(out16.float(), ref, atol=5e-2, rtol=1e-2)
+    acc = torch.ones(257, 130, device="cuda")
+    gemm(a, b, out=acc, accumulate=True)
+    assert torch.allclose(acc, 1 + a.float() @ b.float().T, atol=2e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("act", [None, "tanh", "relu"])
+def test_tc_linear_forward_backward(act):
+    torch.manual_seed(1)
+    ref = nn.Linear(137, 130).cuda()
+    tl = TcLinear(137, 130, act=act).cuda()
+    tl.load_state_dict(ref.state_dict())
+    x = torch.randn(777, 137, device="cuda", requires_grad=True)
+    x2 = x.detach().clone().requires_grad_(True)
+    y_ref = ref(x2)
+    y_ref = y_ref.tanh() if act == "tanh" else (y_ref.relu() if act == "relu" else y_ref)
+    y = tl(x)
+    assert (y - y_ref).abs().max().item() < 3e-2
+    w = torch.randn_like(y)
+    if act == "relu":
+        # bf16 inputs flip the gate of pre-activations within rounding of 0:
+        # compare gradients under the kernel's own gate
+        w = w * ((y > 0) == (y_ref > 0)).float()
+    (y * w).sum().backward()
+    (y_ref * w).sum().backward()
+    for got, want in ((x.grad, x2.grad), (tl.weight.grad, ref.weight.grad), (tl.bias.grad, ref.bias.grad)):
+        rel = (got - want).norm().item() / max(want.norm().item(), 1e-12)
+        assert rel < 2e-2, rel
+
+
+@pytest.mark.gpu
+def test_tensorized_mlp_trains():
+    torch.manual_seed(2)
+    net = nn.Sequential(nn.Linear(64, 256), nn.Tanh(), nn.Linear(256, 256), nn.Tanh(), nn.Linear(256, 1)).cuda()
+    tensorize(net)
+    opt = torch.optim.Adam(net.parameters(), lr=3e-3)
+    x = torch.randn(4096, 64, device="cuda")
+    target = (x[:, :4].sum(-1, keepdim=True)).tanh()
+    first = None
+    for _ in range(150):
+        loss = (net(x) - target).square().mean()
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        first = first if first is not None else loss.item()
+    assert loss.item() < .2 * first
