@@ -98,6 +98,7 @@ class TensorThreeVsThreeEnv:
         self.device = torch.device(device)
         self.dt, self.horizon = float(dt), int(horizon)
         self.field_length = float(field_length)
+        self.field_width = float(field_width)
         self.alliance_zone_depth = float(fieldmod.ALLIANCE_ZONE_DEPTH)
         self.obs_dim, self.action_dim, self.action_kind = OBS_DIM, ACTION_DIM, "categorical"
         self.fuel_count = int(fuel_count)

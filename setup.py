@@ -21,7 +21,6 @@ ext = CUDAExtension(
                 ARCH + ["-O3", "-lineinfo", "-std=c++17", "--use_fast_math",
                         "--expt-relaxed-constexpr"],
     },
-    extra_link_args=["-lcuda"],
 )
 
 setup(
