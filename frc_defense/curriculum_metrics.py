@@ -1,0 +1,2 @@
+"""Compatibility import path: ``frc_defense.curriculum_metrics`` -> ``autodrive_b200.train.curriculum``."""
+from autodrive_b200.train.curriculum import *  # noqa: F401,F403
