@@ -41,12 +41,13 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kThreads = 512;
-constexpr int kPadWords = 256;          // per-rank signal pad (uint32 words)
+constexpr int kPadWords = 1024;         // per-rank signal pad (uint32 words)
 // pad layout (uint32 words): [0,8) ready flags, [8,16) norm flags, [16,24) done
 // flags, [32,48) shard sums of squares as float bits (indexed by rank),
-// [64, 64 + 2*kMaxCta) per-CTA partials (local use only)
+// [64, 64 + kMaxCta] per-CTA partials and the clip scale (local use only)
 constexpr int kFlagReady = 0, kFlagNorm = 8, kFlagDone = 16, kNorms = 32, kPartials = 64;
-constexpr int kMaxCta = 96;
+constexpr int kMaxCta = 296;              // 2 CTAs per SM on a 148-SM part
+constexpr int kUnroll = 4;                // independent 16-byte loads in flight per thread and peer
 
 struct Ptrs {
   float* grad[kMaxRanks];
@@ -79,6 +80,45 @@ __device__ bool cross_rank_barrier(const Ptrs& P, int world, int rank, int slot,
   return true;
 }
 
+// out[4k..4k+3] = (1/W) sum over ranks of grad_q[base + 4k..], k in [0, nvec);
+// returns this thread's sum of squares of the written values. Every thread
+// issues kUnroll independent 16-byte loads per rank before using any, so
+// enough remote bytes are in flight to cover the NVLink round trip.
+__device__ __forceinline__ float reduce_range(const Ptrs& P, int world, float* __restrict__ out, int64_t base,
+                                              int64_t nvec, float inv_w) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  float acc = 0.f;
+  for (int64_t k0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k0 < nvec; k0 += kUnroll * stride) {
+    float4 s[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {
+      if (q >= world) break;
+      float4 x[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t k = k0 + u * stride;
+        x[u] = k < nvec ? __ldcg(reinterpret_cast<const float4*>(P.grad[q] + base) + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        s[u].x += x[u].x; s[u].y += x[u].y; s[u].z += x[u].z; s[u].w += x[u].w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t k = k0 + u * stride;
+      if (k < nvec) {
+        float4 r = make_float4(s[u].x * inv_w, s[u].y * inv_w, s[u].z * inv_w, s[u].w * inv_w);
+        reinterpret_cast<float4*>(out)[k] = r;
+        acc += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
+      }
+    }
+  }
+  return acc;
+}
+
 __global__ void __launch_bounds__(kThreads) fused_allreduce_adam_kernel(
     Ptrs P, int world, int rank, int64_t n_padded, float* __restrict__ m, float* __restrict__ v,
     uint32_t epoch, float lr, float b1, float b2, float eps, float wd, float bias1, float bias2, float max_norm,
@@ -99,20 +139,7 @@ __global__ void __launch_bounds__(kThreads) fused_allreduce_adam_kernel(
   // phase 1: reduce-scatter the owned shard, sum of squares
   float acc = 0.f;
   const float inv_w = 1.f / (float)world;
-  if (healthy) {
-    const int64_t nvec = shard / 4;
-    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nvec; k += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t i = lo + k * 4;
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int q = 0; q < world; ++q) {
-        const float4 x = *reinterpret_cast<const float4*>(P.grad[q] + i);
-        s.x += x.x; s.y += x.y; s.z += x.z; s.w += x.w;
-      }
-      s.x *= inv_w; s.y *= inv_w; s.z *= inv_w; s.w *= inv_w;
-      *reinterpret_cast<float4*>(P.grad[rank] + i) = s;
-      acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
-    }
-  }
+  if (healthy) acc = reduce_range(P, world, P.grad[rank] + lo, lo, shard / 4, inv_w);
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
@@ -176,6 +203,82 @@ __global__ void __launch_bounds__(kThreads) fused_allreduce_adam_kernel(
   grid.sync();
 }
 
+// One-shot variant for small buffers (latency bound): every rank reads every
+// peer's full gradient, reduces it into a local scratch buffer, computes the
+// global norm itself and applies Adam to the whole buffer, so parameters never
+// cross NVLink and there is no norm exchange. Two cross-rank barriers: the
+// gradients are ready, and every peer has finished reading ours.
+__global__ void __launch_bounds__(kThreads) oneshot_allreduce_adam_kernel(
+    Ptrs P, int world, int rank, int64_t n_padded, float* __restrict__ scratch, float* __restrict__ m,
+    float* __restrict__ v, uint32_t epoch, float lr, float b1, float b2, float eps, float wd, float bias1,
+    float bias2, float max_norm, float* __restrict__ norm_out, int* __restrict__ status, long long max_iters) {
+  cg::grid_group grid = cg::this_grid();
+  __shared__ float red[kThreads / 32];
+  __shared__ float scale_s;
+  __shared__ bool ok_s;
+  uint32_t* mypad = P.pad[rank];
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    bool ok = cross_rank_barrier(P, world, rank, kFlagReady, epoch, max_iters);
+    if (!ok) atomicExch(status, 1);
+  }
+  grid.sync();
+  const bool healthy = *(volatile int*)status == 0;
+  const float inv_w = 1.f / (float)world;
+  const int64_t nvec = n_padded / 4;
+  float acc = 0.f;
+  if (healthy) acc = reduce_range(P, world, scratch, 0, nvec, inv_w);
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w];
+    reinterpret_cast<float*>(mypad + kPartials)[blockIdx.x] = t;
+  }
+  grid.sync();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    float total = 0.f;
+    for (int c = 0; c < (int)gridDim.x; ++c) total += reinterpret_cast<float*>(mypad + kPartials)[c];
+    const float norm = sqrtf(total);
+    reinterpret_cast<float*>(mypad + kPartials)[kMaxCta] = max_norm > 0.f ? fminf(1.f, max_norm / (norm + 1e-6f)) : 1.f;
+    *norm_out = norm;
+  }
+  grid.sync();
+  ok_s = healthy;
+  scale_s = reinterpret_cast<volatile float*>(mypad + kPartials)[kMaxCta];
+  __syncthreads();
+  if (ok_s) {
+    const float scale = scale_s;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nvec; k += (int64_t)gridDim.x * blockDim.x) {
+      float4 g = reinterpret_cast<const float4*>(scratch)[k];
+      float4 p = *reinterpret_cast<const float4*>(P.param[rank] + 4 * k);
+      float4 mm = reinterpret_cast<const float4*>(m)[k];
+      float4 vv = reinterpret_cast<const float4*>(v)[k];
+      float* pg = &g.x;
+      float* pp = &p.x;
+      float* pm = &mm.x;
+      float* pv = &vv.x;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float gi = pg[c] * scale + wd * pp[c];
+        pm[c] = b1 * pm[c] + (1.f - b1) * gi;
+        pv[c] = b2 * pv[c] + (1.f - b2) * gi * gi;
+        pp[c] -= lr * (pm[c] / bias1) / (sqrtf(pv[c] / bias2) + eps);
+      }
+      reinterpret_cast<float4*>(m)[k] = mm;
+      reinterpret_cast<float4*>(v)[k] = vv;
+      *reinterpret_cast<float4*>(P.param[rank] + 4 * k) = p;
+    }
+  }
+  __threadfence_system();
+  grid.sync();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    bool ok = cross_rank_barrier(P, world, rank, kFlagDone, epoch, max_iters);
+    if (!ok) atomicCAS(status, 0, 4);
+  }
+  grid.sync();
+}
+
 struct Comm {
   int world = 1, rank = 0, device = 0;
   int64_t n = 0, n_padded = 0;
@@ -185,9 +288,12 @@ struct Comm {
   std::vector<void*> opened;
   uint32_t epoch = 0;
   int grid = 0;
+  bool oneshot = false;                 // small buffers: one-shot all-reduce, full local Adam
+  float* scratch = nullptr;             // one-shot reduced gradient (local)
   torch::Tensor status;                 // int32 [1]
 
   ~Comm() {
+    if (scratch) cudaFree(scratch);
     for (void* p : opened) cudaIpcCloseMemHandle(p);
     if (base) cudaFree(base);
   }
@@ -201,7 +307,7 @@ struct CommHandle {
 
 // Allocate the local region [grad n_padded][param n_padded][signal pad]; its
 // IPC handle is exchanged with the other ranks by `ipc_handle` / `open_peers`.
-CommHandle create(int64_t n, int world, int rank) {
+CommHandle create(int64_t n, int world, int rank, int64_t oneshot_bytes) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) throw std::runtime_error("bad world/rank");
   auto c = std::make_shared<Comm>();
   c->world = world;
@@ -218,6 +324,14 @@ CommHandle create(int64_t n, int world, int rank) {
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_allreduce_adam_kernel, kThreads, 0);
   c->grid = std::max(1, std::min(kMaxCta, sms * std::max(1, per_sm)));
+  c->oneshot = world > 1 && c->n_padded * 4 <= oneshot_bytes;
+  if (c->oneshot) {
+    if (cudaMalloc(&c->scratch, (size_t)c->n_padded * 4) != cudaSuccess)
+      throw std::runtime_error("cudaMalloc of the one-shot scratch failed");
+    int per_sm1 = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm1, oneshot_allreduce_adam_kernel, kThreads, 0);
+    c->grid = std::max(1, std::min(c->grid, sms * std::max(1, per_sm1)));
+  }
   c->status = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, c->device));
   return CommHandle{c};
 }
@@ -279,10 +393,17 @@ void step(CommHandle& h, torch::Tensor m, torch::Tensor v, torch::Tensor norm_ou
   int world = c.world, rank = c.rank;
   int64_t npad = c.n_padded;
   uint32_t epoch = c.epoch;
-  void* args[] = {&c.P, &world, &rank, &npad, &mp, &vp, &epoch, &lr_f, &b1_f, &b2_f, &eps_f, &wd_f,
-                  &bias1, &bias2, &mn, &np, &sp, &iters};
-  cudaError_t err = cudaLaunchCooperativeKernel((void*)fused_allreduce_adam_kernel, dim3(c.grid), dim3(kThreads),
-                                                args, 0, st);
+  cudaError_t err;
+  if (c.oneshot) {
+    float* sc = c.scratch;
+    void* args[] = {&c.P, &world, &rank, &npad, &sc, &mp, &vp, &epoch, &lr_f, &b1_f, &b2_f, &eps_f, &wd_f,
+                    &bias1, &bias2, &mn, &np, &sp, &iters};
+    err = cudaLaunchCooperativeKernel((void*)oneshot_allreduce_adam_kernel, dim3(c.grid), dim3(kThreads), args, 0, st);
+  } else {
+    void* args[] = {&c.P, &world, &rank, &npad, &mp, &vp, &epoch, &lr_f, &b1_f, &b2_f, &eps_f, &wd_f,
+                    &bias1, &bias2, &mn, &np, &sp, &iters};
+    err = cudaLaunchCooperativeKernel((void*)fused_allreduce_adam_kernel, dim3(c.grid), dim3(kThreads), args, 0, st);
+  }
   if (err != cudaSuccess) throw std::runtime_error(std::string("fused all-reduce launch: ") + cudaGetErrorString(err));
 }
 
@@ -293,8 +414,10 @@ void register_comm_ops(py::module& m) {
       .def_property_readonly("n_padded", [](const CommHandle& h) { return h.c->n_padded; })
       .def_property_readonly("grid", [](const CommHandle& h) { return h.c->grid; })
       .def_property_readonly("status", [](const CommHandle& h) { return h.c->status; })
-      .def_property_readonly("epoch", [](const CommHandle& h) { return h.c->epoch; });
-  m.def("peer_comm_create", &create, "allocate the IPC-exported gradient/parameter/signal region");
+      .def_property_readonly("epoch", [](const CommHandle& h) { return h.c->epoch; })
+      .def_property_readonly("oneshot", [](const CommHandle& h) { return h.c->oneshot; });
+  m.def("peer_comm_create", &create, "allocate the IPC-exported gradient/parameter/signal region",
+        py::arg("n"), py::arg("world"), py::arg("rank"), py::arg("oneshot_bytes") = 0);
   m.def("peer_comm_ipc_handle", &ipc_handle);
   m.def("peer_comm_open", &open_peers, "open every peer's region from the exchanged IPC handles");
   m.def("peer_comm_buffers", &local_buffers, "local [grad, param] views");

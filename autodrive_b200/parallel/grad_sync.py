@@ -20,8 +20,8 @@ class GradientSync:
         self.opt = optimizer
         self.world = world
         dev = optimizer.flat.flat.device
-        if backend == "auto":
-            backend = "nccl" if dev.type == "cuda" else "gloo"
+        if backend == "auto":  # the fused peer-memory kernel is the multi-GPU product path
+            backend = "p2p" if dev.type == "cuda" else "gloo"
         if world > 1 and backend == "p2p":
             from .p2p import FusedAllReduceAdam
             self.fused = FusedAllReduceAdam(optimizer)

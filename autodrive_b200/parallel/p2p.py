@@ -8,8 +8,12 @@ for the global clip, applies Adam to the owned shard and all-gathers the new
 parameters with peer stores. Waits on peers are bounded: a rank that stops
 participating makes the others raise `PeerCommError` instead of hanging.
 
-Optimizer moments are kept for the owned shard only (ZeRO-1 layout), so an
-optimizer state saved from one rank covers that rank's shard.
+Two modes, chosen by buffer size: buffers up to ``oneshot_bytes`` (4 MB) use a
+one-shot kernel (each rank reads every peer's whole gradient, reduces it,
+takes the global norm locally and applies Adam to the whole buffer: two
+cross-rank barriers, no parameter traffic); larger ones use the two-shot
+reduce-scatter / sharded Adam / parameter all-gather kernel, whose optimizer
+moments are meaningful for the owned shard only (ZeRO-1 layout).
 """
 from __future__ import annotations
 
@@ -24,8 +28,12 @@ class PeerCommError(RuntimeError):
     pass
 
 
+ONESHOT_BYTES = 4 << 20  # buffers up to 4 MB: one-shot all-reduce (latency bound)
+
+
 class FusedAllReduceAdam:
-    def __init__(self, optimizer, max_wait_iters: int = 1 << 24, check_every: int = 1):
+    def __init__(self, optimizer, max_wait_iters: int = 1 << 24, check_every: int = 1,
+                 oneshot_bytes: int = ONESHOT_BYTES):
         self.ext = require_extension()
         self.opt = optimizer
         grouped = dist.is_available() and dist.is_initialized()
@@ -35,7 +43,8 @@ class FusedAllReduceAdam:
         if flat.flat.device.type != "cuda":
             raise RuntimeError("the peer-memory all-reduce needs CUDA ranks")
         n = flat.flat.numel()
-        self.comm = self.ext.peer_comm_create(n, self.world, self.rank)
+        self.comm = self.ext.peer_comm_create(n, self.world, self.rank, int(oneshot_bytes))
+        self.mode = "one-shot" if self.comm.oneshot else "two-shot"
         handle = self.ext.peer_comm_ipc_handle(self.comm)
         handles = [handle]
         if self.world > 1:
@@ -52,6 +61,8 @@ class FusedAllReduceAdam:
         self.max_wait_iters = int(max_wait_iters)
         self.check_every = max(1, int(check_every))
         self.steps = 0
+        self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._status_event = None
         torch.cuda.synchronize(param.device)
         pdist.barrier()
 
@@ -64,11 +75,23 @@ class FusedAllReduceAdam:
                                 self.max_wait_iters)
         self.steps += 1
         if self.steps % self.check_every == 0:
-            self.check()
+            self.check(block=False)
         return opt.last_norm
 
-    def check(self) -> None:
-        code = int(self.comm.status.item())
+    def check(self, block: bool = True) -> None:
+        """Raise PeerCommError if a step gave up waiting on a peer. Non-blocking
+        checks read the status copied after an earlier step (no host sync on
+        the hot path); a blocking check waits for the latest step."""
+        if block:
+            code = int(self.comm.status.item())
+        else:
+            code = 0
+            if self._status_event is not None and self._status_event.query():
+                code = int(self._status_host[0])
+            self._status_host.copy_(self.comm.status, non_blocking=True)
+            if self._status_event is None:
+                self._status_event = torch.cuda.Event()
+            self._status_event.record()
         if code:
             phase = {1: "gradients-ready", 2: "norm exchange", 4: "completion"}.get(code, str(code))
             raise PeerCommError(f"peer all-reduce wait expired in the {phase} barrier on rank {self.rank}")

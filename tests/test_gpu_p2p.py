@@ -57,7 +57,7 @@ def model():
 a, b = model(), model()
 oa = FusedAdam(a, lr=1e-2, max_grad_norm=.5)
 ob = FusedAdam(b, lr=1e-2, max_grad_norm=.5)
-peer = FusedAllReduceAdam(ob)
+peer = FusedAllReduceAdam(ob, oneshot_bytes=int(os.environ["AD_ONESHOT_BYTES"]))
 torch.manual_seed(100 + rank)
 for _ in range(3):
     x = torch.randn(128, 37, device="cuda")
@@ -66,7 +66,8 @@ for _ in range(3):
     ob.zero_grad(); b(x).square().sum().backward(); peer.step()
 torch.cuda.synchronize()
 diff = max(float((pa - pb).abs().max()) for pa, pb in zip(a.parameters(), b.parameters()))
-print(json.dumps({{"rank": rank, "diff": diff, "norm_a": float(oa.last_norm), "norm_b": float(ob.last_norm)}}))
+print(json.dumps({{"rank": rank, "diff": diff, "norm_a": float(oa.last_norm), "norm_b": float(ob.last_norm),
+                  "mode": peer.mode}}))
 pdist.teardown(state)
 """
 
@@ -78,12 +79,13 @@ def _free_port():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_match_nccl_average(tmp_path):
+@pytest.mark.parametrize("oneshot_bytes,mode", [(0, "two-shot"), (1 << 22, "one-shot")])
+def test_two_ranks_match_nccl_average(tmp_path, oneshot_bytes, mode):
     script = tmp_path / "worker.py"
     script.write_text(WORKER.format(root=ROOT))
     world = min(torch.cuda.device_count(), 8)
     env = {**os.environ, "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_free_port()), "WORLD_SIZE": str(world),
-           "NCCL_NVLS_ENABLE": "0"}
+           "NCCL_NVLS_ENABLE": "0", "AD_ONESHOT_BYTES": str(oneshot_bytes)}
     procs = [subprocess.Popen([sys.executable, str(script)], stdout=subprocess.PIPE, stderr=subprocess.PIPE,
                               text=True, env={**env, "RANK": str(r), "LOCAL_RANK": str(r)}) for r in range(world)]
     outs = [p.communicate(timeout=300) for p in procs]
@@ -91,5 +93,6 @@ def test_two_ranks_match_nccl_average(tmp_path):
         assert p.returncode == 0, se[-3000:]
     for so, _ in outs:
         row = json.loads(so.strip().splitlines()[-1])
+        assert row["mode"] == mode
         assert row["diff"] < 1e-5, row
         assert abs(row["norm_a"] - row["norm_b"]) < 1e-4 * max(1., row["norm_a"]), row
