@@ -45,7 +45,10 @@ constexpr int kPadWords = 1024;         // per-rank signal pad (uint32 words)
 // pad layout (uint32 words): [0,8) ready flags, [8,16) norm flags, [16,24) done
 // flags, [32,48) shard sums of squares as float bits (indexed by rank),
 // [64, 64 + kMaxCta] per-CTA partials and the clip scale (local use only)
-constexpr int kFlagReady = 0, kFlagNorm = 8, kFlagDone = 16, kNorms = 32, kPartials = 64;
+constexpr int kFlagReady = 0, kFlagNorm = 8, kFlagDone = 16, kFlagStats = 24, kNorms = 32, kFlagBcast = 48,
+              kPartials = 64;
+// stats exchange: two parity areas of kMaxRanks x kMaxStats doubles at word 512 and 768
+constexpr int kStatsArea = 512, kMaxStats = 16;
 constexpr int kMaxCta = 296;              // 2 CTAs per SM on a 148-SM part
 constexpr int kUnroll = 4;                // independent 16-byte loads in flight per thread and peer
 
@@ -279,6 +282,74 @@ __global__ void __launch_bounds__(kThreads) oneshot_allreduce_adam_kernel(
   grid.sync();
 }
 
+// Stats all-reduce over peer memory: `nsum` values are summed and `nmax`
+// values max-reduced across ranks in one single-CTA launch (one cross-rank
+// barrier). Values travel as doubles through the peers' signal pads; the
+// epoch's parity selects one of two areas so a peer one call behind never
+// sees its inputs overwritten.
+__global__ void peer_stats_kernel(Ptrs P, int world, int rank, const double* __restrict__ in,
+                                  double* __restrict__ out, int nsum, int nmax, uint32_t epoch,
+                                  int* __restrict__ status, long long max_iters) {
+  const int nv = nsum + nmax;
+  const int area = kStatsArea + (int)(epoch & 1u) * (kMaxRanks * kMaxStats * 2);
+  if ((int)threadIdx.x < nv) {
+    const double x = in[threadIdx.x];
+    for (int q = 0; q < world; ++q)
+      reinterpret_cast<double*>(P.pad[q] + area)[rank * kMaxStats + threadIdx.x] = x;
+  }
+  __syncthreads();
+  __shared__ bool ok;
+  if (threadIdx.x == 0) {
+    ok = cross_rank_barrier(P, world, rank, kFlagStats, epoch, max_iters);
+    if (!ok) atomicCAS(status, 0, 8);
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < nv && ok) {
+    const volatile double* mine = reinterpret_cast<const volatile double*>(P.pad[rank] + area);
+    double acc = mine[threadIdx.x];
+    for (int q = 1; q < world; ++q) {
+      const double y = mine[q * kMaxStats + threadIdx.x];
+      acc = (int)threadIdx.x < nsum ? acc + y : fmax(acc, y);
+    }
+    out[threadIdx.x] = acc;
+  }
+}
+
+// Broadcast of rank `root`'s parameter buffer into every peer's parameter
+// buffer with peer stores (cooperative): the root's CTAs copy, then it
+// releases a flag in every pad; the other ranks wait for it.
+__global__ void __launch_bounds__(kThreads) peer_broadcast_kernel(Ptrs P, int world, int rank, int root,
+                                                                  int64_t n_padded, uint32_t epoch,
+                                                                  int* __restrict__ status, long long max_iters) {
+  cg::grid_group grid = cg::this_grid();
+  if (rank == root) {
+    const int64_t nvec = n_padded / 4;
+    const float4* src = reinterpret_cast<const float4*>(P.param[root]);
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nvec; k += (int64_t)gridDim.x * blockDim.x) {
+      const float4 x = src[k];
+      for (int q = 0; q < world; ++q)
+        if (q != root) reinterpret_cast<float4*>(P.param[q])[k] = x;
+    }
+    __threadfence_system();
+  }
+  grid.sync();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (rank == root) {
+      for (int q = 0; q < world; ++q) st_release_sys(P.pad[q] + kFlagBcast + root, epoch);
+    } else {
+      long long it = 0;
+      while (ld_acquire_sys(P.pad[rank] + kFlagBcast + root) != epoch) {
+        if (++it > max_iters) {
+          atomicCAS(status, 0, 16);
+          break;
+        }
+        __nanosleep(128);
+      }
+    }
+  }
+  grid.sync();
+}
+
 struct Comm {
   int world = 1, rank = 0, device = 0;
   int64_t n = 0, n_padded = 0;
@@ -286,7 +357,7 @@ struct Comm {
   size_t bytes = 0;
   Ptrs P{};
   std::vector<void*> opened;
-  uint32_t epoch = 0;
+  uint32_t epoch = 0, stats_epoch = 0, bcast_epoch = 0;
   int grid = 0;
   bool oneshot = false;                 // small buffers: one-shot all-reduce, full local Adam
   float* scratch = nullptr;             // one-shot reduced gradient (local)
@@ -407,6 +478,45 @@ void step(CommHandle& h, torch::Tensor m, torch::Tensor v, torch::Tensor norm_ou
   if (err != cudaSuccess) throw std::runtime_error(std::string("fused all-reduce launch: ") + cudaGetErrorString(err));
 }
 
+// In-place: sums[0..nsum) summed, maxes[0..nmax) max-reduced across ranks.
+void stats_allreduce(CommHandle& h, torch::Tensor sums, c10::optional<torch::Tensor> maxes, int64_t max_iters) {
+  Comm& c = *h.c;
+  TORCH_CHECK(sums.is_cuda() && sums.scalar_type() == torch::kFloat64 && sums.is_contiguous(), "sums: CUDA float64");
+  const int nsum = (int)sums.numel();
+  int nmax = 0;
+  if (maxes && maxes->defined()) {
+    TORCH_CHECK(maxes->is_cuda() && maxes->scalar_type() == torch::kFloat64 && maxes->is_contiguous(),
+                "maxes: CUDA float64");
+    nmax = (int)maxes->numel();
+  }
+  TORCH_CHECK(nsum + nmax <= kMaxStats, "at most 16 values per stats all-reduce");
+  auto in = nmax ? torch::cat({sums, *maxes}) : sums.clone();
+  auto out = torch::empty_like(in);
+  c.stats_epoch += 1;
+  auto st = c10::cuda::getCurrentCUDAStream().stream();
+  peer_stats_kernel<<<1, 32, 0, st>>>(c.P, c.world, c.rank, in.data_ptr<double>(), out.data_ptr<double>(), nsum,
+                                       nmax, c.stats_epoch, c.status.data_ptr<int>(), (long long)max_iters);
+  TORCH_CHECK(cudaGetLastError() == cudaSuccess, "peer_stats_kernel launch failed");
+  sums.copy_(out.narrow(0, 0, nsum));
+  if (nmax) maxes->copy_(out.narrow(0, nsum, nmax));
+}
+
+void broadcast_params(CommHandle& h, int64_t root, int64_t max_iters) {
+  Comm& c = *h.c;
+  TORCH_CHECK(root >= 0 && root < c.world, "root out of range");
+  c.bcast_epoch += 1;
+  int world = c.world, rank = c.rank, r = (int)root;
+  int64_t npad = c.n_padded;
+  uint32_t epoch = c.bcast_epoch;
+  int* sp = c.status.data_ptr<int>();
+  long long iters = (long long)max_iters;
+  void* args[] = {&c.P, &world, &rank, &r, &npad, &epoch, &sp, &iters};
+  auto st = c10::cuda::getCurrentCUDAStream().stream();
+  cudaError_t err = cudaLaunchCooperativeKernel((void*)peer_broadcast_kernel, dim3(std::min(c.grid, 148)),
+                                                dim3(kThreads), args, 0, st);
+  if (err != cudaSuccess) throw std::runtime_error(std::string("peer broadcast launch: ") + cudaGetErrorString(err));
+}
+
 }  // namespace
 
 void register_comm_ops(py::module& m) {
@@ -421,5 +531,9 @@ void register_comm_ops(py::module& m) {
   m.def("peer_comm_ipc_handle", &ipc_handle);
   m.def("peer_comm_open", &open_peers, "open every peer's region from the exchanged IPC handles");
   m.def("peer_comm_buffers", &local_buffers, "local [grad, param] views");
+  m.def("peer_stats_allreduce", &stats_allreduce, "sum / max all-reduce of up to 16 float64 values over peer memory",
+        py::arg("comm"), py::arg("sums"), py::arg("maxes") = py::none(), py::arg("max_iters") = 1 << 24);
+  m.def("peer_broadcast_params", &broadcast_params, "broadcast the root rank's flat parameters with peer stores",
+        py::arg("comm"), py::arg("root") = 0, py::arg("max_iters") = 1 << 24);
   m.def("peer_comm_step", &step, "fused all-reduce + clip + Adam over peer memory (cooperative launch)");
 }

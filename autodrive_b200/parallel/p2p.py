@@ -78,6 +78,15 @@ class FusedAllReduceAdam:
             self.check(block=False)
         return opt.last_norm
 
+    def stats_allreduce(self, sums: torch.Tensor, maxes: torch.Tensor | None = None) -> None:
+        """In-place cross-rank sum of `sums` and max of `maxes` (float64, <= 16
+        values in total) in one small peer-memory kernel."""
+        self.ext.peer_stats_allreduce(self.comm, sums, maxes, self.max_wait_iters)
+
+    def broadcast_parameters(self, root: int = 0) -> None:
+        """Copy rank `root`'s parameters into every rank's parameters (peer stores)."""
+        self.ext.peer_broadcast_params(self.comm, int(root), self.max_wait_iters)
+
     def check(self, block: bool = True) -> None:
         """Raise PeerCommError if a step gave up waiting on a peer. Non-blocking
         checks read the status copied after an earlier step (no host sync on
@@ -93,5 +102,6 @@ class FusedAllReduceAdam:
                 self._status_event = torch.cuda.Event()
             self._status_event.record()
         if code:
-            phase = {1: "gradients-ready", 2: "norm exchange", 4: "completion"}.get(code, str(code))
+            phase = {1: "gradients-ready", 2: "norm exchange", 4: "completion", 8: "stats exchange",
+                     16: "parameter broadcast"}.get(code, str(code))
             raise PeerCommError(f"peer all-reduce wait expired in the {phase} barrier on rank {self.rank}")

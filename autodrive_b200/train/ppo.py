@@ -206,7 +206,10 @@ class PPOLearner:
             ent = torch.full((1,), float(entropy_coef), device=self.device)
         stats = self._loss_stats
         stats.zero_()
-        reduce = pdist.all_reduce_ if self.world > 1 else None
+        reduce = None
+        if self.world > 1:
+            fused = getattr(self.sync, "fused", None)
+            reduce = fused.stats_allreduce if fused is not None else pdist.all_reduce_
         samples, batches = 0, 0
         for _ in range(cfg.epochs):
             perm = torch.randperm(n, device=self.device)

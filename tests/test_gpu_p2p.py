@@ -66,8 +66,23 @@ for _ in range(3):
     ob.zero_grad(); b(x).square().sum().backward(); peer.step()
 torch.cuda.synchronize()
 diff = max(float((pa - pb).abs().max()) for pa, pb in zip(a.parameters(), b.parameters()))
+sums = torch.tensor([rank + 1., 2. * (rank + 1)], dtype=torch.float64, device="cuda")
+maxes = torch.tensor([float(rank), -float(rank)], dtype=torch.float64, device="cuda")
+for _ in range(3):
+    s2, m2 = sums.clone(), maxes.clone()
+    peer.stats_allreduce(s2, m2)
+tri = world * (world + 1) / 2
+stats_ok = bool(torch.allclose(s2.cpu(), torch.tensor([tri, 2 * tri], dtype=torch.float64))
+                and m2[0].item() == world - 1 and m2[1].item() == 0.)
+if rank == 0:
+    for p in b.parameters():
+        p.data.fill_(.25)
+peer.broadcast_parameters(0)
+torch.cuda.synchronize()
+bcast_ok = all(bool((p == .25).all()) for p in b.parameters())
+peer.check()
 print(json.dumps({{"rank": rank, "diff": diff, "norm_a": float(oa.last_norm), "norm_b": float(ob.last_norm),
-                  "mode": peer.mode}}))
+                  "mode": peer.mode, "stats_ok": stats_ok, "bcast_ok": bcast_ok}}))
 pdist.teardown(state)
 """
 
@@ -95,4 +110,5 @@ def test_two_ranks_match_nccl_average(tmp_path, oneshot_bytes, mode):
         row = json.loads(so.strip().splitlines()[-1])
         assert row["mode"] == mode
         assert row["diff"] < 1e-5, row
+        assert row["stats_ok"] and row["bcast_ok"], row
         assert abs(row["norm_a"] - row["norm_b"]) < 1e-4 * max(1., row["norm_a"]), row
