@@ -415,4 +415,7 @@ def checkpoint_payload(model, agents, architecture, network, action_kind, optimi
                "drivetrain_config": agents.drivetrain_config, "network": network}
     if optimizer is not None:
         payload["optimizer_state_dict"] = optimizer.state_dict()
+    # provenance: SHA-256 tree digest of the weights, computed where they live
+    from ..utils.provenance import state_dict_digest
+    payload["weights_sha256"] = state_dict_digest(payload["model_state_dict"])
     return payload
