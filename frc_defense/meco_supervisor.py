@@ -1,0 +1,2 @@
+"""Compatibility import path: ``frc_defense.meco_supervisor`` -> ``autodrive_b200.meco.ops``."""
+from autodrive_b200.meco.ops import *  # noqa: F401,F403
