@@ -182,6 +182,7 @@ void register_policy_tc_ops(py::module& m);
 void register_tc_gemm_ops(py::module& m);
 void register_adstar_cpu(py::module& m);
 void register_sha256_ops(py::module& m);
+void register_plan_a_ops(py::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "B200-native FRC REBUILT simulator kernels";
@@ -211,4 +212,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_tc_gemm_ops(m);
   register_adstar_cpu(m);
   register_sha256_ops(m);
+  register_plan_a_ops(m);
 }
