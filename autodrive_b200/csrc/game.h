@@ -286,7 +286,133 @@ AD_HD void attacker_objective(G& g, int r, const int32_t* possession, float& gx,
 // Control: strategic action -> navigation target (one thread per robot).
 // `actions` holds the policy's categorical action for nn-mode robots.
 // ---------------------------------------------------------------------------
-AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* possession) {
+// Track-scan results consumed by control_robot, produced by the two scans
+// below (one warp per robot on the GPU, lane-strided over the track slots;
+// one lane on the host).
+struct ControlScan {
+  float top_c[kMaxRobots][4];
+  int top_i[kMaxRobots][4];
+  uint8_t intake[kMaxRobots], alliance[kMaxRobots], nearby[kMaxRobots];
+  float yield[kMaxRobots][4];
+};
+
+// Intake reference point (front-right intake corner plus a short momentum
+// lead) and the mid-field detour limit shared by the scans and the controller.
+AD_HD void intake_reference(G& g, int r, int poss, float& rrx, float& rry, float& detour_limit) {
+  const SimParams& sp = g.sp;
+  const float* p = g.ppose(r);
+  const float* v = g.rvel(r);
+  const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
+  const float c = cosf(p[2]), s = sinf(p[2]);
+  const float irx = p[0] + c * (L * .5f + .15f) + s * (W * .5f);
+  const float iry = p[1] + s * (L * .5f + .15f) - c * (W * .5f);
+  const float horizon = fminf(sp.replan_interval * sp.dt * .5f, .2f);
+  const float mx = v[0] * horizon, my = v[1] * horizon;
+  const float md = sqrtf(mx * mx + my * my);
+  const float mscale = fminf(.5f / fmaxf(md, 1e-6f), 1.f);
+  rrx = irx + mx * mscale;
+  rry = iry + my * mscale;
+  const int cap = sp.capacity[r];
+  const float remaining = 1.f - (float)poss / (float)(cap > 0 ? cap : 1);
+  detour_limit = 2.f + 1.5f * clampf(remaining, 0.f, 1.f);
+}
+
+// Rank the live, legal FUEL tracks of robot r: top-4 by (cost, index) plus the
+// intake / alliance / nearby-midfield flags. Lanes scan strided slots and the
+// top-4 lists merge through a butterfly; (cost, index) is a total order, so the
+// result equals the serial scan's.
+AD_HD void control_scan_tracks(G& g, int r, const int32_t* possession, ControlScan& cs, int lane, int nlanes) {
+  World& w = g.w;
+  const SimParams& sp = g.sp;
+  const int team = sp.team[r];
+  const bool det_offense = sp.mode[r] == MODE_DET && sp.role[r] == 0;
+  const bool hub_on = g.hub_active(team);
+  const float* p = g.ppose(r);
+  float rrx, rry, detour_limit;
+  intake_reference(g, r, possession[r], rrx, rry, detour_limit);
+  Top4 top;
+  top.init();
+  bool intake = false, alliance = false, nearby = false;
+  for (int i = lane; i < sp.P; i += nlanes) {
+    size_t k = g.erp(r, i);
+    if (!w.t_mask[k] || !(w.t_age[k] <= sp.track_timeout)) continue;
+    const float x = g.tx(r, i), y = g.ty(r, i);
+    const bool in_all = in_alliance_zone(sp, team, x);
+    if (det_offense && !hub_on && in_all) continue;
+    intake = true;
+    if (in_all) alliance = true;
+    if (!in_all && sqrtf(sqr(x - p[0]) + sqr(y - p[1])) <= detour_limit) nearby = true;
+    const float cost = sqrtf(sqr(x - rrx) + sqr(y - rry)) + fminf(fmaxf(w.t_age[k], 0.f), 2.f) * .4f;
+    top.push(cost, i);
+  }
+#if defined(__CUDA_ARCH__)
+  if (nlanes > 1) {
+    for (int o = 16; o > 0; o >>= 1) {
+      float oc[4];
+      int oi[4];
+      for (int k = 0; k < 4; ++k) {
+        oc[k] = __shfl_xor_sync(0xffffffffu, top.c[k], o);
+        oi[k] = __shfl_xor_sync(0xffffffffu, top.i[k], o);
+      }
+      for (int k = 0; k < 4; ++k)
+        if (oc[k] < kInf) top.push(oc[k], oi[k]);
+    }
+    intake = __any_sync(0xffffffffu, intake);
+    alliance = __any_sync(0xffffffffu, alliance);
+    nearby = __any_sync(0xffffffffu, nearby);
+  }
+#endif
+  if (lane == 0) {
+    for (int k = 0; k < 4; ++k) {
+      cs.top_c[r][k] = top.c[k];
+      cs.top_i[r][k] = top.i[k];
+    }
+    cs.intake[r] = intake;
+    cs.alliance[r] = alliance;
+    cs.nearby[r] = nearby;
+  }
+}
+
+// Expected FUEL yield around each candidate (confidence x freshness of the
+// live tracks within two robot radii), needed only by the scripted offense
+// while its HUB is active.
+AD_HD void control_scan_yields(G& g, int r, const ControlScan& cs_in, ControlScan& cs, int lane, int nlanes) {
+  World& w = g.w;
+  const SimParams& sp = g.sp;
+  const int team = sp.team[r];
+  const bool det_offense = sp.mode[r] == MODE_DET && sp.role[r] == 0;
+  float y[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool needed = det_offense && g.hub_active(team) && cs_in.intake[r];
+  if (needed) {
+    const float rad = robot_radius_of(g.param(r, RP_LENGTH), g.param(r, RP_WIDTH));
+    float cx[4], cy[4];
+    bool cv[4];
+    for (int k = 0; k < 4; ++k) {
+      cv[k] = cs_in.top_c[r][k] < kInf;
+      cx[k] = cv[k] ? g.tx(r, cs_in.top_i[r][k]) : 0.f;
+      cy[k] = cv[k] ? g.ty(r, cs_in.top_i[r][k]) : 0.f;
+    }
+    for (int j = lane; j < sp.P; j += nlanes) {
+      size_t kj = g.erp(r, j);
+      if (!w.t_mask[kj] || !(w.t_age[kj] <= sp.track_timeout)) continue;
+      const float ax = g.tx(r, j), ay = g.ty(r, j);
+      const float contrib = clampf(w.t_conf[kj], 0.f, 1.f) *
+                            expf(-fmaxf(w.t_age[kj], 0.f) / fmaxf(sp.track_timeout, 1e-6f));
+      for (int k = 0; k < 4; ++k)
+        if (cv[k] && sqrtf(sqr(ax - cx[k]) + sqr(ay - cy[k])) <= 2.f * rad) y[k] += contrib;
+    }
+#if defined(__CUDA_ARCH__)
+    if (nlanes > 1)
+      for (int k = 0; k < 4; ++k)
+        for (int o = 16; o > 0; o >>= 1) y[k] += __shfl_xor_sync(0xffffffffu, y[k], o);
+#endif
+  }
+  if (lane == 0)
+    for (int k = 0; k < 4; ++k) cs.yield[r][k] = y[k];
+}
+
+AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* possession,
+                         const ControlScan& cs) {
   World& w = g.w;
   const SimParams& sp = g.sp;
   const int e = g.e;
@@ -308,29 +434,13 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
   // intake reference (front-right corner of the intake) plus momentum
   float irx = p[0] + c * (L * .5f + .15f) + s * (W * .5f);
   float iry = p[1] + s * (L * .5f + .15f) - c * (W * .5f);
-  float horizon = fminf(sp.replan_interval * sp.dt * .5f, .2f);
-  float mx = v[0] * horizon, my = v[1] * horizon;
-  float md = sqrtf(mx * mx + my * my);
-  float mscale = fminf(.5f / fmaxf(md, 1e-6f), 1.f);
-  float rrx = irx + mx * mscale, rry = iry + my * mscale;
-  // rank live, legal FUEL tracks
+  // ranked FUEL tracks (control_scan_tracks)
   Top4 top;
-  top.init();
-  bool intake_available = false, alliance_fuel = false, nearby_mid = false;
-  float remaining = 1.f - (float)poss / (float)(cap > 0 ? cap : 1);
-  float detour_limit = 2.f + 1.5f * clampf(remaining, 0.f, 1.f);
-  for (int i = 0; i < sp.P; ++i) {
-    size_t k = g.erp(r, i);
-    if (!w.t_mask[k] || !(w.t_age[k] <= sp.track_timeout)) continue;
-    float x = g.tx(r, i), y = g.ty(r, i);
-    bool in_all = in_alliance_zone(sp, team, x);
-    if (det_offense && !hub_on && in_all) continue;
-    intake_available = true;
-    if (in_all) alliance_fuel = true;
-    if (!in_all && sqrtf(sqr(x - p[0]) + sqr(y - p[1])) <= detour_limit) nearby_mid = true;
-    float cost = sqrtf(sqr(x - rrx) + sqr(y - rry)) + fminf(fmaxf(w.t_age[k], 0.f), 2.f) * .4f;
-    top.push(cost, i);
+  for (int k = 0; k < 4; ++k) {
+    top.c[k] = cs.top_c[r][k];
+    top.i[k] = cs.top_i[r][k];
   }
+  const bool intake_available = cs.intake[r], alliance_fuel = cs.alliance[r], nearby_mid = cs.nearby[r];
   bool cand_valid[4];
   for (int k = 0; k < 4; ++k) {
     cand_valid[k] = top.c[k] < kInf;
@@ -419,16 +529,7 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
       if (!hub_on) {
         cost = top.c[k];
       } else {
-        float yield = 0.f;
-        for (int j = 0; j < sp.P; ++j) {
-          size_t kj = g.erp(r, j);
-          if (!w.t_mask[kj] || !(w.t_age[kj] <= sp.track_timeout)) continue;
-          float ax = g.tx(r, j), ay = g.ty(r, j);
-          if (sqrtf(sqr(ax - tx) + sqr(ay - ty)) > 2.f * rad) continue;
-          yield += clampf(w.t_conf[kj], 0.f, 1.f) *
-                   expf(-fmaxf(w.t_age[kj], 0.f) / fmaxf(sp.track_timeout, 1e-6f));
-        }
-        yield = fminf(yield, (float)(cap - poss > 0 ? cap - poss : 0));
+        float yield = fminf(cs.yield[r][k], (float)(cap - poss > 0 ? cap - poss : 0));
         float dx = tx - irx, dy = ty - iry;
         float dist = sqrtf(dx * dx + dy * dy);
         float ux = dx / fmaxf(dist, 1e-6f), uy = dy / fmaxf(dist, 1e-6f);

@@ -45,11 +45,29 @@ AD_HD void count_possession(const World& w, const SimParams& sp, int e, int32_t*
 #endif
 }
 
-AD_HD void control_env(World& w, const SimParams& sp, int e, const int32_t* actions, int32_t* poss) {
+AD_HD void control_env(World& w, const SimParams& sp, int e, const int32_t* actions, int32_t* poss,
+                        ControlScan& cs) {
   count_possession(w, sp, e, poss);
   G g{w, sp, e};
+#if defined(__CUDA_ARCH__)
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int r = warp; r < sp.R; r += nw)
+      if (sp.mode[r] != MODE_NONE) control_scan_tracks(g, r, poss, cs, lane, 32);
+    __syncthreads();
+    for (int r = warp; r < sp.R; r += nw)
+      if (sp.mode[r] != MODE_NONE) control_scan_yields(g, r, cs, cs, lane, 32);
+    __syncthreads();
+  }
+#else
+  for (int r = 0; r < sp.R; ++r)
+    if (sp.mode[r] != MODE_NONE) {
+      control_scan_tracks(g, r, poss, cs, 0, 1);
+      control_scan_yields(g, r, cs, cs, 0, 1);
+    }
+#endif
   PAR_FOR(r, sp.R) {
-    if (sp.mode[r] != MODE_NONE) control_robot(g, r, actions, poss);
+    if (sp.mode[r] != MODE_NONE) control_robot(g, r, actions, poss, cs);
   }
   BARRIER();
   SERIAL_BEGIN
@@ -250,7 +268,8 @@ __global__ void control_kernel(World w, SimParams sp, const int32_t* __restrict_
   const int e = blockIdx.x;
   if (e >= sp.n || !w.active[e]) return;
   __shared__ int32_t poss[kMaxRobots];
-  control_env(w, sp, e, actions, poss);
+  __shared__ ControlScan cs;
+  control_env(w, sp, e, actions, poss, cs);
 }
 
 __global__ void observe_kernel(World w, SimParams sp) {
@@ -445,7 +464,8 @@ void host_control(World w, const SimParams& sp, const int32_t* actions) {
     for (int e = b; e < end; ++e) {
       if (!w.active[e]) continue;
       int32_t poss[kMaxRobots];
-      control_env(w, sp, e, actions, poss);
+      ControlScan cs;
+      control_env(w, sp, e, actions, poss, cs);
     }
   });
 }
