@@ -84,10 +84,11 @@ def stages(args):
         # robot_* and the join wait of warp 0 are on warp 0's timeline; fuel_integrate..fuel_apply and
         # their join wait on the FUEL warps' timeline (concurrent); the rest on the whole CTA's
         names = ("robot_swerve", "robot_sweep", "robot_contacts", "robot_tail", "fuel_integrate_clear",
-                 "fuel_grid", "fuel_pairs", "fuel_apply", "fuel_chassis", "fuel_static", "pre_substeps",
-                 "post_substeps", "robot_warp_join_wait", "fuel_warps_join_wait")
+                 "fuel_scatter", "fuel_pairs", "fuel_apply", "fuel_chassis_reduce", "fuel_static",
+                 "pre_substeps", "post_substeps", "robot_warp_join_wait", "fuel_warps_join_wait",
+                 "fuel_count", "fuel_scan", "fuel_chassis_loop", "unused")
         robot_line = sum(cyc[k] for k in (0, 1, 2, 3, 12))
-        crit = max(1, robot_line + sum(cyc[k] for k in (8, 9, 10, 11)))
+        crit = max(1, robot_line + sum(cyc[k] for k in (8, 9, 10, 11, 16)))
         phases = {n: round(c / crit, 4) for n, c in zip(names, cyc)}
     awake = (env.ws["f_active"].bool() & (env.ws["f_sleep"] == 0)).float().sum(-1).mean().item()
     print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,

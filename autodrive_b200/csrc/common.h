@@ -11,6 +11,7 @@
 
 #include <cstdint>
 #include <cmath>
+#include <cstring>
 
 #if defined(__CUDACC__)
 #define AD_HD __host__ __device__ __forceinline__
@@ -105,6 +106,15 @@ AD_HD float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi)
 AD_HD float sgnf(float v) { return v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f); }
 AD_HD float sqr(float v) { return v * v; }
 AD_HD int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+AD_HD uint32_t float_bits(float v) {
+#if defined(__CUDA_ARCH__)
+  return __float_as_uint(v);
+#else
+  uint32_t u;
+  std::memcpy(&u, &v, sizeof(u));
+  return u;
+#endif
+}
 
 // Wrap an angle to [-pi, pi) with the floor-remainder convention used by the
 // simulator everywhere a heading is wrapped: remainder(a + pi, 2 pi) - pi.

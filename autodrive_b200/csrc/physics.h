@@ -69,7 +69,7 @@ struct TickShared {
   alignas(16) int32_t cell_start[kMaxGridCells + 4];
   alignas(16) uint32_t awake_bits[kMaxGridCells / 32 + 4];  // grid cells holding an awake sphere
   float rtrig[kMaxRobots * 4];                  // per robot: cos, sin, contact reach^2, unused
-  float red[kRedSlots * 20];
+  alignas(16) float red[kRedSlots * 20];
   float red_out[20];
   float scal[8];
   // phase accounting (PHASE_MARK): [0] thread 0's timeline, [1] the FUEL warps' leader

@@ -119,34 +119,85 @@ AD_HD bool ferry_landing(const SimParams& sp, int team, float ox, float oy, floa
   return false;
 }
 
+// Scratch words in TickShared::red used by fuel_actions (no other user then).
+constexpr int kFaWords = (kMaxPieces + 31) / 32;       // one bit per piece
+constexpr int kFaElig = 0;                              // eligible-piece bitmap
+constexpr int kFaHeld = kFaElig + kFaWords;             // held-piece bitmap per robot
+constexpr int kFaPoss = kFaHeld + kMaxRobots * kFaWords;  // possession counts
+constexpr int kFaMin = (kFaPoss + kMaxRobots + 1) & ~1;   // packed (d^2, index) minimum, 8-byte aligned
+static_assert(kFaMin + 2 <= kRedSlots * 20, "fuel_actions scratch exceeds TickShared::red");
+
+AD_HD uint32_t* fa_words(TickShared& s) { return reinterpret_cast<uint32_t*>(s.red); }
+
+AD_HD void fa_set_bit(uint32_t* words, int i) {
+#if defined(__CUDA_ARCH__)
+  atomicOr(&words[i >> 5], 1u << (i & 31));
+#else
+  words[i >> 5] |= 1u << (i & 31);
+#endif
+}
+
+// Index of the lowest set bit at or after `from` in a kFaWords bitmap, or -1.
+AD_HD int fa_next_bit(const uint32_t* words, int from, int n) {
+  for (int wi = from >> 5; wi < kFaWords && (wi << 5) < n; ++wi) {
+    uint32_t m = words[wi];
+    if (wi == (from >> 5)) m &= ~0u << (from & 31);
+    if (m) {
+#if defined(__CUDA_ARCH__)
+      const int b = (wi << 5) + __ffs(m) - 1;
+#else
+      const int b = (wi << 5) + __builtin_ctz(m);
+#endif
+      return b < n ? b : -1;
+    }
+  }
+  return -1;
+}
+
 // Pickup, carried-piece follow, ferry release and scoring for one tick
 // (frc_defense/gamepiece_actions.py:128-511). s.pos/vel/ang hold the FUEL state.
+// Robots act in slot order. Element scans run across the CTA; the per-robot decisions stay on
+// one thread in slot order, so the outcome equals the serial definition:
+// a sweeping robot takes the first `room` eligible pieces by index, a single
+// intake takes the nearest eligible piece (ties to the lower index), and
+// ferry / scoring act on a robot's lowest-index held piece.
 AD_HD void fuel_actions(G& g, TickShared& s, const Rng& rng, uint32_t tick) {
   World& w = g.w;
   const SimParams& sp = g.sp;
   const int e = g.e;
   const float el = g.elapsed();
   const size_t base = (size_t)e * sp.P;
+  uint32_t* fw = fa_words(s);
+  int32_t* possession = reinterpret_cast<int32_t*>(fw + kFaPoss);
+  unsigned long long* best_key = reinterpret_cast<unsigned long long*>(fw + kFaMin);
+  PAR_FOR(k, kFaPoss + kMaxRobots) { fw[k] = 0u; }
   SERIAL_BEGIN
-  int32_t possession[kMaxRobots];
   for (int r = 0; r < sp.R; ++r) {
-    possession[r] = 0;
     g.rcount(r, RC_ACQUIRED_EVENT) = 0;
     g.rcount(r, RC_SCORED_EVENT) = 0;
     g.rcount(r, RC_PASSED_EVENT) = 0;
     g.rcount(r, RC_DENIED_EVENT) = 0;
   }
-  for (int i = 0; i < sp.P; ++i) {
-    int o = w.f_owner[base + i];
-    if (o >= 0 && o < sp.R) possession[o]++;
+  SERIAL_END
+  BARRIER();
+  PAR_FOR(i, sp.P) {
+    const int o = w.f_owner[base + i];
+    if (o >= 0 && o < sp.R) {
+#if defined(__CUDA_ARCH__)
+      atomicAdd(&possession[o], 1);
+#else
+      possession[o]++;
+#endif
+    }
   }
+  BARRIER();
   // ---- pickup, robots in slot order
   for (int r = 0; r < sp.R; ++r) {
     if (sp.mode[r] == MODE_NONE) continue;
-    const float* rp = w.r_pose + g.er(r) * 3;
-    const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
     const bool extended = sp.kind[r] == 1 || g.latch(r, RL_INTAKE_COLLECTING);
     if (!extended) continue;
+    const float* rp = w.r_pose + g.er(r) * 3;
+    const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
     const bool det_offense = sp.mode[r] == MODE_DET && sp.role[r] == 0;
     const int team = sp.team[r];
     const bool hub_on = g.hub_active(team);
@@ -154,40 +205,65 @@ AD_HD void fuel_actions(G& g, TickShared& s, const Rng& rng, uint32_t tick) {
     const float fr = sp.fuel_radius_rules;
     const float lon_lo = L * .5f - .075f - fr, lon_hi = L * .5f + .35f + .3048f + fr;
     const float lat_hi = W * .5f + .075f + fr;
-    int room = sp.capacity[r] - possession[r];
-    bool can_single = el + 1e-6f >= g.rtime(r, RT_NEXT_INTAKE) && possession[r] < sp.capacity[r];
-    float best = kInf;
-    int best_i = -1;
-    int swept = 0;
-    for (int i = 0; i < sp.P; ++i) {
-      if (!w.f_active[base + i] || w.f_owner[base + i] >= 0) continue;
-      if (sp.fuel_physics && s.fpos[2][i] > .20f) continue;
-      float dx = s.fpos[0][i] - rp[0], dy = s.fpos[1][i] - rp[1];
-      if (det_offense && !hub_on && in_alliance_zone(sp, team, s.fpos[0][i])) continue;
-      float lon = dx * c + dy * sn, lat = fabsf(-dx * sn + dy * c);
-      if (lon < lon_lo || lon > lon_hi || lat > lat_hi) continue;
-      if (det_offense) {
-        if (swept < room) {
-          w.f_owner[base + i] = (int8_t)r;
-          swept++;
-        }
-      } else if (can_single) {
-        float d2 = dx * dx + dy * dy;
-        if (d2 < best) {
-          best = d2;
-          best_i = i;
+    const int room = sp.capacity[r] - possession[r];
+    const bool can_single = el + 1e-6f >= g.rtime(r, RT_NEXT_INTAKE) && possession[r] < sp.capacity[r];
+    if (!det_offense && !can_single) continue;
+    PAR_FOR(k, kFaWords) { fw[kFaElig + k] = 0u; }
+    SERIAL_BEGIN
+    *best_key = ~0ull;
+    SERIAL_END
+    BARRIER();
+    PAR_FOR(i, sp.P) {
+      if (w.f_active[base + i] && w.f_owner[base + i] < 0 && !(sp.fuel_physics && s.fpos[2][i] > .20f)) {
+        const float dx = s.fpos[0][i] - rp[0], dy = s.fpos[1][i] - rp[1];
+        const bool skip = det_offense && !hub_on && in_alliance_zone(sp, team, s.fpos[0][i]);
+        const float lon = dx * c + dy * sn, lat = fabsf(-dx * sn + dy * c);
+        if (!skip && lon >= lon_lo && lon <= lon_hi && lat <= lat_hi) {
+          if (det_offense) {
+            fa_set_bit(fw + kFaElig, i);
+          } else {
+            const float d2 = dx * dx + dy * dy;
+            // non-negative floats order like their bit patterns
+            const unsigned long long key = ((unsigned long long)float_bits(d2) << 32) | (unsigned)i;
+            if (d2 < kInf) {
+#if defined(__CUDA_ARCH__)
+              atomicMin(best_key, key);
+#else
+              if (key < *best_key) *best_key = key;
+#endif
+            }
+          }
         }
       }
     }
-    int picked = swept;
-    if (best_i >= 0) {
-      w.f_owner[base + best_i] = (int8_t)r;
+    BARRIER();
+    SERIAL_BEGIN
+    int picked = 0;
+    if (det_offense) {
+      for (int i = fa_next_bit(fw + kFaElig, 0, sp.P); i >= 0 && picked < room; i = fa_next_bit(fw + kFaElig, i + 1, sp.P)) {
+        w.f_owner[base + i] = (int8_t)r;
+        ++picked;
+      }
+    } else if (*best_key != ~0ull) {
+      const int i = (int)(*best_key & 0xffffffffull);
+      w.f_owner[base + i] = (int8_t)r;
       g.rtime(r, RT_NEXT_INTAKE) = el + .20f;
-      picked++;
+      picked = 1;
     }
     possession[r] += picked;
     g.rcount(r, RC_ACQUIRED_EVENT) = picked;
+    SERIAL_END
+    BARRIER();
   }
+  // held-piece bitmaps (lowest index = the piece a robot releases or scores first)
+  PAR_FOR(i, sp.P) {
+    const int o = w.f_owner[base + i];
+    if (w.f_active[base + i] && o >= 0 && o < sp.R) fa_set_bit(fw + kFaHeld + o * kFaWords, i);
+  }
+  BARRIER();
+  SERIAL_BEGIN
+  int next_held[kMaxRobots];
+  for (int r = 0; r < sp.R; ++r) next_held[r] = fa_next_bit(fw + kFaHeld + r * kFaWords, 0, sp.P);
   // ---- ferry release: first held piece of each robot facing home
   for (int r = 0; r < sp.R; ++r) {
     if (sp.mode[r] == MODE_NONE || w.g_action[g.er(r)] != 6 || possession[r] == 0) continue;
@@ -203,13 +279,9 @@ AD_HD void fuel_actions(G& g, TickShared& s, const Rng& rng, uint32_t tick) {
     bool facing = herr <= kPi / 4.f || !dumper;
     bool ready = el + 1e-6f >= g.rtime(r, RT_NEXT_FERRY);
     if (!((at_ferry || dumper) && facing && ready)) continue;
-    int first = -1;
-    for (int i = 0; i < sp.P; ++i)
-      if (w.f_active[base + i] && w.f_owner[base + i] == r) {
-        first = i;
-        break;
-      }
+    const int first = next_held[r];
     if (first < 0) continue;
+    next_held[r] = fa_next_bit(fw + kFaHeld + r * kFaWords, first + 1, sp.P);
     U4 u = rng.draw((uint32_t)e, tick, RNG_LAUNCH, (uint32_t)(r * 2));
     float lx, ly;
     bool net = ferry_landing(sp, team, rp[0], rp[1], u01(u.x), u01(u.y), lx, ly);
@@ -257,13 +329,9 @@ AD_HD void fuel_actions(G& g, TickShared& s, const Rng& rng, uint32_t tick) {
                      el + 1e-6f >= g.rtime(r, RT_NEXT_SCORE);
     g.latch(r, RL_LAST_HUB_ZONE) = ready ? 1 : 0;
     if (!can_score || !has_fuel) continue;
-    int first = -1;
-    for (int i = 0; i < sp.P; ++i)
-      if (w.f_active[base + i] && w.f_owner[base + i] == r) {
-        first = i;
-        break;
-      }
+    const int first = next_held[r];
     if (first < 0) continue;
+    next_held[r] = fa_next_bit(fw + kFaHeld + r * kFaWords, first + 1, sp.P);
     g.rcount(r, RC_SCORED_EVENT) = 1;
     w.g_scores[(size_t)e * 4 + 2 + team] += 1;
     if (el <= 20.f + sp.dt) w.g_scores[(size_t)e * 4 + team] += 1;
