@@ -47,12 +47,13 @@ def stages(args):
     for _ in range(args.warmup):
         env.step_held(random_actions() if args.actions == "random" else None, 20, use_graph=False)
     torch.cuda.synchronize()
-    totals = {"control": 0., "plan": 0., "tick": 0., "observe": 0.}
+    totals = {"control": 0., "plan": 0., "tick": 0., "sense": 0., "observe": 0.}
+    sim.sense_in_tick = False   # the sensor stage is timed on its own
     for t in range(args.ticks):
         if args.actions == "random" and t % 12 == 0:
             env._set_actions(random_actions())
         for name, fn in (("control", lambda: sim.control(env._actions_buf)), ("plan", lambda: sim.plan(0)),
-                         ("tick", lambda: sim.tick(0, 1))):
+                         ("tick", lambda: sim.tick(0, 1)), ("sense", lambda: sim.sense(0))):
             a, b = _events()
             a.record()
             fn()
@@ -78,6 +79,7 @@ def stages(args):
             sim.control(env._actions_buf)
             sim.plan(0)
             sim.tick(0, 1)
+            sim.sense(0)
         torch.cuda.synchronize()
         ext.phase_profile_enable(False)
         cyc = ext.phase_profile_read()
@@ -90,6 +92,7 @@ def stages(args):
         robot_line = sum(cyc[k] for k in (0, 1, 2, 3, 12))
         crit = max(1, robot_line + sum(cyc[k] for k in (8, 9, 10, 11, 16)))
         phases = {n: round(c / crit, 4) for n, c in zip(names, cyc)}
+    sim.sense_in_tick = True
     awake = (env.ws["f_active"].bool() & (env.ws["f_sleep"] == 0)).float().sum(-1).mean().item()
     print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,
                       "awake_fuel_per_world": awake, "phase_share": phases,

@@ -77,7 +77,7 @@ SimParams params_from_dict(const py::dict& d) {
   I(robot_height) I(max_comp) I(pair_damping) I(sleep) I(sleep_time) I(sleep_speed) I(sleep_ang)
   I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule)
   I(perception_interval) I(opponent_kind) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
-  I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(replan_interval)
+  I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(stereo_tracks) I(replan_interval)
   I(teammate_coordination) I(normalize_obs) I(horizon) I(max_speed_nominal) I(max_omega_nominal)
   I(plan_res) I(plan_nx) I(plan_ny) I(plan_sweeps) I(bump_cost) I(seed0) I(seed1)
 #undef I
@@ -109,6 +109,7 @@ struct Sim {
   std::vector<torch::Tensor> keep;
   bool cuda = false;
   int threads = 256;
+  bool sense_in_tick = true;  // run the stereo sensor stage right after each game tick
 
   Sim(std::vector<torch::Tensor> tensors, py::dict params) {
     sp = params_from_dict(params);
@@ -155,6 +156,14 @@ struct Sim {
   void tick(uint32_t t, int run_game) {
     if (cuda) launch_tick(w, sp, t, run_game, threads, stream());
     else host_tick(w, sp, t, run_game);
+    if (run_game && sense_in_tick) sense(0);
+  }
+  // Stereo-cluster FUEL perception (3v3); rows without a sensor update this
+  // tick return at once unless `force`.
+  void sense(int force) {
+    if (!sp.stereo_tracks) return;
+    if (cuda) launch_sense(w, sp, force, stream());
+    else host_sense(w, sp, force);
   }
   void physics(int ticks) {
     if (cuda) launch_physics(w, sp, ticks, threads, stream());
@@ -163,6 +172,7 @@ struct Sim {
   void perceive() {
     if (cuda) launch_perceive(w, sp, threads, stream());
     else host_perceive(w, sp);
+    sense(1);
   }
   void observe() {
     if (cuda) launch_observe(w, sp, stream());
@@ -195,6 +205,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "reduction, fuel static, pre-substep, post-substep, robot-warp join wait, fuel-warps join wait, "
         "fuel count, fuel scan, fuel chassis loop, unused");
   m.def("plan_smem_bytes", [](py::dict d) { return plan_smem_bytes(params_from_dict(d)); });
+  m.def("sense_smem_bytes", [](py::dict d) { return sense_smem_bytes(params_from_dict(d)); });
   py::class_<Sim>(m, "Sim")
       .def(py::init<std::vector<torch::Tensor>, py::dict>())
       .def("control", &Sim::control, py::arg("actions") = py::none())
@@ -203,6 +214,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("physics", &Sim::physics, py::arg("ticks"))
       .def("observe", &Sim::observe)
       .def("perceive", &Sim::perceive)
+      .def("sense", &Sim::sense, py::arg("force") = 0)
+      .def_readwrite("sense_in_tick", &Sim::sense_in_tick)
       .def("set_seed", &Sim::set_seed)
       .def_readwrite("threads", &Sim::threads)
       .def_property_readonly("cuda", [](const Sim& s) { return s.cuda; });

@@ -106,6 +106,15 @@ AD_HD float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi)
 AD_HD float sgnf(float v) { return v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f); }
 AD_HD float sqr(float v) { return v * v; }
 AD_HD int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+AD_HD float float_from_bits(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+  return __uint_as_float(u);
+#else
+  float v;
+  std::memcpy(&v, &u, sizeof(v));
+  return v;
+#endif
+}
 AD_HD uint32_t float_bits(float v) {
 #if defined(__CUDA_ARCH__)
   return __float_as_uint(v);

@@ -458,7 +458,7 @@ AD_HD void perception_update(G& g, TickShared& s, const Rng& rng, uint32_t tick,
         g.tyr(r, i) += g.tvy(r, i) * sp.dt;
       }
     }
-    if (sensor_tick) {
+    if (sensor_tick && !sp.stereo_tracks) {  // stereo-cluster tracks: sense_row()
       bool free_piece = w.f_active[base + i] && w.f_owner[base + i] < 0;
       float px = s.fpos[0][i], py = s.fpos[1][i];
       for (int r = 0; r < sp.R; ++r) {

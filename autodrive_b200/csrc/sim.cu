@@ -7,6 +7,9 @@
 //   tick      one CTA per environment; command synthesis, every physics
 //             substep of robots and FUEL with the state resident in shared
 //             memory, odometry, match clock, FUEL actions, perception, rewards
+//   sense     one CTA per (environment, robot) row on sensor ticks of the 3v3
+//             environment: stereo lenses, angular clustering, stereo fusion
+//             and anonymous track association (sense.h)
 // plus an optional observe stage (one CTA per environment) that writes the
 // 137-feature observation rows.
 //
@@ -306,6 +309,18 @@ __global__ void __launch_bounds__(512) perceive_kernel(World w, SimParams sp) {
   perceive_env(w, sp, s, e);
 }
 
+// One CTA per (env, robot) row; rows whose environment has no sensor update
+// this tick exit at once.
+__global__ void __launch_bounds__(256, 2) sense_kernel(World w, SimParams sp, int force) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int row = blockIdx.x;
+  const int e = row / sp.R, r = row % sp.R;
+  if (e >= sp.n || !w.active[e] || sp.mode[r] == MODE_NONE) return;
+  SenseScratch s;
+  sense_carve(smem, sp.P, &s);
+  sense_row(w, sp, s, e, r, force != 0);
+}
+
 // One CTA per (env, robot) row; rows not due for replanning exit at once.
 __global__ void plan_kernel(World w, SimParams sp, int force) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -402,6 +417,20 @@ void launch_plan(const World& w, const SimParams& sp, int force, cudaStream_t st
   check(cudaGetLastError(), "plan_kernel");
 }
 
+size_t sense_smem_bytes(const SimParams& sp) { return sense_carve(nullptr, sp.P, nullptr); }
+
+void launch_sense(const World& w, const SimParams& sp, int force, cudaStream_t st) {
+  const size_t smem = sense_smem_bytes(sp);
+  static size_t configured = 0;
+  if (smem > configured) {
+    check(cudaFuncSetAttribute(sense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+          "sense_kernel smem attribute");
+    configured = smem;
+  }
+  sense_kernel<<<sp.n * sp.R, 256, smem, st>>>(w, sp, force);
+  check(cudaGetLastError(), "sense_kernel");
+}
+
 void launch_tick(const World& w, const SimParams& sp, uint32_t tick, int run_game, int threads, cudaStream_t st) {
   static bool configured = false;
   const size_t smem = tick_smem_bytes();
@@ -485,6 +514,19 @@ void host_plan(World w, const SimParams& sp, int force) {
       if (!force && (ticks % sp.replan_interval) != 0) continue;
       PlanRequest q = make_plan_request(w, sp, e, r);
       plan_route(w, sp, e, r, q, ps);
+    }
+  });
+}
+
+void host_sense(World w, const SimParams& sp, int force) {
+  host_parallel(sp.n * sp.R, [&](int, int b, int end) {
+    std::vector<uint8_t> buf(sense_smem_bytes(sp) + 16);
+    SenseScratch s;
+    sense_carve(buf.data(), sp.P, &s);
+    for (int row = b; row < end; ++row) {
+      const int e = row / sp.R, r = row % sp.R;
+      if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;
+      sense_row(w, sp, s, e, r, force != 0);
     }
   });
 }

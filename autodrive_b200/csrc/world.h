@@ -108,6 +108,10 @@ enum DType : int { DT_F32 = 0, DT_I32 = 1, DT_U8 = 2, DT_I8 = 3, DT_F64 = 4 };
   X(t_conf, float, DT_F32, 3, N, R, P, 1)                               \
   X(t_quality, float, DT_F32, 3, N, R, P, 1)                            \
   X(t_mask, uint8_t, DT_U8, 3, N, R, P, 1)                              \
+  X(t_spatial, float, DT_F32, 4, N, R, 2, P)                            \
+  X(t_angular, float, DT_F32, 3, N, R, P, 1)                            \
+  X(t_merged, uint8_t, DT_U8, 3, N, R, P, 1)                            \
+  X(t_visible, uint8_t, DT_U8, 3, N, R, P, 1)                           \
   X(o_pose, float, DT_F32, 3, N, R, 3, 1)                               \
   X(o_vel, float, DT_F32, 3, N, R, 3, 1)                                \
   X(o_size, float, DT_F32, 3, N, R, 3, 1)                               \
@@ -179,6 +183,7 @@ struct SimParams {
   float perception_range = 6.f, perception_fov = 1.0471976f;  // half FOV (rad)
   float perception_dropout = .02f, position_noise = .015f, velocity_noise = .05f;
   float track_timeout = 2.f, ball_diameter = .15f, stereo_baseline = .0635f;
+  int stereo_tracks = 0;        // 1: anonymous stereo-cluster FUEL tracks; 0: per-piece tracks
   int replan_interval = 20;
   int teammate_coordination = 0;
   int normalize_obs = 1;

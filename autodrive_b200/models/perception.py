@@ -14,7 +14,8 @@ perception into the dictionary the zoo networks read
                   opponent (fuel_count + 4 tokens) with relative x/y (field
                   units), velocity / own max speed, age / track timeout,
                   confidence, four type flags (self/ally/opponent/FUEL) and x/y
-                  extent (field units); ``entity_mask`` marks valid tokens.
+                  extent (field units; a FUEL track's apparent-object extent);
+                  ``entity_mask`` marks valid tokens.
 
 Only perception state is read (tracks, the policy's pose estimate, teammates'
 reported poses, the opponent track) — never FUEL truth or enemy truth.
@@ -121,7 +122,10 @@ class PerceptionInputs:
         opp_vel = self._sel(ws["o_vel"])[:, :2]
         opp_ext = self._sel(ws["o_size"])[:, :2]
         opp_age = self._sel(ws["o_age"]).reshape(batch)
-        ext_f = torch.full((batch, P, 2), self.piece_extent, device=pos.device) * mask_f[..., None]
+        # stereo-cluster tracks carry the spatial extent of the apparent object;
+        # per-piece tracks (zero extent) fall back to one FUEL diameter
+        ext_f = torch.nan_to_num(self._sel(ws["t_spatial"]).transpose(1, 2))
+        ext_f = torch.where(ext_f > 0., ext_f, torch.full_like(ext_f, self.piece_extent)) * mask_f[..., None]
         positions = torch.cat((pos, own[:, None], mates_pos, opp_pos[:, None]), 1)
         velocities = torch.cat((vel, own_vel[:, None], mates_vel, opp_vel[:, None]), 1)
         extents = torch.cat((ext_f, own_ext[:, None], mates_ext, opp_ext[:, None]), 1)

@@ -168,7 +168,7 @@ class TensorThreeVsThreeEnv:
             teammate_coordination=int(self.teammate_coordination_enabled),
             normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=float(planner_resolution), plan_nx=plan_nx, plan_ny=plan_ny,
-            plan_sweeps=int(planner_sweeps), fuel_radius_rules=.0825,
+            plan_sweeps=int(planner_sweeps), fuel_radius_rules=.0825, stereo_tracks=1,
         )
         self.ws = WorldState(params, self.device)
         self.sim = RobotView(self.ws, dt=self.dt, field_length=field_length, field_width=field_width,
@@ -219,6 +219,11 @@ class TensorThreeVsThreeEnv:
     track_mask = property(lambda self: self.ws["t_mask"].bool())
     track_age = property(lambda self: self.ws["t_age"])
     track_confidence = property(lambda self: self.ws["t_conf"])
+    track_spatial_extent = property(lambda self: self.ws["t_spatial"].transpose(2, 3))
+    track_angular_extent = property(lambda self: self.ws["t_angular"])
+    track_merged = property(lambda self: self.ws["t_merged"].bool())
+    perception_quality_state = property(lambda self: self.ws["t_quality"])
+    _current_fuel_visibility = property(lambda self: self.ws["t_visible"].bool())
     opponent_pose = property(lambda self: self.ws["o_pose"])
     opponent_velocity = property(lambda self: self.ws["o_vel"])
     opponent_size = property(lambda self: self.ws["o_size"])
@@ -317,8 +322,8 @@ class TensorThreeVsThreeEnv:
         ws["g_hub"].masked_fill_(m[:, None], 1)
         for name in ("g_scores", "g_rcount", "g_rtime", "g_rlatch", "g_reward", "c_target",
                      "c_fuel_target", "c_fuel_delta", "c_command", "c_empty_ticks", "t_pos", "t_vel",
-                     "t_conf", "t_quality", "t_mask", "o_pose", "o_vel", "o_size", "o_valid",
-                     "p_path", "p_profile", "p_len", "p_goal", "p_start", "p_progress", "p_trench"):
+                     "t_conf", "t_quality", "t_mask", "t_spatial", "t_angular", "t_merged", "t_visible",
+                     "o_pose", "o_vel", "o_size", "o_valid", "p_path", "p_profile", "p_len", "p_goal", "p_start", "p_progress", "p_trench"):
             t = ws[name]
             t.masked_fill_(m.reshape((-1,) + (1,) * (t.ndim - 1)), 0)
         ws["g_action"].masked_fill_(m[:, None], 7)
