@@ -74,6 +74,7 @@ def stages(args):
         from autodrive_b200.ops import require_extension
         ext = require_extension()
         ext.phase_profile_read()
+        ext.sense_profile_read()
         ext.phase_profile_enable(True)
         for _ in range(args.ticks):
             sim.control(env._actions_buf)
@@ -83,6 +84,10 @@ def stages(args):
         torch.cuda.synchronize()
         ext.phase_profile_enable(False)
         cyc = ext.phase_profile_read()
+        scyc = ext.sense_profile_read()
+        snames = ("load", "lens_visibility", "lens_geometry_sort", "lens_depth_buffer", "lens_objects",
+                  "stereo_fusion", "packing", "association")
+        sense_phases = {n: round(c / max(1, sum(scyc)), 4) for n, c in zip(snames, scyc)}
         # robot_* and the join wait of warp 0 are on warp 0's timeline; fuel_integrate..fuel_apply and
         # their join wait on the FUEL warps' timeline (concurrent); the rest on the whole CTA's
         names = ("robot_swerve", "robot_sweep", "robot_contacts", "robot_tail", "fuel_integrate_clear",
@@ -96,6 +101,7 @@ def stages(args):
     awake = (env.ws["f_active"].bool() & (env.ws["f_sleep"] == 0)).float().sum(-1).mean().item()
     print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,
                       "awake_fuel_per_world": awake, "phase_share": phases,
+                      "sense_phase_share": sense_phases if args.phases else None,
                       "ms_per_tick": per_tick, "env_ticks_per_s": args.envs / (total / 1e3),
                       "threads": sim.threads}))
 

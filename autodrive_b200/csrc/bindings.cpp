@@ -204,6 +204,28 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "contacts, robot tail, fuel integrate+clear, fuel scatter, fuel pairs, fuel apply, fuel chassis "
         "reduction, fuel static, pre-substep, post-substep, robot-warp join wait, fuel-warps join wait, "
         "fuel count, fuel scan, fuel chassis loop, unused");
+  m.def("sense_rank_sort_host", [](torch::Tensor keys) {
+        // host twin of the sensor stage's bearing sort (both the all-pairs and bucketed paths)
+        auto k = keys.detach().to(torch::kCPU, torch::kFloat32).contiguous();
+        const int n = (int)k.numel();
+        if (n > 2 * kMaxPieces) throw std::runtime_error("at most 2 x 640 keys");
+        const int P = n / 2 + 1;
+        std::vector<uint8_t> buf(sense_carve(nullptr, P, nullptr) + 16);
+        SenseScratch s;
+        sense_carve(buf.data(), P, &s);
+        for (int b = 0; b <= kSortBuckets; ++b) s.sbucket[b] = 0;
+        const float* kp = k.data_ptr<float>();
+        for (int j = 0; j < n; ++j) sense_sort_add(s, j, kp[j]);
+        std::vector<int16_t> order(n > 0 ? n : 1);
+        sense_rank_sort(kp, n, order.data(), s);
+        auto out = torch::empty({n}, torch::kInt64);
+        for (int j = 0; j < n; ++j) out[j] = (int64_t)order[j];
+        return out;
+      }, "stable ascending order of keys in [-pi, pi] by the sensor stage's rank sort (host)");
+  m.def("sense_profile_read", &sense_profile_read,
+        "read and reset the sense kernel's 8 per-phase cycle totals (summed over rows; counted while the "
+        "phase profile is enabled): load, lens visibility, lens geometry+sort, lens depth buffer, lens "
+        "objects, stereo fusion, packing, association");
   m.def("plan_smem_bytes", [](py::dict d) { return plan_smem_bytes(params_from_dict(d)); });
   m.def("sense_smem_bytes", [](py::dict d) { return sense_smem_bytes(params_from_dict(d)); });
   py::class_<Sim>(m, "Sim")

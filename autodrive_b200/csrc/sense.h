@@ -48,11 +48,13 @@
 namespace ad {
 
 constexpr int kDepthBins = 256;
+constexpr int kSortBuckets = 512;  // equal-width bearing buckets over [-pi, pi]
+constexpr int kDirectRankMax = 256;  // lists up to this length are ranked all-pairs
 constexpr uint32_t RNG_SENSE = 7;
 
 struct SenseScratch {
   // free-piece state of the environment [P]
-  float *px, *py, *pvx, *pvy;
+  float *px, *py;
   uint8_t* pfree;
   // per-lens / per-side / association work (aliased) -----------------------
   int16_t* cidx;     // [2P] compacted element -> source index
@@ -75,7 +77,12 @@ struct SenseScratch {
   int32_t* winner;
   float* qual;
   uint8_t *observed, *accepted;
-  int32_t* misc;     // [64] warp scratch
+  int32_t* misc;     // [64] warp scratch, profile counters, occluder counts
+  float* occ;        // [4 (kMaxBoxes + kMaxRobots)] occluder table of the current lens
+  uint8_t* occ_on;   // [kMaxBoxes + kMaxRobots] occluders that can touch its view
+  // bucketed rank sort
+  int32_t* sbucket;  // [kSortBuckets + 1] bucket counts, then bucket starts
+  int16_t *stmp, *sslot;  // [2P] bucket-ordered elements, slot within the bucket
 };
 
 AD_HD size_t sense_align(size_t v) { return (v + 15) & ~(size_t)15; }
@@ -92,8 +99,6 @@ AD_HD size_t sense_carve(uint8_t* base, int P, SenseScratch* s) {
   SenseScratch t{};
   t.px = (float*)take(P1 * 4);
   t.py = (float*)take(P1 * 4);
-  t.pvx = (float*)take(P1 * 4);
-  t.pvy = (float*)take(P1 * 4);
   t.pfree = take(P1);
   t.cidx = (int16_t*)take(P2 * 2);
   t.key = (float*)take(P2 * 4);
@@ -134,11 +139,36 @@ AD_HD size_t sense_carve(uint8_t* base, int P, SenseScratch* s) {
   t.observed = t.flag;
   t.accepted = t.flag + P1;
   t.misc = (int32_t*)take(64 * 4);
+  t.sbucket = (int32_t*)take((kSortBuckets + 1) * 4);
+  t.occ = (float*)take(4 * (kMaxBoxes + kMaxRobots) * 4);
+  t.occ_on = take(kMaxBoxes + kMaxRobots);
+  t.stmp = (int16_t*)take(P2 * 2);
+  t.sslot = (int16_t*)take(P2 * 2);
   if (s) *s = t;
   return off;
 }
 
 constexpr int SM_WARP = 0;  // misc[0, 32): per-warp counts of a compaction
+// Opt-in per-phase cycle accounting (GPU only): misc[32] switches it on,
+// misc[34..52) holds kSensePhases 64-bit totals plus the last mark. Thread 0
+// marks right after a CTA barrier, so a bucket is that phase's share of the
+// row's critical path: 0 load, 1 lens visibility, 2 lens geometry + sort,
+// 3 lens depth buffer, 4 lens objects, 5 stereo fusion, 6 packing,
+// 7 association.
+constexpr int kSenseProfOn = 32, kSenseProfAcc = 34, kSensePhases = 8;
+#if defined(__CUDA_ARCH__)
+#define SENSE_MARK(s, k)                                                                       \
+  do {                                                                                         \
+    if ((s).misc[kSenseProfOn] && threadIdx.x == 0) {                                          \
+      unsigned long long* acc_ = reinterpret_cast<unsigned long long*>((s).misc + kSenseProfAcc); \
+      const unsigned long long t_ = clock64();                                                 \
+      acc_[(k)] += t_ - acc_[kSensePhases];                                                    \
+      acc_[kSensePhases] = t_;                                                                 \
+    }                                                                                          \
+  } while (0)
+#else
+#define SENSE_MARK(s, k) ((void)0)
+#endif
 
 // Order-preserving compaction of the indices i < n whose flag is set:
 // out[0..count) = those indices ascending. Every thread returns the count.
@@ -172,46 +202,115 @@ AD_HD int sense_compact(const uint8_t* flags, int n, int16_t* out, int32_t* warp
 #endif
 }
 
-// Stable rank sort: order[rank] = j for keys[0..n) ascending (ties by j).
-AD_HD void sense_rank_sort(const float* keys, int n, int16_t* order) {
+AD_HD int sense_bucket(float key) {
+  return clampi((int)floorf((key + kPi) * ((float)kSortBuckets / kTwoPi)), 0, kSortBuckets - 1);
+}
+
+// In-place exclusive scan of counts[0..kSortBuckets); counts[kSortBuckets] = total.
+AD_HD void sense_scan_buckets(int32_t* counts, int32_t* warp_sums) {
+#if defined(__CUDA_ARCH__)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = (kSortBuckets + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  int local = 0;
+  for (int k = 0; k < per; ++k) local += b0 + k < kSortBuckets ? counts[b0 + k] : 0;
+  int incl = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  int carry = 0, total = 0;
+  for (int w2 = 0; w2 < nw; ++w2) {
+    carry += w2 < warp ? warp_sums[w2] : 0;
+    total += warp_sums[w2];
+  }
+  int run = carry + incl - local;
+  for (int k = 0; k < per; ++k) {
+    if (b0 + k < kSortBuckets) {
+      const int c = counts[b0 + k];
+      counts[b0 + k] = run;
+      run += c;
+    }
+  }
+  if (threadIdx.x == 0) counts[kSortBuckets] = total;
+  __syncthreads();
+#else
+  (void)warp_sums;
+  int run = 0;
+  for (int b = 0; b < kSortBuckets; ++b) {
+    const int c = counts[b];
+    counts[b] = run;
+    run += c;
+  }
+  counts[kSortBuckets] = run;
+#endif
+}
+
+// Stable rank sort of keys in [-pi, pi]: order[rank] = j ascending by key,
+// ties by j. The loop that writes keys[j] also calls sense_sort_add(s, j,
+// key), which drops element j into an equal-width key bucket (a bucket's
+// internal order is arbitrary); after a barrier sense_rank_sort() scans the
+// bucket counts, lists every bucket's elements, and each element counts the
+// smaller (key, index) pairs of its own bucket. Buckets hold few elements, so
+// the cost is near linear. The bucket counts are zero between sorts (cleared
+// at set-up and again at the end of every sort).
+AD_HD void sense_sort_add(SenseScratch& s, int j, float key) {
+  const int b = sense_bucket(key);
+#if defined(__CUDA_ARCH__)
+  s.sslot[j] = (int16_t)atomicAdd(&s.sbucket[b], 1);
+#else
+  s.sslot[j] = (int16_t)s.sbucket[b]++;
+#endif
+}
+
+AD_HD void sense_rank_sort(const float* keys, int n, int16_t* order, SenseScratch& s) {
+  int32_t* cnt = s.sbucket;
+  if (n <= kDirectRankMax) {
+    // short lists: all-pairs ranks in one pass beat the bucket passes' barriers
+    PAR_FOR(j, n) {
+      const float kj = keys[j];
+      int r = 0;
+      for (int k = 0; k < n; ++k) {
+        const float kk = keys[k];
+        r += (kk < kj) || (kk == kj && k < j);
+      }
+      order[r] = (int16_t)j;
+    }
+    BARRIER();
+    PAR_FOR(b, kSortBuckets + 1) { cnt[b] = 0; }
+    return;
+  }
+  sense_scan_buckets(cnt, s.misc + SM_WARP);
+  PAR_FOR(j, n) { s.stmp[cnt[sense_bucket(keys[j])] + s.sslot[j]] = (int16_t)j; }
+  BARRIER();
   PAR_FOR(j, n) {
     const float kj = keys[j];
-    int r = 0;
-    for (int k = 0; k < n; ++k) {
+    const int b = sense_bucket(kj);
+    const int t0 = cnt[b], t1 = cnt[b + 1];
+    int r = t0;
+    for (int t = t0; t < t1; ++t) {
+      const int k = s.stmp[t];
       const float kk = keys[k];
       r += (kk < kj) || (kk == kj && k < j);
     }
     order[r] = (int16_t)j;
   }
   BARRIER();
+  // the next sort's first bucket access follows at least one more barrier
+  PAR_FOR(b, kSortBuckets + 1) { cnt[b] = 0; }
 }
 
-AD_HD float sense_wrapped_bearing(float dx, float dy, float heading) {
-  return angle_diff(atan2f(dy, dx), heading);
+// Bearing of (dx, dy) relative to the unit heading (hx, hy), in [-pi, pi].
+AD_HD float sense_bearing(float dx, float dy, float hx, float hy) {
+  return atan2f(hx * dy - hy * dx, hx * dx + hy * dy);
 }
 
-// Segment origin -> origin + (dx, dy) passes through a solid field box
-// (3 cm margin), ignoring the first and last 2 % of the segment.
-AD_HD bool sense_box_blocked(const SimParams& sp, float ox, float oy, float dx, float dy) {
-  const bool par_x = fabsf(dx) < 1e-8f, par_y = fabsf(dy) < 1e-8f;
-  for (int b = 0; b < sp.num_boxes; ++b) {
-    const Box& bx = sp.boxes[b];
-    const float hx = bx.hx + .03f, hy = bx.hy + .03f;
-    if ((par_x && fabsf(ox - bx.cx) > hx) || (par_y && fabsf(oy - bx.cy) > hy)) continue;
-    const float sx = par_x ? 1.f : dx, sy = par_y ? 1.f : dy;
-    const float tx0 = (bx.cx - hx - ox) / sx, tx1 = (bx.cx + hx - ox) / sx;
-    const float ty0 = (bx.cy - hy - oy) / sy, ty1 = (bx.cy + hy - oy) / sy;
-    const float nx = par_x ? -kInf : fminf(tx0, tx1), fx = par_x ? kInf : fmaxf(tx0, tx1);
-    const float ny = par_y ? -kInf : fminf(ty0, ty1), fy = par_y ? kInf : fmaxf(ty0, ty1);
-    const float enter = fmaxf(fmaxf(nx, ny), .02f), leave = fminf(fminf(fx, fy), .98f);
-    if (leave >= enter) return true;
-  }
-  return false;
-}
-
-// Lens pose c (0/1 intake left/right, 2/3 opposite left/right) of robot r.
+// Lens pose c (0/1 intake left/right, 2/3 opposite left/right) of robot r:
+// optical centre (lx, ly) and unit viewing direction (hx, hy).
 AD_HD void sense_lens_pose(const World& w, const SimParams& sp, int e, int r, int c, float& lx, float& ly,
-                           float& lh) {
+                           float& hx, float& hy) {
   const size_t er = (size_t)e * sp.R + r;
   const float* p = w.r_pose + er * 3;
   const float L = w.r_param[er * kNumRobotParams + RP_LENGTH];
@@ -220,60 +319,129 @@ AD_HD void sense_lens_pose(const World& w, const SimParams& sp, int e, int r, in
   const float lat = (c & 1) ? -.5f * sp.stereo_baseline : .5f * sp.stereo_baseline;
   lx = p[0] + cth * fwd - sth * lat;
   ly = p[1] + sth * fwd + cth * lat;
-  lh = c < 2 ? p[2] : angle_diff(p[2] + kPi, 0.f);
+  hx = c < 2 ? cth : -cth;
+  hy = c < 2 ? sth : -sth;
+}
+
+// Occluders that can touch lens c's field of view (a circle of radius `rad`
+// around (cx, cy) reaching the range disc and the view cone). Slot k of the
+// row's occluder table holds solid box k (+3 cm margin) as [x0, x1, y0, y1]
+// or, after the boxes, robot q as [x, y, radius^2, 0]; slot flags mark the
+// occluders that matter for this lens. One slot per thread; a barrier follows.
+AD_HD bool sense_occluder_near(float cx, float cy, float rad, float lx, float ly, float hx, float hy, float range,
+                               float hf, bool full_fov) {
+  const float dx = cx - lx, dy = cy - ly;
+  const float dist = sqrtf(dx * dx + dy * dy);
+  if (dist > range + rad) return false;
+  if (full_fov || dist <= rad) return true;
+  const float ang = fabsf(sense_bearing(dx, dy, hx, hy));
+  return ang <= hf + asinf(fminf(rad / dist, 1.f));
+}
+
+AD_HD void sense_build_occluders(const World& w, const SimParams& sp, SenseScratch& s, int e, int r, float lx,
+                                 float ly, float hx, float hy, float hf, bool full_fov) {
+  PAR_FOR(k, sp.num_boxes + sp.R) {
+    float* o = s.occ + 4 * k;
+    bool near = false;
+    if (k < sp.num_boxes) {
+      const Box& bx = sp.boxes[k];
+      const float ex = bx.hx + .03f, ey = bx.hy + .03f;
+      near = sense_occluder_near(bx.cx, bx.cy, sqrtf(ex * ex + ey * ey), lx, ly, hx, hy, sp.perception_range, hf,
+                                 full_fov);
+      o[0] = bx.cx - ex;
+      o[1] = bx.cx + ex;
+      o[2] = bx.cy - ey;
+      o[3] = bx.cy + ey;
+    } else {
+      const int q = k - sp.num_boxes;
+      const size_t eq = (size_t)e * sp.R + q;
+      const float* qp = w.r_pose + eq * 3;
+      const float rad = robot_radius_of(w.r_param[eq * kNumRobotParams + RP_LENGTH],
+                                        w.r_param[eq * kNumRobotParams + RP_WIDTH]);
+      near = q != r && sense_occluder_near(qp[0], qp[1], rad, lx, ly, hx, hy, sp.perception_range, hf, full_fov);
+      o[0] = qp[0];
+      o[1] = qp[1];
+      o[2] = rad * rad;
+      o[3] = 0.f;
+    }
+    s.occ_on[k] = near ? 1 : 0;
+  }
+}
+
+// Segment lens -> lens + (dx, dy) blocked by a flagged box (ignoring the
+// first and last 2 % of the segment) or passing within a flagged robot's
+// radius (closest point strictly inside the 2..98 % window).
+AD_HD bool sense_occluded(const SenseScratch& s, float lx, float ly, float dx, float dy, int nbox, int nall) {
+  const bool par_x = fabsf(dx) < 1e-8f, par_y = fabsf(dy) < 1e-8f;
+  const float ix = par_x ? 0.f : 1.f / dx, iy = par_y ? 0.f : 1.f / dy;
+  for (int b = 0; b < nbox; ++b) {
+    if (!s.occ_on[b]) continue;
+    const float* o = s.occ + 4 * b;
+    if ((par_x && (lx < o[0] || lx > o[1])) || (par_y && (ly < o[2] || ly > o[3]))) continue;
+    const float tx0 = (o[0] - lx) * ix, tx1 = (o[1] - lx) * ix;
+    const float ty0 = (o[2] - ly) * iy, ty1 = (o[3] - ly) * iy;
+    const float nx = par_x ? -kInf : fminf(tx0, tx1), fx = par_x ? kInf : fmaxf(tx0, tx1);
+    const float ny = par_y ? -kInf : fminf(ty0, ty1), fy = par_y ? kInf : fmaxf(ty0, ty1);
+    if (fminf(fminf(fx, fy), .98f) >= fmaxf(fmaxf(nx, ny), .02f)) return true;
+  }
+  const float inv_den = 1.f / fmaxf(dx * dx + dy * dy, 1e-8f);
+  for (int q = nbox; q < nall; ++q) {
+    if (!s.occ_on[q]) continue;
+    const float* o = s.occ + 4 * q;
+    const float t = ((o[0] - lx) * dx + (o[1] - ly) * dy) * inv_den;
+    if (!(t > .02f && t < .98f)) continue;
+    const float cx = lx + t * dx - o[0], cy = ly + t * dy - o[1];
+    if (cx * cx + cy * cy <= o[2]) return true;
+  }
+  return false;
 }
 
 // Cluster what lens c sees into the side object list at offset `base`;
 // returns the number of object slots written (groups, valid or not).
 AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e, int r, int c, int base) {
   const int P = sp.P;
-  float lx, ly, lh;
-  sense_lens_pose(w, sp, e, r, c, lx, ly, lh);
+  float lx, ly, hx, hy;
+  sense_lens_pose(w, sp, e, r, c, lx, ly, hx, hy);
   const float hf = fminf(sp.perception_fov, kPi);
   const bool full_fov = sp.perception_fov >= kPi;
   const float D = sp.ball_diameter;
-  // 1. visibility
+  // 1. visibility: range, view cone (angle to the viewing direction <= hf,
+  // tested as dot >= |d| cos hf), then the occluders near this lens
+  sense_build_occluders(w, sp, s, e, r, lx, ly, hx, hy, hf, full_fov);
+  PAR_FOR(b, kDepthBins) { s.bins[b] = float_bits(kInf); }
+  BARRIER();
+  const int nb = sp.num_boxes, nr = sp.num_boxes + sp.R;
+  const float range2 = sp.perception_range * sp.perception_range, cos_hf = cosf(hf);
   PAR_FOR(i, P) {
     bool vis = s.pfree[i] != 0;
     if (vis) {
       const float dx = s.px[i] - lx, dy = s.py[i] - ly;
-      vis = sqrtf(dx * dx + dy * dy) <= sp.perception_range;
-      if (vis && !full_fov) vis = fabsf(sense_wrapped_bearing(dx, dy, lh)) <= hf;
-      if (vis) vis = !sense_box_blocked(sp, lx, ly, dx, dy);
-      if (vis) {
-        const float den = fmaxf(dx * dx + dy * dy, 1e-8f);
-        for (int q = 0; q < sp.R && vis; ++q) {
-          if (q == r) continue;
-          const size_t eq = (size_t)e * sp.R + q;
-          const float* qp = w.r_pose + eq * 3;
-          const float t = ((qp[0] - lx) * dx + (qp[1] - ly) * dy) / den;
-          if (!(t > .02f && t < .98f)) continue;
-          const float cxq = lx + t * dx - qp[0], cyq = ly + t * dy - qp[1];
-          const float rad = robot_radius_of(w.r_param[eq * kNumRobotParams + RP_LENGTH],
-                                            w.r_param[eq * kNumRobotParams + RP_WIDTH]);
-          if (sqrtf(cxq * cxq + cyq * cyq) <= rad) vis = false;
-        }
-      }
+      const float d2 = dx * dx + dy * dy;
+      vis = d2 <= range2;
+      if (vis && !full_fov) vis = hx * dx + hy * dy >= cos_hf * sqrtf(d2);
+      if (vis) vis = !sense_occluded(s, lx, ly, dx, dy, nb, nr);
     }
     s.flag[i] = vis ? 1 : 0;
   }
-  PAR_FOR(b, kDepthBins) { s.bins[b] = float_bits(kInf); }
   BARRIER();
   const int n = sense_compact(s.flag, P, s.cidx, s.misc + SM_WARP);
+  SENSE_MARK(s, 1);
   // 2. geometry of the visible pieces, bearing order
   PAR_FOR(j, n) {
     const int i = s.cidx[j];
     const float dx = s.px[i] - lx, dy = s.py[i] - ly;
     const float d = sqrtf(dx * dx + dy * dy);
-    const float b = sense_wrapped_bearing(dx, dy, lh);
+    const float b = sense_bearing(dx, dy, hx, hy);
     const float h = atan2f(D * .5f, fmaxf(d, 1e-4f));
     s.key[j] = b;
+    sense_sort_add(s, j, b);
     s.rng[j] = d;
     s.lo[j] = fmaxf(-hf, b - h);
     s.hi[j] = fminf(hf, b + h);
   }
   BARRIER();
-  sense_rank_sort(s.key, n, s.order);
+  sense_rank_sort(s.key, n, s.order, s);
+  SENSE_MARK(s, 2);
   // 3. depth buffer and visible fractions
   const float bw = 2.f * hf / (float)kDepthBins;
   PAR_FOR(j, n) {
@@ -299,6 +467,7 @@ AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e
     s.frac[j] = (float)seen / (float)(b1 - b0 + 1);
   }
   BARRIER();
+  SENSE_MARK(s, 3);
   // 4. apparent objects: runs of joined neighbours in bearing order
   PAR_FOR(t, n) {
     bool join = false;
@@ -331,8 +500,8 @@ AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e
       mem += 1.f;
       sx += x * f;
       sy += y * f;
-      vx += s.pvx[i] * f;
-      vy += s.pvy[i] * f;
+      vx += w.f_vel[(size_t)e * 3 * P + i] * f;
+      vy += w.f_vel[(size_t)e * 3 * P + P + i] * f;
       mnx = fminf(mnx, x);
       mny = fminf(mny, y);
       mxx = fmaxf(mxx, x);
@@ -354,6 +523,7 @@ AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e
     s.cconf[o] = valid ? fminf(1.f, den / fmaxf(mem, 1.f)) : 0.f;
   }
   BARRIER();
+  SENSE_MARK(s, 4);
   return groups;
 }
 
@@ -363,21 +533,23 @@ AD_HD int sense_fuse(const World& w, const SimParams& sp, SenseScratch& s, int e
                      int out) {
   const int P = sp.P;
   const float* p = w.r_pose + ((size_t)e * sp.R + r) * 3;
-  const float heading = p[2] + (side ? kPi : 0.f);
+  const float sgn = side ? -1.f : 1.f;
+  const float hx = sgn * cosf(p[2]), hy = sgn * sinf(p[2]);
   PAR_FOR(k, m) { s.flag[k] = s.cvalid[k]; }
   BARRIER();
   const int n = sense_compact(s.flag, m, s.cidx, s.misc + SM_WARP);
   PAR_FOR(j, n) {
     const int k = s.cidx[j];
     const float dx = s.cx[k] - p[0], dy = s.cy[k] - p[1];
-    const float b = sense_wrapped_bearing(dx, dy, heading);
+    const float b = sense_bearing(dx, dy, hx, hy);
     s.key[j] = b;
+    sense_sort_add(s, j, b);
     s.lo[j] = b - s.cang[k] * .5f;
     s.hi[j] = b + s.cang[k] * .5f;
     s.rng[j] = sqrtf(dx * dx + dy * dy);
   }
   BARRIER();
-  sense_rank_sort(s.key, n, s.order);
+  sense_rank_sort(s.key, n, s.order, s);
   PAR_FOR(t, n) {
     bool join = false;
     if (t > 0) {
@@ -430,6 +602,7 @@ AD_HD int sense_fuse(const World& w, const SimParams& sp, SenseScratch& s, int e
     s.fmerged[o] = (merged || members > 1) ? 1 : 0;
   }
   BARRIER();
+  SENSE_MARK(s, 5);
   return groups;
 }
 
@@ -446,12 +619,12 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
   PAR_FOR(i, P) {
     s.px[i] = w.f_pos[(size_t)e * 3 * P + i];
     s.py[i] = w.f_pos[(size_t)e * 3 * P + P + i];
-    s.pvx[i] = w.f_vel[(size_t)e * 3 * P + i];
-    s.pvy[i] = w.f_vel[(size_t)e * 3 * P + P + i];
     s.pfree[i] = (w.f_active[base_p + i] && w.f_owner[base_p + i] < 0) ? 1 : 0;
     w.t_visible[row * P + i] = 0;
   }
+  PAR_FOR(b, kSortBuckets + 1) { s.sbucket[b] = 0; }
   BARRIER();
+  SENSE_MARK(s, 0);
   // rear pair first, so the packed order (rear >= 0, front, rear < 0) is known
   int nside[2] = {0, 0};
   for (int side = 1; side >= 0; --side) {
@@ -476,6 +649,7 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
     s.det[k] = (int16_t)src;
   }
   BARRIER();
+  SENSE_MARK(s, 6);
   // 5. association: live tracks in bearing order
   const float* own = w.r_pose + row * 3;
   const float* tpx = w.t_pos + row * 2 * P;
@@ -484,53 +658,53 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
   BARRIER();
   int16_t* tslot = s.gstart;  // compacted live slots
   const int nt = sense_compact(s.flag, P, tslot, s.misc + SM_WARP);
+  const float ohx = cosf(own[2]), ohy = sinf(own[2]);
   PAR_FOR(j, nt) {
     const int k = tslot[j];
-    s.key[j] = sense_wrapped_bearing(tpx[k] - own[0], tpy[k] - own[1], own[2]);
+    s.key[j] = sense_bearing(tpx[k] - own[0], tpy[k] - own[1], ohx, ohy);
+    sense_sort_add(s, j, s.key[j]);
   }
   BARRIER();
   int16_t* torder = s.gstart + P;  // rank -> compacted live slot
-  sense_rank_sort(s.key, nt, torder);
+  sense_rank_sort(s.key, nt, torder, s);
   const float gate = .35f + 4.f * sp.position_noise;
   float* qstate = w.t_quality + row * P;
   PAR_FOR(i, P) { s.winner[i] = P + 1; }
   BARRIER();
-  PAR_FOR(i, P) {
+  PAR_FOR(i, ndet) {
     bool observed = false;
     int cand = -1;
-    if (i < ndet) {
-      const int f = s.det[i];
-      const float dx = s.fx[f] - own[0], dy = s.fy[f] - own[1];
-      const float dist = fmaxf(sqrtf(dx * dx + dy * dy), .05f);
-      const float width = 2.f * atanf((sp.ball_diameter * .5f) / dist);
-      const float inst = clampf(expf(-dist / 8.f) * fminf(width / .012f, 1.f), 0.f, 1.f) * s.fconf[f];
-      const float q = (.8f * qstate[i] + .2f * inst) * s.fconf[f];
-      qstate[i] = q;
-      s.qual[i] = q;
-      observed = rng.uniform((uint32_t)e, tick_id, RNG_SENSE, (uint32_t)(r * kMaxPieces + i)) <
-                 q * (1.f - sp.perception_dropout);
-      if (observed) {
-        float best = kInf;
-        const int r0 = i - 1 < 0 ? 0 : i - 1, r1 = i + 1 < P - 1 ? i + 1 : P - 1;
-        for (int rk = r0; rk <= r1; ++rk) {
-          if (rk >= nt) continue;
-          const int slot = tslot[torder[rk]];
-          const float ex = tpx[slot] - s.fx[f], ey = tpy[slot] - s.fy[f];
-          const float d = sqrtf(ex * ex + ey * ey);
-          if (d < best) {
-            best = d;
-            cand = slot;
-          }
+    const int f = s.det[i];
+    const float dx = s.fx[f] - own[0], dy = s.fy[f] - own[1];
+    const float dist = fmaxf(sqrtf(dx * dx + dy * dy), .05f);
+    const float width = 2.f * atanf((sp.ball_diameter * .5f) / dist);
+    const float inst = clampf(expf(-dist / 8.f) * fminf(width / .012f, 1.f), 0.f, 1.f) * s.fconf[f];
+    const float q = (.8f * qstate[i] + .2f * inst) * s.fconf[f];
+    qstate[i] = q;
+    s.qual[i] = q;
+    observed = rng.uniform((uint32_t)e, tick_id, RNG_SENSE, (uint32_t)(r * kMaxPieces + i)) <
+               q * (1.f - sp.perception_dropout);
+    if (observed) {
+      float best = kInf;
+      const int r0 = i - 1 < 0 ? 0 : i - 1, r1 = i + 1 < P - 1 ? i + 1 : P - 1;
+      for (int rk = r0; rk <= r1; ++rk) {
+        if (rk >= nt) continue;
+        const int slot = tslot[torder[rk]];
+        const float ex = tpx[slot] - s.fx[f], ey = tpy[slot] - s.fy[f];
+        const float d = sqrtf(ex * ex + ey * ey);
+        if (d < best) {
+          best = d;
+          cand = slot;
         }
-        if (cand >= 0 && best <= gate) {
+      }
+      if (cand >= 0 && best <= gate) {
 #if defined(__CUDA_ARCH__)
-          atomicMin(&s.winner[cand], i);
+        atomicMin(&s.winner[cand], i);
 #else
-          if (i < s.winner[cand]) s.winner[cand] = i;
+        if (i < s.winner[cand]) s.winner[cand] = i;
 #endif
-        } else {
-          cand = -1;
-        }
+      } else {
+        cand = -1;
       }
     }
     s.cand[i] = (int16_t)cand;
@@ -538,7 +712,7 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
   }
   BARRIER();
   // matched detections keep their track; the rest take free slots in order
-  PAR_FOR(i, P) {
+  PAR_FOR(i, ndet) {
     const int c = s.cand[i];
     const bool won = s.observed[i] && c >= 0 && s.winner[c] == i;
     s.accepted[i] = won ? 1 : 0;
@@ -547,7 +721,7 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
   }
   BARRIER();
   int16_t* needs = s.gstart;  // live-slot list no longer needed
-  const int nneed = sense_compact(s.flag, P, needs, s.misc + SM_WARP);
+  const int nneed = sense_compact(s.flag, ndet, needs, s.misc + SM_WARP);
   PAR_FOR(i, P) { s.flag[i] = w.t_mask[row * P + i] ? 0 : 1; }
   BARRIER();
   int16_t* freelist = s.gstart + P;
@@ -561,7 +735,7 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
   }
   BARRIER();
   // track writes
-  PAR_FOR(i, P) {
+  PAR_FOR(i, ndet) {
     if (!s.accepted[i]) continue;
     const int slot = s.target[i], f = s.det[i];
     const size_t k = row * P + slot;
@@ -598,6 +772,7 @@ AD_HD void sense_row(World& w, const SimParams& sp, SenseScratch& s, int e, int 
     w.t_visible[k] = 1;
   }
   BARRIER();
+  SENSE_MARK(s, 7);
 }
 
 }  // namespace ad

@@ -284,6 +284,7 @@ __global__ void observe_kernel(World w, SimParams sp) {
 
 __device__ int g_prof_on = 0;
 __device__ unsigned long long g_prof[18];
+__device__ unsigned long long g_sense_prof[kSensePhases];
 
 __global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -318,7 +319,17 @@ __global__ void __launch_bounds__(256, 2) sense_kernel(World w, SimParams sp, in
   if (e >= sp.n || !w.active[e] || sp.mode[r] == MODE_NONE) return;
   SenseScratch s;
   sense_carve(smem, sp.P, &s);
+  if (threadIdx.x == 0) {
+    s.misc[kSenseProfOn] = g_prof_on;
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(s.misc + kSenseProfAcc);
+    for (int k = 0; k < kSensePhases; ++k) acc[k] = 0ull;
+    acc[kSensePhases] = clock64();
+  }
   sense_row(w, sp, s, e, r, force != 0);
+  if (threadIdx.x == 0 && s.misc[kSenseProfOn]) {
+    const unsigned long long* acc = reinterpret_cast<const unsigned long long*>(s.misc + kSenseProfAcc);
+    for (int k = 0; k < kSensePhases; ++k) atomicAdd(&g_sense_prof[k], acc[k]);
+  }
 }
 
 // One CTA per (env, robot) row; rows not due for replanning exit at once.
@@ -383,6 +394,16 @@ std::vector<unsigned long long> phase_profile_read() {
   check(cudaMemcpyFromSymbol(out.data(), g_prof, sizeof(unsigned long long) * 18), "phase profile read");
   std::vector<unsigned long long> zero(18, 0ull);
   check(cudaMemcpyToSymbol(g_prof, zero.data(), sizeof(unsigned long long) * 18), "phase profile reset");
+  return out;
+}
+
+std::vector<unsigned long long> sense_profile_read() {
+  std::vector<unsigned long long> out(kSensePhases, 0ull);
+  check(cudaMemcpyFromSymbol(out.data(), g_sense_prof, sizeof(unsigned long long) * kSensePhases),
+        "sense profile read");
+  std::vector<unsigned long long> zero(kSensePhases, 0ull);
+  check(cudaMemcpyToSymbol(g_sense_prof, zero.data(), sizeof(unsigned long long) * kSensePhases),
+        "sense profile reset");
   return out;
 }
 

@@ -141,3 +141,14 @@ def test_sense_kernel_matches_host_twin():
     assert torch.equal(cpu.ws["t_merged"], gpu.ws["t_merged"].cpu())
     for name in ("t_pos", "t_spatial", "t_conf", "t_quality"):
         assert torch.allclose(cpu.ws[name], gpu.ws[name].cpu(), atol=2e-3, rtol=1e-3), name
+
+
+@pytest.mark.parametrize("n", [1, 37, 256, 257, 600, 1280])
+def test_bearing_rank_sort_is_a_stable_sort(n):
+    from autodrive_b200.ops import require_extension
+    g = torch.Generator().manual_seed(n)
+    keys = (torch.rand(n, generator=g) * 2 - 1) * math.pi
+    keys[::7] = keys[0]                      # ties resolve by index
+    keys[1::11] = math.pi                    # the last bucket's edge
+    order = require_extension().sense_rank_sort_host(keys)
+    assert torch.equal(order, torch.sort(keys, stable=True).indices)
