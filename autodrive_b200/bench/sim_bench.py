@@ -93,7 +93,7 @@ def stages(args):
         names = ("robot_swerve", "robot_sweep", "robot_contacts", "robot_tail", "fuel_integrate_clear",
                  "fuel_scatter", "fuel_pairs", "fuel_apply", "fuel_chassis_reduce", "fuel_static",
                  "pre_substeps", "post_substeps", "robot_warp_join_wait", "fuel_warps_join_wait",
-                 "fuel_count", "fuel_scan", "fuel_chassis_loop", "unused")
+                 "fuel_count", "fuel_scan", "fuel_chassis_loop", "fuel_pairs_loop")
         robot_line = sum(cyc[k] for k in (0, 1, 2, 3, 12))
         crit = max(1, robot_line + sum(cyc[k] for k in (8, 9, 10, 11, 16)))
         phases = {n: round(c / crit, 4) for n, c in zip(names, cyc)}

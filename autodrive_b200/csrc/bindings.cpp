@@ -203,7 +203,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "read and reset the 18 per-phase cycle totals (summed over CTAs): robot swerve, robot sweep, robot "
         "contacts, robot tail, fuel integrate+clear, fuel scatter, fuel pairs, fuel apply, fuel chassis "
         "reduction, fuel static, pre-substep, post-substep, robot-warp join wait, fuel-warps join wait, "
-        "fuel count, fuel scan, fuel chassis loop, unused");
+        "fuel count, fuel scan, fuel chassis loop, fuel pairs loop (the pairs bucket then holds only its reduction)");
   m.def("sense_rank_sort_host", [](torch::Tensor keys) {
         // host twin of the sensor stage's bearing sort (both the all-pairs and bucketed paths)
         auto k = keys.detach().to(torch::kCPU, torch::kFloat32).contiguous();

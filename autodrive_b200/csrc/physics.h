@@ -1237,16 +1237,19 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
     int deg = 0;
     {
       const float px = s.fpos[0][i], py = s.fpos[1][i], pz = s.fpos[2][i];
-      // neighbour rows: cells x-1..x+1 of a row are consecutive in the sorted order
-      const int cx = clampi((int)floorf(px / sp.grid_cell), 0, sp.grid_nx - 1);
-      const int cy = clampi((int)floorf(py / sp.grid_cell), 0, sp.grid_ny - 1);
-      const int x0 = cx > 0 ? cx - 1 : 0, x1 = cx + 1 < sp.grid_nx ? cx + 1 : sp.grid_nx - 1;
+      // candidate cells: those overlapping [p - r2, p + r2] in x and y (any
+      // contact lies there; the cell index is monotone in the coordinate; a
+      // 0.1 mm margin absorbs rounding); the cells of a row are consecutive in
+      // the sorted order
+      const float inv_cell = 1.f / sp.grid_cell, reach = r2 + 1e-4f;
+      const int x0 = clampi((int)floorf((px - reach) * inv_cell), 0, sp.grid_nx - 1);
+      const int x1 = clampi((int)floorf((px + reach) * inv_cell), 0, sp.grid_nx - 1);
+      const int y0 = clampi((int)floorf((py - reach) * inv_cell), 0, sp.grid_ny - 1);
+      const int y1 = clampi((int)floorf((py + reach) * inv_cell), 0, sp.grid_ny - 1);
       const bool sleep_i = s.sleep[i];
       const V3 vi = V3{s.fvel[0][i], s.fvel[1][i], s.fvel[2][i]};
       const V3 wi = V3{s.fang[0][i], s.fang[1][i], s.fang[2][i]};
-      for (int oy = -1; oy <= 1; ++oy) {
-        const int yy = cy + oy;
-        if (yy < 0 || yy >= sp.grid_ny) continue;
+      for (int yy = y0; yy <= y1; ++yy) {
         const int row = yy * sp.grid_nx;
         if (sleep_i) {  // a sleeping sphere only interacts with awake ones
           bool awake_row = false;
@@ -1294,6 +1297,7 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
     local_max[1] = fmaxf(local_max[1], (float)deg);
   }
   group_sync(g);
+  PHASE_MARK_BY(s, 17, g.first);
   group_max<2>(s, local_max, g);
   PHASE_MARK_BY(s, 6, g.first);
   // crowded piles share one Jacobi response scale per world
