@@ -24,6 +24,7 @@ int64_t dim_value(const std::string& sym, int64_t N, int64_t R, int64_t P) {
   if (sym == "Q") return R * (R - 1) / 2;
   if (sym == "K") return kPathPoints;
   if (sym == "O") return kObsDim;
+  if (sym == "S") return kRasterPoints;
   if (sym == "kNumRobotParams") return kNumRobotParams;
   return std::stoll(sym);
 }
@@ -77,13 +78,14 @@ SimParams params_from_dict(const py::dict& d) {
   I(robot_height) I(max_comp) I(pair_damping) I(sleep) I(sleep_time) I(sleep_speed) I(sleep_ang)
   I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule)
   I(perception_interval) I(opponent_kind) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
-  I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(stereo_tracks) I(replan_interval)
+  I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(stereo_tracks) I(sweeping) I(raster_lookahead) I(replan_interval)
   I(teammate_coordination) I(normalize_obs) I(horizon) I(max_speed_nominal) I(max_omega_nominal)
   I(plan_res) I(plan_nx) I(plan_ny) I(plan_sweeps) I(bump_cost) I(seed0) I(seed1)
 #undef I
   p.Q = p.R * (p.R - 1) / 2;
   set_boxes(d, "boxes", p.boxes, kMaxBoxes, p.num_boxes);
   set_boxes(d, "bumps", p.bumps, kMaxBumps, p.num_bumps);
+  set_boxes(d, "depots", p.depots, 2, p.num_depots);
   set_array(d, "hub_x", p.hub_x, 2);
   set_array(d, "hub_y", p.hub_y, 2);
   set_array(d, "team", p.team, kMaxRobots);

@@ -38,7 +38,7 @@ struct G {
   AD_HD float param(int r, int k) const { return w.r_param[er(r) * kNumRobotParams + k]; }
   AD_HD float* ppose(int r) { return w.policy_pose + er(r) * 3; }
   AD_HD float* rvel(int r) { return w.r_vel + er(r) * 3; }
-  AD_HD uint8_t& latch(int r, int k) { return w.g_rlatch[er(r) * 8 + k]; }
+  AD_HD uint8_t& latch(int r, int k) { return w.g_rlatch[er(r) * kLatches + k]; }
   AD_HD float& rtime(int r, int k) { return w.g_rtime[er(r) * 3 + k]; }
   AD_HD int32_t& rcount(int r, int k) { return w.g_rcount[er(r) * 6 + k]; }
   AD_HD float elapsed() const { return w.g_time[(size_t)e * 2]; }
@@ -294,6 +294,13 @@ struct ControlScan {
   int top_i[kMaxRobots][4];
   uint8_t intake[kMaxRobots], alliance[kMaxRobots], nearby[kMaxRobots];
   float yield[kMaxRobots][4];
+  // cluster collection of the scripted offense (set by control_robot)
+  uint8_t edge[kMaxRobots];      // collecting: trace the FUEL cloud's contour this tick
+  uint8_t approach[kMaxRobots];  // heading for the intake-strip approach pose
+  int cluster_count[kMaxRobots];
+  float cluster_center[kMaxRobots][2];
+  float boundary[kMaxRobots][2];  // intake right corner along the collect heading
+  float inward[kMaxRobots][2];    // density-weighted pull of the tracks (control_scan_cloud)
 };
 
 // Intake reference point (front-right intake corner plus a short momentum
@@ -411,8 +418,274 @@ AD_HD void control_scan_yields(G& g, int r, const ControlScan& cs_in, ControlSca
     for (int k = 0; k < 4; ++k) cs.yield[r][k] = y[k];
 }
 
-AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* possession,
-                         const ControlScan& cs) {
+
+// ---------------------------------------------------------------------------
+// Scripted offense collection (frc_defense/_tensor_3v3_actions.py:677-890,
+// frc_defense/_tensor_3v3_navigation.py:84-127).
+// ---------------------------------------------------------------------------
+AD_HD bool env_has_det_offense(const SimParams& sp) {
+  for (int r = 0; r < sp.R; ++r)
+    if (sp.mode[r] == MODE_DET && sp.role[r] == 0) return true;
+  return false;
+}
+
+// Each robot's closed raster route: kRasterPoints samples; the cursor is the
+// sample the robot was last nearest to.
+AD_HD const float* raster_point(const World& w, int r, int k) {
+  return w.raster_pts + ((size_t)r * kRasterPoints + k) * 2;
+}
+
+AD_HD int raster_nearest(const World& w, int r, int from, int count, float x, float y) {
+  int best_k = from;
+  float best = kInf;
+  for (int o = 0; o < count; ++o) {
+    const int k = (from + o) % kRasterPoints;
+    const float* q = raster_point(w, r, k);
+    const float d2 = sqr(q[0] - x) + sqr(q[1] - y);
+    if (d2 < best) {
+      best = d2;
+      best_k = k;
+    }
+  }
+  return best_k;
+}
+
+// Before target selection: a robot that was not sweeping re-anchors to the
+// nearest route sample, a sweeping one searches the next 33 samples.
+AD_HD void raster_prepare(G& g, int r) {
+  int32_t& c = g.w.c_raster[g.er(r)];
+  const float* p = g.ppose(r);
+  c = 1 + (c <= 0 ? raster_nearest(g.w, r, 0, kRasterPoints, p[0], p[1])
+                  : raster_nearest(g.w, r, (c - 1) % kRasterPoints, 33, p[0], p[1]));
+}
+
+// After the tick: a sweeping robot's cursor follows it; any other robot
+// re-anchors at its next decision.
+AD_HD void raster_finish(G& g, int r) {
+  int32_t& c = g.w.c_raster[g.er(r)];
+  if (g.latch(r, RL_RASTER_SWEEP) && c > 0) {
+    const float* p = g.ppose(r);
+    c = 1 + raster_nearest(g.w, r, (c - 1) % kRasterPoints, 33, p[0], p[1]);
+  } else {
+    c = 0;
+  }
+}
+
+// Route sample `raster_lookahead` ahead of the cursor and the route tangent there.
+AD_HD void raster_target(G& g, int r, float& tx, float& ty, float& dirx, float& diry) {
+  const int c = g.w.c_raster[g.er(r)] > 0 ? g.w.c_raster[g.er(r)] - 1 : 0;
+  const int k = (c + g.sp.raster_lookahead) % kRasterPoints;
+  const float* a = raster_point(g.w, r, k);
+  const float* b = raster_point(g.w, r, (k + 1) % kRasterPoints);
+  tx = a[0];
+  ty = a[1];
+  const float dx = b[0] - a[0], dy = b[1] - a[1];
+  const float n = fmaxf(sqrtf(dx * dx + dy * dy), 1e-6f);
+  dirx = dx / n;
+  diry = dy / n;
+}
+
+// Chassis pose that puts the selected ball in the front intake strip: short
+// of the ball on the approach line, or, for a ball in the robot's own depot,
+// the nearest reachable pose beside the depot's field side or open ends.
+AD_HD void approach_pose(G& g, int r, float fx, float fy, float fdx, float fdy, float& tx, float& ty) {
+  const SimParams& sp = g.sp;
+  const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
+  const float rad = robot_radius_of(L, W);
+  const float d = fmaxf(sqrtf(fdx * fdx + fdy * fdy), 1e-6f);
+  tx = clampf(fx - fdx / d * .45f, rad, sp.field_length - rad);
+  ty = clampf(fy - fdy / d * .45f, rad, sp.field_width - rad);
+  const int team = sp.team[r];
+  if (team >= sp.num_depots) return;
+  const Box& dp = sp.depots[team];
+  if (!(fabsf(fx - dp.cx) <= dp.hx && fabsf(fy - dp.cy) <= dp.hy)) return;
+  const float hl = L * .5f, hw = W * .5f;
+  const float xmin = hl, xmax = sp.field_length - hl, ymin = hw, ymax = sp.field_width - hw;
+  const float side_x = team == 0 ? dp.cx + dp.hx + hl - .20f : dp.cx - dp.hx - hl + .20f;
+  const float cand[3][2] = {{side_x, clampf(fy, ymin, ymax)},
+                            {clampf(fx, xmin, xmax), dp.cy - dp.hy - .015f - hw},
+                            {clampf(fx, xmin, xmax), dp.cy + dp.hy + .015f + hw}};
+  const float* p = g.ppose(r);
+  float best = kInf;
+  int best_k = -1;
+  for (int k = 0; k < 3; ++k) {
+    const float ox = fabsf(fx - cand[k][0]), oy = fabsf(fy - cand[k][1]);
+    const float along = k == 0 ? ox : oy, across = k == 0 ? oy : ox;
+    const bool reachable = along <= hl + .35f + .083f && across <= hw + .075f + .083f && cand[k][0] >= xmin &&
+                           cand[k][0] <= xmax && cand[k][1] >= ymin && cand[k][1] <= ymax;
+    const float dist = sqrtf(sqr(cand[k][0] - p[0]) + sqr(cand[k][1] - p[1]));
+    if (reachable && dist < best) {
+      best = dist;
+      best_k = k;
+    }
+  }
+  if (best_k >= 0) {
+    tx = cand[best_k][0];
+    ty = cand[best_k][1];
+  }
+}
+
+// Cluster collection state machine of a scripted robot (targets for target-
+// based collection, the intake-strip approach, search targets). Robots that
+// collect inside a cluster are marked for contour tracing (cs.edge).
+AD_HD void collection_targets(G& g, int r, int action, int poss, bool no_track_search, bool alliance_fuel,
+                              const bool* cand_valid, const int* cand, float irx, float iry, float fx, float fy,
+                              float& fdx, float& fdy, float& tx, float& ty, ControlScan& cs) {
+  World& w = g.w;
+  const SimParams& sp = g.sp;
+  const size_t er = g.er(r);
+  const float* p = g.ppose(r);
+  const int team = sp.team[r];
+  const bool det_offense = sp.mode[r] == MODE_DET && sp.role[r] == 0;
+  const bool tbc = det_offense && (action < 4 || (action == 6 && poss == 0));
+  // the pickup candidates near the intake form a cluster
+  int count = 0;
+  float nearest = kInf, ccx = 0.f, ccy = 0.f;
+  for (int k = 0; k < 4; ++k) {
+    if (!cand_valid[k]) continue;
+    const float x = g.tx(r, cand[k]), y = g.ty(r, cand[k]);
+    const float ld = sqrtf(sqr(x - irx) + sqr(y - iry));
+    nearest = fminf(nearest, ld);
+    if (ld < 1.7f) {
+      ++count;
+      ccx += x;
+      ccy += y;
+    }
+  }
+  ccx /= (float)(count > 1 ? count : 1);
+  ccy /= (float)(count > 1 ? count : 1);
+  bool depot_target = false;
+  for (int k = 0; k < sp.num_depots; ++k)
+    depot_target = depot_target || (fabsf(fx - sp.depots[k].cx) <= sp.depots[k].hx &&
+                                    fabsf(fy - sp.depots[k].cy) <= sp.depots[k].hy);
+  const float herr = fabsf(angle_diff(atan2f(fdy, fdx), p[2]));
+  const bool depot_ready = sqrtf(fdx * fdx + fdy * fdy) <= 1.15f && herr <= .35f;
+  const bool at_cluster = count >= 2 && nearest <= 1.25f && (!depot_target || depot_ready);
+  const bool current_cluster = count >= 2 && nearest <= 2.4f;
+  uint8_t& collecting_latch = g.latch(r, RL_TARGET_COLLECTING);
+  int32_t& empty = w.c_empty_ticks[er];
+  const bool was = collecting_latch != 0;
+  const int empty_next = (was && !current_cluster) ? empty + 1 : 0;
+  int grace = (int)ceilf(.4f / sp.dt);
+  grace = grace < 1 ? 1 : grace;
+  bool next = was ? empty_next < grace : at_cluster;
+  next = next && tbc;
+  if (next && !was) {
+    // enter on the line to the selected ball
+    const float td = sqrtf(fdx * fdx + fdy * fdy);
+    w.c_collect_heading[er] = td > .1f ? atan2f(fdy, fdx) : p[2];
+  }
+  collecting_latch = next ? 1 : 0;
+  empty = empty_next;
+  // search: the raster route while no track is known, else the ferry lane
+  const bool positioned = in_alliance_zone(sp, team, p[0]) && g.hub_active(team);
+  const bool no_alliance_fuel_search = positioned && !alliance_fuel && poss > 0;
+  if (tbc && !next && action == 6 && !no_alliance_fuel_search) {
+    if (no_track_search) {
+      float dx, dy;
+      raster_target(g, r, tx, ty, dx, dy);
+    } else {
+      ferry_target(g, r, tx, ty);
+    }
+  }
+  if (no_alliance_fuel_search) ferry_target(g, r, tx, ty);
+  // contour tracing inputs
+  if (next) {
+    const float course = w.c_collect_heading[er];
+    const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
+    const float fwx = cosf(course), fwy = sinf(course);
+    cs.edge[r] = 1;
+    cs.boundary[r][0] = p[0] + fwx * (L * .5f + .15f) + fwy * (W * .5f);
+    cs.boundary[r][1] = p[1] + fwy * (L * .5f + .15f) - fwx * (W * .5f);
+    cs.cluster_count[r] = count;
+    cs.cluster_center[r][0] = ccx;
+    cs.cluster_center[r][1] = ccy;
+  }
+  // approach pose for a ball outside a cluster (or a depot ball not lined up)
+  if (tbc && action < 4 && (!next || (depot_target && !depot_ready))) {
+    approach_pose(g, r, fx, fy, fdx, fdy, tx, ty);
+    cs.approach[r] = 1;
+  }
+}
+
+// Density-weighted pull of the live eligible tracks on the intake's boundary
+// corner (Gaussian kernel of max(1.5 W, 0.7 m), fading with track age), one
+// warp per robot.
+AD_HD void control_scan_cloud(G& g, int r, ControlScan& cs, int lane, int nlanes) {
+  World& w = g.w;
+  const SimParams& sp = g.sp;
+  const int team = sp.team[r];
+  const bool hub_on = g.hub_active(team);
+  const float W = g.param(r, RP_WIDTH);
+  const float sigma = fmaxf(W * 1.5f, .7f);
+  const float bx = cs.boundary[r][0], by = cs.boundary[r][1];
+  float sx = 0.f, sy = 0.f;
+  for (int j = lane; j < sp.P; j += nlanes) {
+    const size_t k = g.erp(r, j);
+    if (!w.t_mask[k] || !(w.t_age[k] <= sp.track_timeout)) continue;
+    const float x = g.tx(r, j), y = g.ty(r, j);
+    if (!hub_on && in_alliance_zone(sp, team, x)) continue;  // scripted offense: inactive-HUB rule
+    const float dx = x - bx, dy = y - by;
+    const float dist = sqrtf(dx * dx + dy * dy);
+    const float wt = expf(-.5f * sqr(dist / sigma)) * expf(-fmaxf(w.t_age[k], 0.f) * .2f);
+    sx += dx * wt;
+    sy += dy * wt;
+  }
+#if defined(__CUDA_ARCH__)
+  if (nlanes > 1)
+    for (int o = 16; o > 0; o >>= 1) {
+      sx += __shfl_xor_sync(0xffffffffu, sx, o);
+      sy += __shfl_xor_sync(0xffffffffu, sy, o);
+    }
+#endif
+  if (lane == 0) {
+    cs.inward[r][0] = sx;
+    cs.inward[r][1] = sy;
+  }
+}
+
+// Contour tracing: keep the cluster on the intake's right side, turning the
+// collect heading toward the local edge tangent at most half the chassis
+// turn rate; the target is 3 m along the new heading while that stays inside
+// the field.
+AD_HD void control_edge_finish(G& g, int r, const ControlScan& cs) {
+  if (!cs.edge[r]) return;
+  World& w = g.w;
+  const SimParams& sp = g.sp;
+  const size_t er = g.er(r);
+  const float* p = g.ppose(r);
+  const float course = w.c_collect_heading[er];
+  const float fwx = cosf(course), fwy = sinf(course);
+  const float ix = cs.inward[r][0], iy = cs.inward[r][1];
+  const float in_n = sqrtf(ix * ix + iy * iy);
+  const bool grad_valid = in_n > .15f;
+  const float cx = cs.cluster_center[r][0] - cs.boundary[r][0], cy = cs.cluster_center[r][1] - cs.boundary[r][1];
+  const float c_n = sqrtf(cx * cx + cy * cy);
+  const bool center_valid = cs.cluster_count[r] >= 2 && c_n > .15f;
+  if (!(grad_valid || center_valid)) return;
+  const float nx = grad_valid ? ix / fmaxf(in_n, 1e-6f) : cx / fmaxf(c_n, 1e-6f);
+  const float ny = grad_valid ? iy / fmaxf(in_n, 1e-6f) : cy / fmaxf(c_n, 1e-6f);
+  float tnx = -ny, tny = nx;
+  if (tnx * fwx + tny * fwy < 0.f) {
+    tnx = -tnx;
+    tny = -tny;
+  }
+  const float turn = g.param(r, RP_OMEGA) * .5f * sp.dt;
+  const float next_course = course + clampf(angle_diff(atan2f(tny, tnx), course), -turn, turn);
+  const float tfx = cosf(next_course), tfy = sinf(next_course);
+  const float rad = robot_radius_of(g.param(r, RP_LENGTH), g.param(r, RP_WIDTH));
+  const float gx = p[0] + tfx * 3.f, gy = p[1] + tfy * 3.f;
+  if (!(gx >= rad && gx <= sp.field_length - rad && gy >= rad && gy <= sp.field_width - rad)) return;
+  w.c_collect_heading[er] = next_course;
+  if (!cs.approach[r]) {
+    w.c_target[er * 2] = gx;
+    w.c_target[er * 2 + 1] = gy;
+  }
+  w.c_fuel_delta[er * 2] = tfx;
+  w.c_fuel_delta[er * 2 + 1] = tfy;
+}
+
+AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* possession, ControlScan& cs) {
   World& w = g.w;
   const SimParams& sp = g.sp;
   const int e = g.e;
@@ -574,12 +847,6 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
   if (action < 4) {
     tx = fx;
     ty = fy;
-    if (target_based) {
-      // stop the chassis centre short of the ball so it ends in the intake strip
-      float d = fmaxf(sqrtf(fdx * fdx + fdy * fdy), 1e-6f);
-      tx = clampf(fx - fdx / d * .45f, rad, sp.field_length - rad);
-      ty = clampf(fy - fdy / d * .45f, rad, sp.field_width - rad);
-    }
   } else if (action == 4) {
     safe_score_target(g, r, tx, ty);
   } else if (action == 5) {
@@ -614,6 +881,22 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
     tx = dumper_ferry ? p[0] : ftx;
     ty = dumper_ferry ? p[1] : fty;
   }
+  // scripted offense collection: raster sweep, or cluster collection with
+  // contour tracing and intake-strip approach poses
+  bool raster_sweep = det_offense && no_track_search;
+  cs.edge[r] = 0;
+  cs.approach[r] = 0;
+  if (sp.sweeping) {
+    const bool sweeping = det_offense && (action < 4 || (action == 6 && poss == 0));
+    if (sweeping) {
+      raster_target(g, r, tx, ty, fdx, fdy);
+      raster_sweep = true;
+    }
+  } else if (env_has_det_offense(sp)) {
+    collection_targets(g, r, action, poss, no_track_search, alliance_fuel, cand_valid, top.i, irx, iry, fx, fy,
+                       fdx, fdy, tx, ty, cs);
+  }
+  g.latch(r, RL_RASTER_SWEEP) = raster_sweep ? 1 : 0;
   if (sp.R == 2 && r == 1 && mode == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
     // scripted two-robot attacker variants steer straight at a derived point
     // (frc_defense/tensor_defense_step.py:108-180)
@@ -884,7 +1167,7 @@ AD_HD void synthesize_commands(G& g, const int32_t* possession) {
       float ferr2 = fabsf(angle_diff(atan2f(pfy, pfx), p[2]));
       float turn_dist = speed * ferr2 / fmaxf(omega_lim, .1f);
       float approach = fmaxf(.9f, turn_dist);
-      if (!w.g_rlatch[er * 8 + RL_TARGET_COLLECTING] && pfd <= approach) {
+      if (!w.g_rlatch[er * kLatches + RL_TARGET_COLLECTING] && pfd <= approach) {
         tbx = fd[0];
         tby = fd[1];
       }
@@ -978,7 +1261,7 @@ AD_HD void synthesize_commands(G& g, const int32_t* possession) {
     const size_t er = g.er(r);
     const float* p = g.ppose(r);
     if (sp.mode[r] == MODE_DIRECT) continue;  // command supplied by the caller
-    if (w.g_rlatch[er * 8 + RL_SPARE]) {       // parked (static) opponent this episode
+    if (w.g_rlatch[er * kLatches + RL_STATIC_OPPONENT]) {       // parked (static) opponent this episode
       float* out = w.c_command + er * 3;
       out[0] = out[1] = out[2] = 0.f;
       continue;

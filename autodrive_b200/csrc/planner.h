@@ -324,7 +324,7 @@ AD_HD PlanRequest make_plan_request(World& w, const SimParams& sp, int e, int r)
   q.gx = w.c_target[g.er(r) * 2];
   q.gy = w.c_target[g.er(r) * 2 + 1];
   q.heading = p[2];
-  bool extended = sp.kind[r] == 1 || w.g_rlatch[g.er(r) * 8 + RL_INTAKE_COLLECTING];
+  bool extended = sp.kind[r] == 1 || w.g_rlatch[g.er(r) * kLatches + RL_INTAKE_COLLECTING];
   q.length = g.param(r, RP_LENGTH) + (extended ? .6096f : 0.f);
   q.width = g.param(r, RP_WIDTH);
   q.speed = g.param(r, RP_SPEED);

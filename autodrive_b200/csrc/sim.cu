@@ -52,6 +52,9 @@ AD_HD void control_env(World& w, const SimParams& sp, int e, const int32_t* acti
                         ControlScan& cs) {
   count_possession(w, sp, e, poss);
   G g{w, sp, e};
+  PAR_FOR(r, sp.R) {
+    if (sp.mode[r] == MODE_DET && sp.role[r] == 0) raster_prepare(g, r);
+  }
 #if defined(__CUDA_ARCH__)
   {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -71,6 +74,22 @@ AD_HD void control_env(World& w, const SimParams& sp, int e, const int32_t* acti
 #endif
   PAR_FOR(r, sp.R) {
     if (sp.mode[r] != MODE_NONE) control_robot(g, r, actions, poss, cs);
+  }
+  BARRIER();
+  // contour tracing of the robots that collect inside a cluster
+#if defined(__CUDA_ARCH__)
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int r = warp; r < sp.R; r += nw)
+      if (sp.mode[r] != MODE_NONE && cs.edge[r]) control_scan_cloud(g, r, cs, lane, 32);
+  }
+#else
+  for (int r = 0; r < sp.R; ++r)
+    if (sp.mode[r] != MODE_NONE && cs.edge[r]) control_scan_cloud(g, r, cs, 0, 1);
+#endif
+  BARRIER();
+  PAR_FOR(r, sp.R) {
+    if (sp.mode[r] != MODE_NONE) control_edge_finish(g, r, cs);
   }
   BARRIER();
   SERIAL_BEGIN
@@ -211,6 +230,7 @@ AD_HD void tick_env(World& w, const SimParams& sp, TickShared& s, int e, uint32_
     float th = est[2] + .5f * (prior[r * 3 + 2] + s.vel[r * 3 + 2]) * sp.dt;
     est[2] = atan2f(sinf(th), cosf(th));
     for (int k = 0; k < 3; ++k) pol[k] = est[k];
+    if (sp.mode[r] == MODE_DET && sp.role[r] == 0) raster_finish(g, r);
   }
   w.g_steps[(size_t)e * 2] += 1;
   update_match(w, sp, e);

@@ -23,6 +23,7 @@ constexpr int kMaxBoxes = 16;
 constexpr int kMaxBumps = 4;
 constexpr int kObsDim = 137;
 constexpr int kNumRobotParams = 14;
+constexpr int kRasterPoints = 256;   // samples of each robot's closed raster route
 
 // Robot parameter columns in r_param.
 enum RobotParam : int {
@@ -46,10 +47,12 @@ enum RobotCount : int {
 // Per-robot game timers [N][R][3].
 enum RobotTimer : int { RT_NEXT_INTAKE = 0, RT_NEXT_SCORE, RT_NEXT_FERRY };
 
-// Per-robot latches [N][R][8].
+// Per-robot latches [N][R][kLatches].
+constexpr int kLatches = 16;
 enum RobotLatch : int {
   RL_FERRY_COMMITTED = 0, RL_SCORE_COMMITTED, RL_LAST_HUB_ZONE, RL_INTAKE_COLLECTING,
-  RL_SCORE_INTENT, RL_TARGET_COLLECTING, RL_NO_TRACK_SEARCH, RL_SPARE,
+  RL_SCORE_INTENT, RL_TARGET_COLLECTING, RL_NO_TRACK_SEARCH, RL_STATIC_OPPONENT,
+  RL_RASTER_SWEEP,  // the raster cursor follows this robot after the tick
 };
 
 // dtype codes shared with Python.
@@ -88,7 +91,7 @@ enum DType : int { DT_F32 = 0, DT_I32 = 1, DT_U8 = 2, DT_I8 = 3, DT_F64 = 4 };
   X(g_first_inactive, int32_t, DT_I32, 1, N, 1, 1, 1)                   \
   X(g_rcount, int32_t, DT_I32, 3, N, R, 6, 1)                           \
   X(g_rtime, float, DT_F32, 3, N, R, 3, 1)                              \
-  X(g_rlatch, uint8_t, DT_U8, 3, N, R, 8, 1)                            \
+  X(g_rlatch, uint8_t, DT_U8, 3, N, R, 16, 1)                          \
   X(g_action, int32_t, DT_I32, 2, N, R, 1, 1)                           \
   X(g_reward, float, DT_F32, 2, N, R, 1, 1)                             \
   X(c_target, float, DT_F32, 3, N, R, 2, 1)                             \
@@ -97,6 +100,8 @@ enum DType : int { DT_F32 = 0, DT_I32 = 1, DT_U8 = 2, DT_I8 = 3, DT_F64 = 4 };
   X(c_target_index, int32_t, DT_I32, 2, N, R, 1, 1)                     \
   X(c_collect_heading, float, DT_F32, 2, N, R, 1, 1)                    \
   X(c_empty_ticks, int32_t, DT_I32, 2, N, R, 1, 1)                      \
+  X(c_raster, int32_t, DT_I32, 2, N, R, 1, 1)  /* raster cursor + 1; 0: re-anchor */ \
+  X(raster_pts, float, DT_F32, 3, R, S, 2, 1)                           \
   X(c_avoid, int32_t, DT_I32, 2, N, Q, 1, 1)                            \
   X(c_command, float, DT_F32, 3, N, R, 3, 1)                            \
   X(c_cand, int32_t, DT_I32, 3, N, R, 4, 1)                             \
@@ -184,6 +189,10 @@ struct SimParams {
   float perception_dropout = .02f, position_noise = .015f, velocity_noise = .05f;
   float track_timeout = 2.f, ball_diameter = .15f, stereo_baseline = .0635f;
   int stereo_tracks = 0;        // 1: anonymous stereo-cluster FUEL tracks; 0: per-piece tracks
+  int sweeping = 0;             // scripted offense collects along its raster route
+  int raster_lookahead = 20;    // raster route samples ahead of the cursor
+  int num_depots = 0;
+  Box depots[2];                // open-floor depot footprints (red, blue)
   int replan_interval = 20;
   int teammate_coordination = 0;
   int normalize_obs = 1;

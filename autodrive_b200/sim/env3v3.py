@@ -93,8 +93,6 @@ class TensorThreeVsThreeEnv:
             raise ValueError("turret_scoring_bps must be finite and positive")
         if behavior_probe is not None:
             raise ValueError("behavior probes are not supported by this simulator")
-        if sweeping_enabled:
-            raise ValueError("raster sweeping is not supported; use target-based collection")
         self.device = torch.device(device)
         self.dt, self.horizon = float(dt), int(horizon)
         self.field_length = float(field_length)
@@ -118,7 +116,7 @@ class TensorThreeVsThreeEnv:
         if teammate_coordination_enabled is None:
             teammate_coordination_enabled = teammate_intent_knowledge
         self.teammate_coordination_enabled = bool(teammate_coordination_enabled)
-        self.sweeping_enabled = False
+        self.sweeping_enabled = bool(sweeping_enabled)
         self.robot_fuel_capacity_values = tuple(
             int(turret_fuel_capacity if k == "turret" else max_fuel_capacity) for k in types)
         self.fuel_capacity = max(self.robot_fuel_capacity_values)
@@ -169,8 +167,14 @@ class TensorThreeVsThreeEnv:
             normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=float(planner_resolution), plan_nx=plan_nx, plan_ny=plan_ny,
             plan_sweeps=int(planner_sweeps), fuel_radius_rules=.0825, stereo_tracks=1,
+            sweeping=int(self.sweeping_enabled), raster_lookahead=20,
+            depots=[d.as_tensor() for d in sorted(fieldmod.depot_boxes(self.field_boxes),
+                                                   key=lambda b: b.alliance != "red")],
         )
         self.ws = WorldState(params, self.device)
+        self.raster_sweep_points = torch.tensor(self._raster_route_points(), device=self.device,
+                                                dtype=torch.float32)
+        self.ws["raster_pts"].copy_(self.raster_sweep_points)
         self.sim = RobotView(self.ws, dt=self.dt, field_length=field_length, field_width=field_width,
                              team_ids=TEAM_IDS, boxes=[b.as_tensor() for b in solids],
                              bumps=[b.as_tensor() for b in bumps], swerve=self.swerve, base=base,
@@ -234,6 +238,62 @@ class TensorThreeVsThreeEnv:
     @property
     def planner(self):
         return PlannerView(self.ws)
+
+    # ------------------------------------------------------------ raster route
+    def _raster_route_points(self, samples: int = 256):
+        """Closed raster route of every robot, `samples` points evenly spaced by
+        arc length (frc_defense/_tensor_3v3_navigation.py:13-82).
+
+        Each alliance sweeps its own half of the neutral zone: two passes that
+        span almost the whole field height (0.65 m from the walls) joined by
+        cubic Bezier U-turns of radius 0.32 m whose control points overshoot
+        the turn line by 0.55 radius, densified at 0.10 m on the passes and
+        0.04 m on the turns before resampling.
+        """
+        width, length = self.field_width, self.field_length
+        y_lo, y_hi, turn = .65, width - .65, .32
+        x_near = self.alliance_zone_depth + .55
+        x_far = length * .5 - .35
+        routes = []
+        for team in TEAM_IDS:
+            if team == 0:
+                xa, xb = x_near + turn, x_far - turn
+            else:
+                xa, xb = length - x_near - turn, length - x_far + turn
+            pts = []
+
+            def segment(a, b):
+                n = max(2, math.ceil(math.dist(a, b) / .10))
+                pts.extend((a[0] + (b[0] - a[0]) * k / n, a[1] + (b[1] - a[1]) * k / n) for k in range(n))
+
+            def u_turn(a, c1, c2, b):
+                n = max(8, math.ceil(math.dist(a, b) / .04))
+                for k in range(n):
+                    t = k / n
+                    u = 1. - t
+                    w = (u * u * u, 3. * u * u * t, 3. * u * t * t, t * t * t)
+                    pts.append(tuple(w[0] * a[i] + w[1] * c1[i] + w[2] * c2[i] + w[3] * b[i] for i in (0, 1)))
+
+            top_a, top_b = (xa, y_hi - turn), (xb, y_hi - turn)
+            bot_a, bot_b = (xb, y_lo + turn), (xa, y_lo + turn)
+            segment((xa, y_lo + turn), top_a)
+            u_turn(top_a, (xa, y_hi + .55 * turn), (xb, y_hi + .55 * turn), top_b)
+            segment(top_b, bot_a)
+            u_turn(bot_a, (xb, y_lo - .55 * turn), (xa, y_lo - .55 * turn), bot_b)
+            pts.append(pts[0])
+            arc = [0.]
+            for a, b in zip(pts, pts[1:]):
+                arc.append(arc[-1] + math.dist(a, b))
+            route, seg = [], 0
+            for k in range(samples):
+                s = arc[-1] * k / samples
+                while seg + 1 < len(arc) - 1 and arc[seg + 1] < s:
+                    seg += 1
+                f = (s - arc[seg]) / max(arc[seg + 1] - arc[seg], 1e-9)
+                a, b = pts[seg], pts[seg + 1]
+                route.append((a[0] + (b[0] - a[0]) * f, a[1] + (b[1] - a[1]) * f))
+            routes.append(route)
+        return routes
 
     # ------------------------------------------------------------ fuel layout
     def _initial_fuel_layout(self):
@@ -321,7 +381,7 @@ class TensorThreeVsThreeEnv:
         ws["g_steps"][:, 1].masked_fill_(m, self.replan_interval - 1)
         ws["g_hub"].masked_fill_(m[:, None], 1)
         for name in ("g_scores", "g_rcount", "g_rtime", "g_rlatch", "g_reward", "c_target",
-                     "c_fuel_target", "c_fuel_delta", "c_command", "c_empty_ticks", "t_pos", "t_vel",
+                     "c_fuel_target", "c_fuel_delta", "c_command", "c_empty_ticks", "c_raster", "t_pos", "t_vel",
                      "t_conf", "t_quality", "t_mask", "t_spatial", "t_angular", "t_merged", "t_visible",
                      "o_pose", "o_vel", "o_size", "o_valid", "p_path", "p_profile", "p_len", "p_goal", "p_start", "p_progress", "p_trench"):
             t = ws[name]
