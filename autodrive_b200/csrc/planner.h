@@ -5,7 +5,10 @@
 // chassis inflation, blocked start/goal projection to a nearby free cell,
 // 8-connected cost-to-go by Jacobi Bellman sweeps with corner cutting blocked
 // and a bump traversal penalty, greedy descent extraction (<= 72 points),
-// line-of-sight shortcutting and a curvature/braking speed profile.
+// PathPlanner line-of-sight simplification with cubic Bezier corner smoothing
+// (tensor_adstar.py:772-1037; handles shortened until the curve stays on free
+// cells), equal-arc resampling to 72 points and a curvature/braking speed
+// profile.
 //
 // On the GPU one CTA owns one route with the whole grid (occupancy + two value
 // buffers) in shared memory; the Bellman sweeps run until a sweep changes no
@@ -49,6 +52,95 @@ AD_HD bool grid_line_clear(const SimParams& sp, const uint8_t* blocked, float x0
     if (blocked[cell_index(sp, ix, iy)]) return false;
   }
   return true;
+}
+
+
+AD_HD bool grid_point_blocked(const SimParams& sp, const uint8_t* blocked, float x, float y) {
+  const int ix = clampi((int)floorf(x / sp.plan_res), 0, sp.plan_nx - 1);
+  const int iy = clampi((int)floorf(y / sp.plan_res), 0, sp.plan_ny - 1);
+  return blocked[cell_index(sp, ix, iy)] != 0;
+}
+
+// Resample the n-point chain pt(0..n-1) to kPathPoints points evenly spaced by
+// arc length (the segment after a station on ties); returns whether every
+// resampled point lies on a free cell.
+template <typename PointFn>
+AD_HD bool resample_route(const SimParams& sp, const uint8_t* blocked, int n, PointFn pt, float* out) {
+  float total = 0.f, ax, ay, bx, by;
+  pt(0, ax, ay);
+  for (int k = 1; k < n; ++k) {
+    pt(k, bx, by);
+    total += sqrtf(sqr(bx - ax) + sqr(by - ay));
+    ax = bx;
+    ay = by;
+  }
+  pt(0, ax, ay);
+  int k = n > 1 ? 1 : 0;
+  pt(k, bx, by);
+  float sa = 0.f, sb = sqrtf(sqr(bx - ax) + sqr(by - ay));
+  bool clear = true;
+  for (int q = 0; q < kPathPoints; ++q) {
+    const float target = total * (float)q / (float)(kPathPoints - 1);
+    while (k < n - 1 && sb <= target) {
+      ax = bx;
+      ay = by;
+      sa = sb;
+      pt(++k, bx, by);
+      sb += sqrtf(sqr(bx - ax) + sqr(by - ay));
+    }
+    const float f = clampf((target - sa) / fmaxf(sb - sa, 1e-8f), 0.f, 1.f);
+    out[q * 2] = ax + (bx - ax) * f;
+    out[q * 2 + 1] = ay + (by - ay) * f;
+    clear = clear && !grid_point_blocked(sp, blocked, out[q * 2], out[q * 2 + 1]);
+  }
+  return clear;
+}
+
+// PathPlanner-style corner poses of the simplified polyline s[0..m-1]: the
+// start, for every corner an incoming pose 80 % along the incoming leg and an
+// outgoing pose 20 % along the outgoing leg (each with its leg's heading),
+// and the end; 2m - 2 poses. (ux, uy) is the unit heading (+x for a
+// zero-length leg).
+AD_HD void corner_pose(const float* s, int m, int k, float& x, float& y, float& ux, float& uy) {
+  const int count = 2 * m - 2;
+  int a, b;
+  float f;
+  if (k == 0) {
+    a = 0, b = 1, f = 0.f;
+  } else if (k >= count - 1) {
+    a = m - 2, b = m - 1, f = 1.f;
+  } else {
+    const int c = (k + 1) / 2;
+    if (k & 1) a = c - 1, b = c, f = .8f;
+    else a = c, b = c + 1, f = .2f;
+  }
+  const float dx = s[b * 2] - s[a * 2], dy = s[b * 2 + 1] - s[a * 2 + 1];
+  x = s[a * 2] + f * dx;
+  y = s[a * 2 + 1] + f * dy;
+  const float n = sqrtf(dx * dx + dy * dy);
+  ux = n > 0.f ? dx / n : 1.f;
+  uy = n > 0.f ? dy / n : 0.f;
+}
+
+// Point idx of the sampled cubic Bezier chain through the corner poses (pose
+// 0, then 8 samples per segment, t = 1/8 .. 1), handles `factor` x segment
+// length along the pose headings.
+AD_HD void bezier_chain_point(const float* s, int m, float factor, int idx, float& x, float& y) {
+  float x0, y0, ux0, uy0, x3, y3, ux3, uy3;
+  if (idx == 0) {
+    corner_pose(s, m, 0, x, y, ux0, uy0);
+    return;
+  }
+  const int seg = (idx - 1) / 8, j = (idx - 1) % 8 + 1;
+  corner_pose(s, m, seg, x0, y0, ux0, uy0);
+  corner_pose(s, m, seg + 1, x3, y3, ux3, uy3);
+  const float d = sqrtf(sqr(x3 - x0) + sqr(y3 - y0)) * factor;
+  const float x1 = x0 + ux0 * d, y1 = y0 + uy0 * d;
+  const float x2 = x3 - ux3 * d, y2 = y3 - uy3 * d;
+  const float t = (float)j / 8.f, u = 1.f - t;
+  const float w0 = u * u * u, w1 = 3.f * u * u * t, w2 = 3.f * u * t * t, w3 = t * t * t;
+  x = w0 * x0 + w1 * x1 + w2 * x2 + w3 * x3;
+  y = w0 * y0 + w1 * y1 + w2 * y2 + w3 * y3;
 }
 
 struct PlanRequest {
@@ -221,58 +313,60 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     ps.path[(len - 1) * 2] = ps.tmp[0];
     ps.path[(len - 1) * 2 + 1] = ps.tmp[1];
   }
-  // line-of-sight shortcut: keep the farthest visible point from each anchor
-  int out = 0;
+  // line-of-sight simplification (PathPlanner): a lattice point is kept only
+  // when the last kept point cannot see the point after it
+  float* simp = ps.tmp + 4;  // [kPathPoints * 2]
+  int m = 1;
+  simp[0] = ps.path[0];
+  simp[1] = ps.path[1];
   if (len > 1) {
     int anchor = 0;
-    ps.tmp[2] = ps.path[0];
-    ps.tmp[3] = ps.path[1];
-    out = 1;
-    while (anchor < len - 1) {
-      int next = anchor + 1;
-      for (int k = len - 1; k > anchor + 1; --k) {
-        if (grid_line_clear(sp, ps.blocked, ps.path[anchor * 2], ps.path[anchor * 2 + 1], ps.path[k * 2],
-                            ps.path[k * 2 + 1])) {
-          next = k;
-          break;
-        }
+    for (int k = 1; k < len - 1; ++k) {
+      if (!grid_line_clear(sp, ps.blocked, ps.path[anchor * 2], ps.path[anchor * 2 + 1], ps.path[(k + 1) * 2],
+                           ps.path[(k + 1) * 2 + 1])) {
+        simp[m * 2] = ps.path[k * 2];
+        simp[m * 2 + 1] = ps.path[k * 2 + 1];
+        ++m;
+        anchor = k;
       }
-      ps.tmp[2 + out * 2] = ps.path[next * 2];
-      ps.tmp[2 + out * 2 + 1] = ps.path[next * 2 + 1];
-      out++;
-      anchor = next;
     }
-  } else {
-    ps.tmp[2] = ps.path[0];
-    ps.tmp[3] = ps.path[1];
-    out = 1;
+    simp[m * 2] = ps.path[(len - 1) * 2];
+    simp[m * 2 + 1] = ps.path[(len - 1) * 2 + 1];
+    ++m;
   }
-  // densify long segments so the follower sees curvature at corners only
+  // smoothed route: cubic Bezier corners with the longest handle (0.4, 0.28,
+  // 0.18, 0.1, 0 x segment length) whose samples and kPathPoints-point
+  // equal-arc resampling stay on free cells; else the simplified polyline,
+  // else the lattice route, each resampled the same way
   float* dst = w.p_path + er * kPathPoints * 2;
-  int n = 0;
-  for (int k = 0; k < out && n < kPathPoints; ++k) {
-    if (k > 0) {
-      float ax = ps.tmp[2 + (k - 1) * 2], ay = ps.tmp[2 + (k - 1) * 2 + 1];
-      float bx = ps.tmp[2 + k * 2], by = ps.tmp[2 + k * 2 + 1];
-      float seg = sqrtf(sqr(bx - ax) + sqr(by - ay));
-      int pieces = (int)ceilf(seg / (2.f * sp.plan_res));
-      for (int m = 1; m < pieces && n < kPathPoints - 1; ++m) {
-        float f = (float)m / (float)pieces;
-        dst[n * 2] = ax + (bx - ax) * f;
-        dst[n * 2 + 1] = ay + (by - ay) * f;
-        n++;
+  if (len > 1) {
+    const float* src = ps.path;
+    auto lattice = [&](int k, float& x, float& y) { x = src[k * 2]; y = src[k * 2 + 1]; };
+    auto polyline = [&](int k, float& x, float& y) { x = simp[k * 2]; y = simp[k * 2 + 1]; };
+    bool done = false;
+    const float factors[5] = {.4f, .28f, .18f, .1f, 0.f};
+    const int samples = 1 + (2 * m - 3) * 8;
+    for (int fi = 0; fi < 5 && !done; ++fi) {
+      const float factor = factors[fi];
+      auto curve = [&](int k, float& x, float& y) { bezier_chain_point(simp, m, factor, k, x, y); };
+      bool clear = true;
+      for (int k = 0; k < samples && clear; ++k) {
+        float x, y;
+        curve(k, x, y);
+        clear = !grid_point_blocked(sp, ps.blocked, x, y);
       }
+      if (clear) done = resample_route(sp, ps.blocked, samples, curve, dst);
     }
-    dst[n * 2] = ps.tmp[2 + k * 2];
-    dst[n * 2 + 1] = ps.tmp[2 + k * 2 + 1];
-    n++;
-  }
-  for (int k = n; k < kPathPoints; ++k) {
-    dst[k * 2] = dst[(n - 1) * 2];
-    dst[k * 2 + 1] = dst[(n - 1) * 2 + 1];
+    if (!done) done = resample_route(sp, ps.blocked, m, polyline, dst);
+    if (!done) resample_route(sp, ps.blocked, len, lattice, dst);
+  } else {
+    for (int k = 0; k < kPathPoints; ++k) {
+      dst[k * 2] = ps.path[0];
+      dst[k * 2 + 1] = ps.path[1];
+    }
   }
   // a one-cell route from start==goal still counts as a single point
-  w.p_len[er] = len > 1 ? n : 1;
+  w.p_len[er] = len > 1 ? kPathPoints : 1;
   // speed profile: curvature caps then backward braking envelope
   float* prof = w.p_profile + er * kPathPoints;
   const float mu = fmaxf(q.lat_mu, .1f), acc = fmaxf(q.accel, .2f), vcap = fmaxf(q.speed, .1f);
