@@ -1,0 +1,2 @@
+"""Compatibility import path: ``frc_defense.meco_diagnostic_monitor`` -> ``autodrive_b200.meco.adapter``."""
+from autodrive_b200.meco.adapter import *  # noqa: F401,F403
