@@ -469,7 +469,11 @@ void step(CommHandle& h, torch::Tensor m, torch::Tensor v, torch::Tensor norm_ou
     float* sc = c.scratch;
     void* args[] = {&c.P, &world, &rank, &npad, &sc, &mp, &vp, &epoch, &lr_f, &b1_f, &b2_f, &eps_f, &wd_f,
                     &bias1, &bias2, &mn, &np, &sp, &iters};
-    err = cudaLaunchCooperativeKernel((void*)oneshot_allreduce_adam_kernel, dim3(c.grid), dim3(kThreads), args, 0, st);
+    // latency-bound: about two float4 per thread, so the grid-wide syncs span
+    // only the CTAs that have work
+    const int64_t want = (npad / 4 + 2 * kThreads - 1) / (2 * kThreads);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(c.grid, want));
+    err = cudaLaunchCooperativeKernel((void*)oneshot_allreduce_adam_kernel, dim3(grid), dim3(kThreads), args, 0, st);
   } else {
     void* args[] = {&c.P, &world, &rank, &npad, &mp, &vp, &epoch, &lr_f, &b1_f, &b2_f, &eps_f, &wd_f,
                     &bias1, &bias2, &mn, &np, &sp, &iters};
