@@ -164,12 +164,12 @@ def run_train(args, rank, world, local):
     e2e_ticks = args.envs * (state["ticks"] - t0) * world
     decisions_ticks = ticks_timed / max(1, args.steps)
     minibatches = args.epochs * args.minibatches
-    # own kernels per step: control+plan+tick per tick, observe + policy act per decision, the
+    # own kernels per step: control+plan+tick+sense per tick, observe + policy act per decision, the
     # bootstrap value, GAE, and per minibatch either (adv stats, fused fwd+bwd, partial reduce,
     # sum-of-squares, Adam, weight pack) on the tensor-core path or (sum-of-squares, Adam)
     per_mb = 6 if learner.tc is not None else 2
     per_decision = 2 if learner.tc is not None else 1
-    launches = int(args.steps * (decisions_ticks * 3 + per_decision * args.decisions + 2 + per_mb * minibatches))
+    launches = int(args.steps * (decisions_ticks * 4 + per_decision * args.decisions + 2 + per_mb * minibatches))
     return {
         "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -234,7 +234,7 @@ def run_sim(args, rank, world, local):
         "clocks": clocks.summary(),
         "e2e": {"value": env_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
                 "h2d_bytes_per_step": host_actions.numel() * 4, "d2h_bytes_per_step": host_rewards.numel() * 4},
-        "gpu_launches": (ticks * 3 + 1) * args.steps,
+        "gpu_launches": (ticks * 4 + 1) * args.steps,
     }
 
 
