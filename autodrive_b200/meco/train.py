@@ -427,7 +427,8 @@ def main(argv=None) -> int:
     elif args.command == "evaluate":
         policy = None
         if args.checkpoint:
-            payload = torch.load(args.checkpoint, map_location=args.device, weights_only=False)
+            from ..utils.checkpoint import load_verified
+            payload = load_verified(args.checkpoint, map_location=args.device, weights_only=False)
             policy = MecoPolicy(payload["track"]).to(args.device)
             policy.load_state_dict(payload["model_state_dict"])
             policy.eval()

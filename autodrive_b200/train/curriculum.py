@@ -595,7 +595,8 @@ def evaluate_curriculum(policy_or_checkpoint, scenario_ids, *, episodes: int, sp
 
 
 def load_checkpoint(path, *, config: TrainingConfig | None = None, device="cpu"):
-    payload = torch.load(path, map_location=device, weights_only=False)
+    from ..utils.checkpoint import load_verified
+    payload = load_verified(path, map_location=device, weights_only=False)
     if payload.get("curriculum_version") != CURRICULUM_VERSION:
         raise ValueError("checkpoint from another curriculum version")
     if config is not None and payload.get("config_identity") != config.identity():
@@ -631,7 +632,8 @@ def train_curriculum(config: TrainingConfig, *, resume: str | None = None) -> di
         model = sac
     start = 0
     if resume:
-        payload = torch.load(resume, map_location=dev, weights_only=False)
+        from ..utils.checkpoint import load_verified
+        payload = load_verified(resume, map_location=dev, weights_only=False)
         if payload.get("config_identity") != config.identity():
             raise ValueError("checkpoint configuration does not match this run (strict resume)")
         model.load_state_dict(payload["model_state_dict"])

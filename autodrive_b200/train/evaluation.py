@@ -33,7 +33,8 @@ def wilson_interval(successes: int, total: int, z: float = 1.96) -> tuple[float,
 
 
 def load_policy(checkpoint, device):
-    payload = torch.load(checkpoint, map_location=device, weights_only=True)
+    from ..utils.checkpoint import load_verified
+    payload = load_verified(checkpoint, map_location=device)
     network = payload.get("network", "mlp")
     model = build_policy(network, int(payload["obs_dim"]), int(payload["action_dim"]), payload["action_kind"])
     model.load_state_dict(payload["model_state_dict"])

@@ -26,7 +26,8 @@ from .ppo import atomic_json, train_once
 
 
 def checkpoint_vector(path) -> torch.Tensor:
-    payload = torch.load(path, map_location="cpu", weights_only=True)
+    from ..utils.checkpoint import load_verified
+    payload = load_verified(path)
     return torch.cat([v.detach().float().reshape(-1) for v in payload["model_state_dict"].values()])
 
 

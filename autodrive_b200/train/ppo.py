@@ -299,7 +299,8 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
     action_kind = agents.action_kind
     initial_state = None
     if initial_checkpoint is not None:
-        payload = torch.load(initial_checkpoint, map_location=dev, weights_only=True)
+        from ..utils.checkpoint import load_verified
+        payload = load_verified(initial_checkpoint, map_location=dev)
         if payload.get("task") != "defense":
             raise ValueError("initial checkpoint must be tagged as a defense policy")
         if payload.get("drivetrain_config") != agents.drivetrain_config:
