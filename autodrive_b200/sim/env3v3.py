@@ -19,6 +19,7 @@ import math
 import torch
 
 from .. import field as fieldmod
+from ..utils import trace
 from .robots import RobotView, hub_line_spawn_poses
 from .world import FuelPhysicsConfig, SwerveParameters, WorldState, build_params, fuel_config
 
@@ -508,7 +509,8 @@ class TensorThreeVsThreeEnv:
                 entry = (graph, reward_buf)
                 self._graphs[key] = entry
             graph, reward_buf = entry
-            graph.replay()
+            with trace.stage("sim_interval"):
+                graph.replay()
             rewards = reward_buf
         else:
             rewards = torch.zeros((self.n, NUM_ROBOTS), device=self.device)

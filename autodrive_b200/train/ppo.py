@@ -25,6 +25,7 @@ import torch
 
 from ..models import build_policy
 from ..ops import policy_tc
+from ..utils import trace
 from ..parallel import dist as pdist
 from ..parallel.grad_sync import GradientSync, sync_parameters
 from .optim import FusedAdam
@@ -337,10 +338,12 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
             agents.env.opponent = kind
             _set_opponent(agents.env, OPPONENT_KINDS[kind])
         t0 = time.perf_counter()
-        buf, obs, ticks = collect_rollout(agents, learner, obs, rollout_steps, clock, episode_ticks)
+        with trace.stage("rollout"):
+            buf, obs, ticks = collect_rollout(agents, learner, obs, rollout_steps, clock, episode_ticks)
         stats = torch.zeros(3, dtype=torch.float64, device=dev)
-        adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
-                             buf["next_values"], gamma, gae_lambda, stats)
+        with trace.stage("gae"):
+            adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
+                                 buf["next_values"], gamma, gae_lambda, stats)
         flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim),
                 "actions": buf["actions"].reshape((-1, agents.action_dim) if action_kind == "continuous" else (-1,)),
                 "mask": buf["mask"].reshape(-1, agents.action_dim) if buf["mask"] is not None else None,
@@ -349,7 +352,8 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
         if action_kind == "categorical":
             action_counts += torch.bincount(flat["actions"], minlength=agents.action_dim).float()
         coef = entropy_coef * max(0., 1. - update / max(1, updates - 1))
-        upd = learner.update(flat, coef)
+        with trace.stage("update"):
+            upd = learner.update(flat, coef)
         counters = torch.tensor([float(rollout_steps * agents.n_agents), float(ticks * num_envs),
                                  float(buf["rewards"].sum().item()), float(upd["samples"]),
                                  float(upd["approx_kl_sum"].item()), float(upd["clip_fraction_sum"].item()),

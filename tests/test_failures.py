@@ -89,3 +89,12 @@ def test_rank_that_raises_mid_run_ends_its_peer(tmp_path):
     # the survivor gets an error from its next collective instead of hanging
     assert procs[0].returncode != 0
     assert "finished" not in outs[0][0]
+
+
+def test_trace_stages_are_noops_without_nvtx():
+    from autodrive_b200.utils import trace
+    trace.set_enabled(True)          # no CUDA here: still a no-op
+    with trace.stage("rollout"):
+        x = 1
+    trace.set_enabled(False)
+    assert x == 1 and not trace.enabled()
