@@ -28,7 +28,9 @@ def _events():
 def stages(args):
     from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
     dev = torch.device("cuda", 0)
-    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed, fuel_physics=not args.static)
+    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed, fuel_physics=not args.static,
+                                fuel_count=args.fuel_count, perception_interval=args.perception_interval,
+                                planner_resolution=args.planner_resolution)
     if args.threads:
         env.ws.sim.threads = args.threads
     sim = env.ws.sim
@@ -112,6 +114,8 @@ def fuel(args):
     dev = torch.device("cuda", 0)
     cfg = FuelPhysicsConfig(adaptive_substeps=False, substeps=10, broadphase="grid", contact_mode="fused",
                             solver="jacobi", sleep=True)
+    # (0.2 m grid cells: a 0.15 m grid would exceed the 4096-cell shared-memory
+    # grid; the broadphase is exact, so the cell size changes speed, not contacts)
     env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed, fuel_physics=cfg,
                                 fuel_count=max(args.pieces, 96))
     if args.threads:
@@ -164,6 +168,9 @@ def main():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--threads", type=int, default=0)
     p.add_argument("--static", action="store_true")
+    p.add_argument("--fuel-count", type=int, default=504, help="stages: FUEL pieces per world")
+    p.add_argument("--perception-interval", type=int, default=2, help="stages: ticks between sensor updates")
+    p.add_argument("--planner-resolution", type=float, default=.3, help="stages: planner grid cell (m)")
     p.add_argument("--phases", action="store_true", help="stages: also report the tick kernel's per-phase cycle shares")
     p.add_argument("--actions", choices=("held", "random"), default="held",
                    help="stages: default held actions, or random valid strategic actions every 12 ticks")

@@ -74,7 +74,7 @@ class TensorThreeVsThreeEnv:
                  behavior_probe_hub_active=True, random_gamepiece_placement=False,
                  field_length=16.54, field_width=8.07, obstacles=(), fuel_physics=True,
                  field_layout="2026_rebuilt", defer_initial_perception=False,
-                 planner_resolution=.3, planner_sweeps=72, swerve=None):
+                 planner_resolution=.3, planner_sweeps=None, swerve=None):
         self.n = int(num_envs)
         if self.n < 1:
             raise ValueError("num_envs must be positive")
@@ -167,7 +167,9 @@ class TensorThreeVsThreeEnv:
             teammate_coordination=int(self.teammate_coordination_enabled),
             normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=float(planner_resolution), plan_nx=plan_nx, plan_ny=plan_ny,
-            plan_sweeps=int(planner_sweeps), fuel_radius_rules=.0825, stereo_tracks=1,
+            plan_sweeps=int(planner_sweeps if planner_sweeps is not None else
+                            max(72, math.ceil(72 * .3 / planner_resolution - 1e-6))),
+            fuel_radius_rules=.0825, stereo_tracks=1,
             sweeping=int(self.sweeping_enabled), raster_lookahead=20,
             depots=[d.as_tensor() for d in sorted(fieldmod.depot_boxes(self.field_boxes),
                                                    key=lambda b: b.alliance != "red")],

@@ -79,13 +79,15 @@ def atomic_save(path: Path, value: dict) -> None:
 
 
 def make_env(kind: str, num_envs: int, device, seed: int, opponent: str, horizon: int,
-             architecture: str = "strategic_adstar", fuel_physics=True, static_opponent_fraction: float = 0.):
-    """Environment factory (frc_defense/tensor_training_runtime.py:156-178)."""
+             architecture: str = "strategic_adstar", fuel_physics=True, static_opponent_fraction: float = 0.,
+             **env_kwargs):
+    """Environment factory (frc_defense/tensor_training_runtime.py:156-178). Extra keywords go to
+    the 3v3 environment (FUEL count, perception interval, planner resolution, ...)."""
     if kind == "3v3":
         from ..sim.env3v3 import TensorThreeVsThreeEnv
         env = TensorThreeVsThreeEnv(num_envs=num_envs, device=device, seed=seed, horizon=horizon,
                                     control_modes=("deterministic",) * 3 + ("nn",) * 3,
-                                    fuel_physics=fuel_physics)
+                                    fuel_physics=fuel_physics, **env_kwargs)
         return ThreeVsThreeAgents(env)
     from ..sim.env_defense import TensorDefenseEnv
     mode = {"direct": "direct", "tactical_adstar": "tactical", "strategic_adstar": "strategic"}.get(

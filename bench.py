@@ -2,9 +2,10 @@
 
 Default workload (`--mode train`), one step = one PPO training iteration of
 the 3v3 defense configuration on every GPU:
-  * TensorThreeVsThreeEnv, 2048 worlds per GPU, fuel physics on (504 FUEL,
-    64 robot+FUEL substeps per 20 ms tick), perception every 2 ticks, route
-    replanning every 20 ticks, three scripted offense robots and three learned
+  * TensorThreeVsThreeEnv, 2048 worlds per GPU, fuel physics on (400 FUEL,
+    64 robot+FUEL substeps per 20 ms tick), stereo perception and strategic
+    observations every tick, route replanning every 20 ticks on the
+    reference's 0.3 m grid (56 x 27 cells), three scripted offense robots and three learned
     defenders sharing one 137->8 ActorCritic (random init, fp32);
   * a rollout of `--decisions` strategic decisions held 12/13 ticks each
     (4 Hz), the GAE kernel, then PPO with 4 epochs x 8 minibatches, gradient
@@ -36,6 +37,13 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "3v3 env-ticks/sec and PPO samples/sec, 1/2/4/8 B200, device-timed max over ranks"
+# The 3v3 full-match benchmark world: 400 FUEL, perception and strategic
+# observations every tick. Routes are planned on the 0.3 m grid (56 x 27)
+# that the reference's 3v3 environment always uses (it has no resolution
+# keyword), so both arms plan on the same grid; the finer 0.1 m grid is
+# available through `planner_resolution`. (The reference's own defaults are
+# 504 FUEL and perception every 2nd tick.)
+BENCH_ENV = {"fuel_count": 400, "perception_interval": 1, "planner_resolution": .3}
 
 
 def _dist_init():
@@ -89,7 +97,8 @@ def run_train(args, rank, world, local):
     from autodrive_b200.train.rollout import StrategicClock, gae_advantages
     from autodrive_b200.utils.clocks import ClockSampler
     dev = torch.device("cuda", local)
-    agents = make_env("3v3", args.envs, dev, args.seed + rank * 1_000_003, "offense", 8000, fuel_physics=True)
+    agents = make_env("3v3", args.envs, dev, args.seed + rank * 1_000_003, "offense", 8000, fuel_physics=True,
+                      **BENCH_ENV)
     samples = agents.n_agents * args.decisions
     cfg = PPOConfig(rollout_steps=args.decisions, epochs=args.epochs,
                     minibatch_size=samples // args.minibatches, grad_backend=args.grad_backend)
@@ -176,8 +185,9 @@ def run_train(args, rank, world, local):
         "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (random-init seeded REBUILT matches and policy; no external data)",
         "ppo_samples_per_s": samples_total / (ms / 1e3), "ppo_samples_per_step_per_gpu": samples,
-        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 504 FUEL, 64 substeps/tick) "
-                            "+ PPO on ActorCritic 137->128->128->8 for 3 learned defenders",
+        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 400 FUEL, 64 substeps/tick, "
+                            "perception every tick, 0.3 m planner grid 56x27 as in the reference, replan every 20 ticks) "
+                            "+ PPO on the strategic_adstar ActorCritic 137->128->128->8 for 3 learned defenders",
                    "global_batch": args.envs * world, "envs_per_gpu": args.envs,
                    "seq_len": args.decisions, "decisions_per_step": args.decisions,
                    "env_ticks_per_step_per_world": decisions_ticks, "ppo_epochs": args.epochs,
@@ -203,7 +213,7 @@ def run_sim(args, rank, world, local):
     from autodrive_b200.utils.clocks import ClockSampler
     dev = torch.device("cuda", local)
     env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed + rank,
-                                fuel_physics=True, horizon=8000)
+                                fuel_physics=True, horizon=8000, **BENCH_ENV)
     ticks = args.ticks_per_step
     actions = torch.full((args.envs, 6), 7, dtype=torch.int32, device=dev)
     for _ in range(args.warmup):
@@ -227,8 +237,9 @@ def run_sim(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (random-init seeded REBUILT matches, deterministic scripted controllers)",
-        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match, fuel physics on (504 FUEL, 64 substeps/tick), "
-                            "perception every 2 ticks, replan every 20 ticks, simulator only",
+        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match, fuel physics on (400 FUEL, 64 substeps/tick), "
+                            "perception every tick, 0.3 m planner grid 56x27 as in the reference, replan every 20 ticks, "
+                            "simulator only",
                    "global_batch": args.envs * world, "envs_per_gpu": args.envs, "seq_len": ticks,
                    "parallelism": f"env-batch x dp{world}", "l2": "working set > 126 MB L2 (no flush needed)"},
         "clocks": clocks.summary(),
@@ -253,7 +264,8 @@ def run_reference(args, rank, world, local):
     modes = ("deterministic",) * 3 + (("nn",) * 3 if args.mode == "train" else ("deterministic",) * 3)
     env = RefEnv(num_envs=calib, device=dev, seed=args.seed + rank, control_modes=modes,
                  robot_roles=("offense",) * 3 + ("defense",) * 3, horizon=8000, randomize=True,
-                 fuel_count=504, fused_sensor_rng=True, fuel_physics=True)
+                 fuel_count=BENCH_ENV["fuel_count"], perception_interval=BENCH_ENV["perception_interval"],
+                 fused_sensor_rng=True, fuel_physics=True)
     actions = torch.full((calib, 6), 7, dtype=torch.long, device=dev)
     env.step(actions, capture_observation=False, capture_info=False)
     torch.cuda.synchronize()
