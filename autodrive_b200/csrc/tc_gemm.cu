@@ -26,6 +26,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "tc_sm100.h"
 
 namespace py = pybind11;
@@ -47,6 +49,8 @@ struct GemmArgs {
   const float* bias;   // [N] or null
   int act;             // 0 none, 1 tanh, 2 relu, 3 gelu (tanh form)
   int accumulate;      // C += result (fp32 output only)
+  int k_steps;         // K steps (of kBK) per split along blockIdx.z
+  int64_t split_stride;  // elements between the fp32 partial outputs of two splits
   int* status;
 };
 
@@ -76,7 +80,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-  const int KT = (g.K + kBK - 1) / kBK;
+  // split-K: this CTA contracts K steps [kb, ke); each split writes its own
+  // fp32 partial (the host sums them)
+  const int KT_all = (g.K + kBK - 1) / kBK;
+  const int kb = blockIdx.z * g.k_steps;
+  const int ke = min(KT_all, kb + g.k_steps);
+  const int KT = max(0, ke - kb);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -110,7 +119,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       const uint32_t sb = sa + kTileBytes;
       const uint32_t full = full0 + 8 * s;
       tc::mbar_arrive_expect_tx(full, kStageBytes);
-      const int k0 = kt * kBK;
+      const int k0 = (kb + kt) * kBK;
       if (A_MN) {
         tc::tma_load_2d(sa, &ta, m0, k0, full);
         tc::tma_load_2d(sa + kTileBytes / 2, &ta, m0 + 64, k0, full);
@@ -165,14 +174,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         if (row < g.M) {
           const int c0 = n0 + 32 * cc;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c0 + i;
-            if (col < g.N) {
-              float x = v[i] + (g.bias ? g.bias[col] : 0.f);
-              x = apply_act(x, g.act);
-              const int64_t off = (int64_t)row * g.ldc + col;
-              if (g.c_f32) g.c_f32[off] = g.accumulate ? g.c_f32[off] + x : x;
-              else g.c_bf16[off] = __float2bfloat16_rn(x);
+          for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i] + (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f), g.act);
+          const int64_t off0 = (int64_t)blockIdx.z * g.split_stride + (int64_t)row * g.ldc + c0;
+          // each thread owns one output row: a full in-bounds 32-column chunk
+          // goes out as 16-byte vector stores (64 B bf16 / 128 B fp32 per row)
+          const bool vec = c0 + 32 <= g.N && (g.ldc % 8) == 0 &&
+                           ((reinterpret_cast<uintptr_t>(g.c_f32 ? (void*)g.c_f32 : (void*)g.c_bf16)) & 15) == 0;
+          if (vec && g.c_f32) {
+            float4* dst = reinterpret_cast<float4*>(g.c_f32 + off0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (g.accumulate) {
+                const float4 o = dst[j];
+                x.x += o.x, x.y += o.y, x.z += o.z, x.w += o.w;
+              }
+              dst[j] = x;
+            }
+          } else if (vec) {
+            uint4* dst = reinterpret_cast<uint4*>(g.c_bf16 + off0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u;
+              uint32_t* w = &u.x;
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * h], v[8 * j + 2 * h + 1]);
+                w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+              }
+              dst[j] = u;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (c0 + i < g.N) {
+                if (g.c_f32) g.c_f32[off0 + i] = g.accumulate ? g.c_f32[off0 + i] + v[i] : v[i];
+                else g.c_bf16[off0 + i] = __float2bfloat16_rn(v[i]);
+              }
             }
           }
         }
@@ -226,7 +264,8 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cud
                                      (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
     configured = true;
   }
-  dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM);
+  const int splits = ((g.K + kBK - 1) / kBK + g.k_steps - 1) / g.k_steps;
+  dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM, splits);
   tc_gemm_kernel<A_MN, B_MN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "tc_gemm launch failed");
 }
@@ -286,10 +325,39 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   const CUtensorMap ta = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), kBK) : make_map(a.data_ptr(), M, K, a.stride(0), kBM);
   const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), kBK) : make_map(b.data_ptr(), N, K, b.stride(0), kBN);
   auto st = c10::cuda::getCurrentCUDAStream().stream();
+  // Few output tiles over a long contraction (weight gradients: K = tokens)
+  // leave most SMs idle; split K so about two CTAs per SM run, each over at
+  // least 8 K steps, into fp32 partials that are summed afterwards.
+  const int64_t KT = (K + kBK - 1) / kBK;
+  const int64_t tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+  int64_t splits = 1;
+  if (tiles < 148 && KT >= 16) splits = std::min<int64_t>(KT / 8, (296 + tiles - 1) / tiles);
+  g.k_steps = (int)((KT + splits - 1) / splits);
+  splits = (KT + g.k_steps - 1) / g.k_steps;
+  torch::Tensor partial;
+  if (splits > 1) {
+    partial = torch::empty({splits, M, N}, c.options().dtype(torch::kFloat32));
+    g.c_f32 = partial.data_ptr<float>();
+    g.c_bf16 = nullptr;
+    g.ldc = N;
+    g.split_stride = M * N;
+    g.bias = nullptr;
+    g.act = 0;
+    g.accumulate = 0;
+  }
   if (!a_mn && !b_mn) launch<false, false>(ta, tb, g, st);
   else if (!a_mn && b_mn) launch<false, true>(ta, tb, g, st);
   else if (a_mn && !b_mn) launch<true, false>(ta, tb, g, st);
   else launch<true, true>(ta, tb, g, st);
+  if (splits > 1) {
+    auto z = partial.sum(0);
+    if (bias && bias->defined()) z += *bias;
+    if (act == 1) z = z.tanh();
+    else if (act == 2) z = z.relu();
+    else if (act == 3) z = torch::gelu(z, "tanh");
+    if (accumulate) c.add_(z);
+    else c.copy_(z);
+  }
 }
 
 }  // namespace

@@ -38,7 +38,11 @@ import torch
 from torch import Tensor, nn
 from torch.nn import functional as F
 
+from torch.nn.attention import SDPBackend, sdpa_kernel
+
 from ..ops.tc_linear import _TcLinearFn, tensorize
+
+_SDPA_BACKENDS = [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.MATH]
 
 
 def _linear(x: Tensor, weight: Tensor, bias: Tensor | None, tensor_cores: bool) -> Tensor:
@@ -247,7 +251,10 @@ class SelfAttention(nn.Module):
         qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
         q, k, v = qkv.view(b, t, 3, self.heads, d // self.heads).permute(2, 0, 3, 1, 4)
         bias = torch.zeros((b, 1, 1, t), device=x.device, dtype=q.dtype).masked_fill(padding[:, None, None, :], -torch.inf)
-        o = F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
+        # the memory-efficient kernel takes the padding bias directly; the cuDNN
+        # backend rebuilds its execution plan on the host for such masks
+        with sdpa_kernel(_SDPA_BACKENDS):
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=bias)
         return self.out_proj(o.transpose(1, 2).reshape(b, t, d))
 
 

@@ -206,6 +206,82 @@ def run_train(args, rank, world, local):
     }
 
 
+def run_train_zoo(args, rank, world, local):
+    """PPO step with a perception-input zoo policy (e.g. the ~4M-parameter
+    entity encoder, d = 256, 4 heads, 2 blocks) in bf16 autocast."""
+    import torch
+    sys.path.insert(0, HERE)
+    from autodrive_b200.bench.zoo_ppo import ZooPPO
+    from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
+    from autodrive_b200.utils.clocks import ClockSampler
+    dev = torch.device("cuda", local)
+    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed + rank * 1_000_003,
+                                control_modes=("deterministic",) * 3 + ("nn",) * 3, fuel_physics=True,
+                                horizon=8000, **BENCH_ENV)
+    ppo = ZooPPO(env, args.network, world, epochs=args.epochs, minibatches=args.minibatches,
+                 grad_backend=args.grad_backend)
+    state = {"ticks": 0, "upd": None, "events": None}
+    stats_dev = torch.zeros(3, device=dev)
+
+    def step():
+        ev = None
+        if state["events"] is not None:
+            ev = []
+            state["events"].append(ev)
+        ticks, upd = ppo.step(args.decisions, ev)
+        state["ticks"] += ticks
+        stats_dev[0] = upd["mean_reward"]
+        stats_dev[1] = upd["approx_kl_sum"] / max(1, upd["batches"])
+        stats_dev[2] = upd["entropy_sum"] / max(1, upd["batches"])
+
+    for _ in range(args.warmup):
+        step()
+    t0 = state["ticks"]
+    state["events"] = []
+    with ClockSampler(local) as clocks:
+        ms = _timed(step, args.steps, world)
+    torch.cuda.synchronize()
+    breakdown = {"rollout": sum(e[0].elapsed_time(e[1]) for e in state["events"]) / args.steps,
+                 "update": sum(e[1].elapsed_time(e[2]) for e in state["events"]) / args.steps}
+    state["events"] = None
+    ticks_timed = state["ticks"] - t0
+    value = args.envs * ticks_timed * world / (ms / 1e3)
+    samples = args.envs * 3 * args.decisions
+    host_stats = torch.zeros(3).pin_memory()
+    host_seed = torch.tensor([float(args.seed)]).pin_memory()
+    seed_dev = torch.zeros(1, device=dev)
+
+    def e2e_step():
+        seed_dev.copy_(host_seed, non_blocking=True)
+        step()
+        host_stats.copy_(stats_dev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        _ = float(host_stats[0])
+
+    t1 = state["ticks"]
+    e2e_ms = _timed(e2e_step, args.steps, world)
+    e2e_ticks = args.envs * (state["ticks"] - t1) * world
+    return {
+        "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init seeded REBUILT matches and policy; no external data)",
+        "ppo_samples_per_s": samples * args.steps * world / (ms / 1e3), "ppo_samples_per_step_per_gpu": samples,
+        "config": {"model": f"TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 400 FUEL, perception every "
+                            f"tick) + PPO on PerceptionActorCritic {args.network} ({ppo.params} parameters, "
+                            f"bf16 autocast, fp32 master) for 3 learned defenders",
+                   "global_batch": args.envs * world, "envs_per_gpu": args.envs, "seq_len": args.decisions,
+                   "ppo_epochs": args.epochs, "ppo_minibatches": args.minibatches,
+                   "grad_backend": ppo.sync.backend, "parallelism": f"env-batch x dp{world}",
+                   "l2": "working set > 126 MB L2 (no flush needed)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
+                "h2d_bytes_per_step": host_seed.numel() * 4, "d2h_bytes_per_step": host_stats.numel() * 4},
+        "gpu_launches": None,
+        "breakdown_ms_per_step": {k: round(v, 3) for k, v in breakdown.items()},
+    }
+
+
 def run_sim(args, rank, world, local):
     import torch
     sys.path.insert(0, HERE)
@@ -296,6 +372,9 @@ def main():
     p.add_argument("--epochs", type=int, default=4)
     p.add_argument("--minibatches", type=int, default=8)
     p.add_argument("--grad-backend", default="auto")
+    p.add_argument("--network", default="mlp",
+                   help="train mode policy: mlp (strategic_adstar ActorCritic, fused tcgen05 kernels) or a "
+                        "perception zoo architecture such as entity_attention_256")
     p.add_argument("--ticks-per-step", type=int, default=20, help="ticks per step (sim mode)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
@@ -309,7 +388,8 @@ def main():
     if args.impl == "reference":
         result = run_reference(args, rank, world, local)
     else:
-        result = (run_train if args.mode == "train" else run_sim)(args, rank, world, local)
+        train = run_train if args.network == "mlp" else run_train_zoo
+        result = (train if args.mode == "train" else run_sim)(args, rank, world, local)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

@@ -26,7 +26,8 @@ def test_tc_linear_cpu_matches_linear():
 @pytest.mark.gpu
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
-@pytest.mark.parametrize("mnk", [(128, 128, 64), (300, 200, 152), (1000, 72, 1024), (64, 520, 40)])
+@pytest.mark.parametrize("mnk", [(128, 128, 64), (300, 200, 152), (1000, 72, 1024), (64, 520, 40),
+                                 (256, 136, 40000)])   # the last one runs split-K
 def test_gemm_majors_match_fp32(a_mn, b_mn, mnk):
     m, n, k = mnk
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
