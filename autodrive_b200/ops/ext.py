@@ -17,6 +17,7 @@ def extension():
     global _EXT, _ERR
     if _EXT is None and _ERR is None:
         try:
+            import torch  # noqa: F401 - loads libc10 / libtorch, which _C links against
             _EXT = importlib.import_module("autodrive_b200._C")
         except Exception as exc:  # noqa: BLE001 - surfaced by require_extension
             _ERR = exc
