@@ -8,17 +8,24 @@
 //   dX       dX = dY W       A = dY (K-major),  B = W  (MN-major)
 //   dW       dW = dY^T X     A = dY (MN-major), B = X  (MN-major)
 //
-// One CTA per 128x128 output tile, 192 threads:
+// Persistent kernel: one CTA per SM (at most one per work item) walks the
+// 128x128 output tiles (x split-K slices) in a static round-robin, N tiles
+// fastest so the CTAs running at the same time share A row blocks in L2.
+// 192 threads:
 //   warp 0  TMA producer: 2-D tiled loads (128-byte swizzle) of the A and B
-//           tiles of each 64-deep K step into a 4-stage shared-memory ring;
-//   warp 1  allocates 128 TMEM columns; one lane issues 4 tcgen05.mma per K
-//           step and commits each stage back to the producer, then signals
-//           the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld of the fp32 accumulator rows, + bias,
+//           tiles of each 64-deep K step into a 4-stage shared-memory ring
+//           that runs continuously across tiles;
+//   warp 1  allocates 256 TMEM columns (two 128-column fp32 accumulators);
+//           one lane issues 4 tcgen05.mma per K step into the accumulator of
+//           the current tile, commits each stage back to the producer and
+//           the finished accumulator to the epilogue;
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator rows (the accumulator
+//           is handed back to the MMA warp as soon as it is read), + bias,
 //           activation, fp32 or bf16 stores with bounds checks.
-// Out-of-range tile parts are zero-filled by the TMA unit. Every mbarrier
-// wait is bounded in wall-clock time; a wait that runs out sets a bit in a
-// device status word and the CTA drains and exits.
+// With two accumulators the epilogue of tile i overlaps the loads and MMAs
+// of tile i+1. Out-of-range tile parts are zero-filled by the TMA unit.
+// Every mbarrier wait is bounded in wall-clock time; a wait that runs out
+// sets a bit in a device status word and the CTA drains and exits.
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cuda.h>
@@ -40,6 +47,7 @@ constexpr uint32_t kTileBytes = 128 * 128;        // one 128 x 64 bf16 operand t
 constexpr uint32_t kStageBytes = 2 * kTileBytes;
 constexpr uint64_t kWaitNs = 2000000000ull;       // 2 s
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr uint32_t kAccCols = 128;                // one fp32 accumulator: 128 lanes x 128 columns
 
 struct GemmArgs {
   int M, N, K;
@@ -49,8 +57,9 @@ struct GemmArgs {
   const float* bias;   // [N] or null
   int act;             // 0 none, 1 tanh, 2 relu, 3 gelu (tanh form)
   int accumulate;      // C += result (fp32 output only)
-  int k_steps;         // K steps (of kBK) per split along blockIdx.z
-  int64_t split_stride;  // elements between the fp32 partial outputs of two splits
+  int k_steps;         // K steps (of kBK) per split-K slice
+  int splits;          // split-K slices (1: no split)
+  int64_t split_stride;  // elements between the fp32 partial outputs of two slices
   int* status;
 };
 
@@ -66,38 +75,95 @@ __device__ __forceinline__ float apply_act(float x, int act) {
   }
 }
 
+// Work item w -> (m0, n0, split slice z); N tiles fastest.
+struct TileCoord { int m0, n0, z; };
+__device__ __forceinline__ TileCoord tile_of(int w, int tiles_n, int tiles_m) {
+  TileCoord t;
+  t.n0 = (w % tiles_n) * kBN;
+  const int r = w / tiles_n;
+  t.m0 = (r % tiles_m) * kBM;
+  t.z = r / tiles_m;
+  return t;
+}
+
+// One accumulator's 32 x 32 chunk of this thread's row: bias, activation and
+// the store (16-byte vectors for a full aligned chunk, scalars otherwise).
+__device__ __forceinline__ void store_chunk(const GemmArgs& g, float (&v)[32], int row, int c0, int z) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i] + (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f), g.act);
+  const int64_t off0 = (int64_t)z * g.split_stride + (int64_t)row * g.ldc + c0;
+  // each thread owns one output row: a full in-bounds 32-column chunk goes
+  // out as 16-byte vector stores (64 B bf16 / 128 B fp32 per row)
+  const bool vec = c0 + 32 <= g.N && (g.ldc % 8) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(g.c_f32 ? (void*)g.c_f32 : (void*)g.c_bf16)) & 15) == 0;
+  if (vec && g.c_f32) {
+    float4* dst = reinterpret_cast<float4*>(g.c_f32 + off0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      if (g.accumulate) {
+        const float4 o = dst[j];
+        x.x += o.x, x.y += o.y, x.z += o.z, x.w += o.w;
+      }
+      dst[j] = x;
+    }
+  } else if (vec) {
+    uint4* dst = reinterpret_cast<uint4*>(g.c_bf16 + off0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u;
+      uint32_t* w = &u.x;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * h], v[8 * j + 2 * h + 1]);
+        w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+      }
+      dst[j] = u;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (c0 + i < g.N) {
+        if (g.c_f32) g.c_f32[off0 + i] = g.accumulate ? g.c_f32[off0 + i] + v[i] : v[i];
+        else g.c_bf16[off0 + i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+}
+
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* misc = smem + kStages * kStageBytes;
-  const uint32_t full0 = tc::smem_u32(misc);             // kStages mbarriers
-  const uint32_t empty0 = full0 + 8 * kStages;           // kStages mbarriers
-  const uint32_t accbar = empty0 + 8 * kStages;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kStages + 1));
-  int* s_fail = reinterpret_cast<int*>(misc + 8 * (2 * kStages + 1) + 8);
+  const uint32_t full0 = tc::smem_u32(misc);             // kStages mbarriers: stage loaded
+  const uint32_t empty0 = full0 + 8 * kStages;           // kStages mbarriers: stage consumed
+  const uint32_t tfull0 = empty0 + 8 * kStages;          // 2 mbarriers: accumulator complete
+  const uint32_t tempty0 = tfull0 + 16;                  // 2 mbarriers: accumulator read out
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kStages + 4));
+  int* s_fail = reinterpret_cast<int*>(misc + 8 * (2 * kStages + 4) + 8);
+  volatile int* fail = s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-  // split-K: this CTA contracts K steps [kb, ke); each split writes its own
-  // fp32 partial (the host sums them)
+  const int tiles_n = (g.N + kBN - 1) / kBN, tiles_m = (g.M + kBM - 1) / kBM;
+  const int total = tiles_n * tiles_m * g.splits;
   const int KT_all = (g.K + kBK - 1) / kBK;
-  const int kb = blockIdx.z * g.k_steps;
-  const int ke = min(KT_all, kb + g.k_steps);
-  const int KT = max(0, ke - kb);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       tc::mbar_init(full0 + 8 * s, 1);
       tc::mbar_init(empty0 + 8 * s, 1);
     }
-    tc::mbar_init(accbar, 1);
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(tfull0 + 8 * a, 1);
+      tc::mbar_init(tempty0 + 8 * a, 128);   // every epilogue thread arrives
+    }
     tc::mbar_init_fence();
     *s_fail = 0;
   }
   if (warp == 1) {
-    tc::tmem_alloc(tc::smem_u32(s_tmem), 128);
+    tc::tmem_alloc(tc::smem_u32(s_tmem), 2 * kAccCols);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -106,114 +172,100 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   const uint32_t tmem = *s_tmem;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kStages;
-      if (kt >= kStages && !tc::mbar_wait(empty0 + 8 * s, ((kt / kStages) - 1) & 1, kWaitNs)) {
-        atomicOr(g.status, 1);
-        atomicExch(s_fail, 1);
-        break;
-      }
-      if (*reinterpret_cast<volatile int*>(s_fail)) break;
-      const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
-      const uint32_t sb = sa + kTileBytes;
-      const uint32_t full = full0 + 8 * s;
-      tc::mbar_arrive_expect_tx(full, kStageBytes);
-      const int k0 = (kb + kt) * kBK;
-      if (A_MN) {
-        tc::tma_load_2d(sa, &ta, m0, k0, full);
-        tc::tma_load_2d(sa + kTileBytes / 2, &ta, m0 + 64, k0, full);
-      } else {
-        tc::tma_load_2d(sa, &ta, k0, m0, full);
-      }
-      if (B_MN) {
-        tc::tma_load_2d(sb, &tb, n0, k0, full);
-        tc::tma_load_2d(sb + kTileBytes / 2, &tb, n0 + 64, k0, full);
-      } else {
-        tc::tma_load_2d(sb, &tb, k0, n0, full);
+    // ---- TMA producer: one ring position per K step, across all tiles ----
+    uint32_t it = 0;
+    for (int w = blockIdx.x; w < total && !*fail; w += gridDim.x) {
+      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
+      for (int kt = kb; kt < ke; ++kt, ++it) {
+        const uint32_t s = it % kStages;
+        if (it >= kStages && !tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, kWaitNs)) {
+          atomicOr(g.status, 1);
+          atomicExch(s_fail, 1);
+          break;
+        }
+        if (*fail) break;
+        const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
+        const uint32_t sb = sa + kTileBytes;
+        const uint32_t full = full0 + 8 * s;
+        tc::mbar_arrive_expect_tx(full, kStageBytes);
+        const int k0 = kt * kBK;
+        if (A_MN) {
+          tc::tma_load_2d(sa, &ta, t.m0, k0, full);
+          tc::tma_load_2d(sa + kTileBytes / 2, &ta, t.m0 + 64, k0, full);
+        } else {
+          tc::tma_load_2d(sa, &ta, k0, t.m0, full);
+        }
+        if (B_MN) {
+          tc::tma_load_2d(sb, &tb, t.n0, k0, full);
+          tc::tma_load_2d(sb + kTileBytes / 2, &tb, t.n0 + 64, k0, full);
+        } else {
+          tc::tma_load_2d(sb, &tb, k0, t.n0, full);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer: tile lt accumulates into TMEM columns (lt & 1) * 128 ----
     const uint32_t id = tc::idesc_bf16(kBM, kBN, A_MN, B_MN);
-    bool ok = true;
-    for (int kt = 0; kt < KT && ok; ++kt) {
-      const int s = kt % kStages;
-      if (!tc::mbar_wait(full0 + 8 * s, (kt / kStages) & 1, kWaitNs)) {
-        atomicOr(g.status, 2);
+    uint32_t it = 0;
+    int lt = 0;
+    for (int w = blockIdx.x; w < total && !*fail; w += gridDim.x, ++lt) {
+      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
+      const int acc = lt & 1;
+      if (lt >= 2 && !tc::mbar_wait(tempty0 + 8 * acc, ((lt >> 1) - 1) & 1, kWaitNs)) {
+        atomicOr(g.status, 8);
         atomicExch(s_fail, 1);
-        ok = false;
         break;
       }
       tc::tc_fence_after();
-      const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
-      const uint32_t sb = sa + kTileBytes;
+      const uint32_t d = tmem + acc * kAccCols;
+      bool ok = true;
+      for (int kt = kb; kt < ke; ++kt, ++it) {
+        const uint32_t s = it % kStages;
+        if (!tc::mbar_wait(full0 + 8 * s, (it / kStages) & 1, kWaitNs)) {
+          atomicOr(g.status, 2);
+          atomicExch(s_fail, 1);
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t sa = tc::smem_u32(smem + s * kStageBytes);
+        const uint32_t sb = sa + kTileBytes;
 #pragma unroll
-      for (int ks = 0; ks < kBK / 16; ++ks) {
-        const uint64_t da = A_MN ? tc::desc_mnmajor(sa, kBK, ks) : tc::desc_kmajor(sa, kBM, ks);
-        const uint64_t db = B_MN ? tc::desc_mnmajor(sb, kBK, ks) : tc::desc_kmajor(sb, kBN, ks);
-        tc::mma_bf16(tmem, da, db, id, kt > 0 || ks > 0);
+        for (int ks = 0; ks < kBK / 16; ++ks) {
+          const uint64_t da = A_MN ? tc::desc_mnmajor(sa, kBK, ks) : tc::desc_kmajor(sa, kBM, ks);
+          const uint64_t db = B_MN ? tc::desc_mnmajor(sb, kBK, ks) : tc::desc_kmajor(sb, kBN, ks);
+          tc::mma_bf16(d, da, db, id, kt > kb || ks > 0);
+        }
+        tc::mma_commit(empty0 + 8 * s);   // stage free once these MMAs have read it
       }
-      tc::mma_commit(empty0 + 8 * s);   // stage free once these MMAs have read it
+      tc::mma_commit(tfull0 + 8 * acc);   // accumulator complete (or nothing issued)
+      if (!ok) break;
     }
-    tc::mma_commit(accbar);             // accumulator complete (or nothing issued)
   }
 
   if (warp >= 2) {
     // ---- epilogue ----
-    const bool got = tc::mbar_wait(accbar, 0, kWaitNs);
-    if (!got) atomicOr(g.status, 4);
-    tc::tc_fence_after();
-    const int q = warp & 3;
-    const int row = m0 + 32 * q + lane;
-    if (got && !*reinterpret_cast<volatile int*>(s_fail)) {
+    const int q = warp & 3;               // TMEM lanes 32q..32q+31 belong to this warp
+    int lt = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++lt) {
+      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const int acc = lt & 1;
+      const bool got = tc::mbar_wait(tfull0 + 8 * acc, (lt >> 1) & 1, kWaitNs);
+      if (!got) atomicOr(g.status, 4);
+      if (!got || *fail) break;
+      tc::tc_fence_after();
+      const int row = t.m0 + 32 * q + lane;
 #pragma unroll 1
       for (int cc = 0; cc < kBN / 32; ++cc) {
         float v[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
-        if (row < g.M) {
-          const int c0 = n0 + 32 * cc;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i] + (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f), g.act);
-          const int64_t off0 = (int64_t)blockIdx.z * g.split_stride + (int64_t)row * g.ldc + c0;
-          // each thread owns one output row: a full in-bounds 32-column chunk
-          // goes out as 16-byte vector stores (64 B bf16 / 128 B fp32 per row)
-          const bool vec = c0 + 32 <= g.N && (g.ldc % 8) == 0 &&
-                           ((reinterpret_cast<uintptr_t>(g.c_f32 ? (void*)g.c_f32 : (void*)g.c_bf16)) & 15) == 0;
-          if (vec && g.c_f32) {
-            float4* dst = reinterpret_cast<float4*>(g.c_f32 + off0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-              if (g.accumulate) {
-                const float4 o = dst[j];
-                x.x += o.x, x.y += o.y, x.z += o.z, x.w += o.w;
-              }
-              dst[j] = x;
-            }
-          } else if (vec) {
-            uint4* dst = reinterpret_cast<uint4*>(g.c_bf16 + off0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 u;
-              uint32_t* w = &u.x;
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * h], v[8 * j + 2 * h + 1]);
-                w[h] = *reinterpret_cast<const uint32_t*>(&b2);
-              }
-              dst[j] = u;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (c0 + i < g.N) {
-                if (g.c_f32) g.c_f32[off0 + i] = g.accumulate ? g.c_f32[off0 + i] + v[i] : v[i];
-                else g.c_bf16[off0 + i] = __float2bfloat16_rn(v[i]);
-              }
-            }
-          }
+        tc::tmem_ld32(tmem + acc * kAccCols + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
+        if (cc == kBN / 32 - 1) {         // accumulator read out: the MMA warp may reuse it
+          tc::tc_fence_before();
+          tc::mbar_arrive(tempty0 + 8 * acc);
         }
+        if (row < g.M) store_chunk(g, v, row, t.n0 + 32 * cc, t.z);
       }
     }
   }
@@ -221,7 +273,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 128);
+    tc::tmem_dealloc(tmem, 2 * kAccCols);
   }
 }
 
@@ -256,6 +308,17 @@ CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, in
   return m;
 }
 
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  TORCH_CHECK(cudaGetDevice(&dev) == cudaSuccess, "cudaGetDevice failed");
+  TORCH_CHECK(dev >= 0 && dev < 64, "tc_gemm: device index out of range");
+  if (!counts[dev])
+    TORCH_CHECK(cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) == cudaSuccess,
+                "cudaDeviceGetAttribute(multiProcessorCount) failed");
+  return counts[dev];
+}
+
 template <bool A_MN, bool B_MN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
   static bool configured = false;
@@ -264,8 +327,10 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cud
                                      (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
     configured = true;
   }
-  const int splits = ((g.K + kBK - 1) / kBK + g.k_steps - 1) / g.k_steps;
-  dim3 grid((g.N + kBN - 1) / kBN, (g.M + kBM - 1) / kBM, splits);
+  // persistent: one CTA per SM, never more CTAs than work items
+  const int64_t total = (int64_t)((g.N + kBN - 1) / kBN) * ((g.M + kBM - 1) / kBM) * g.splits;
+  TORCH_CHECK(total < (1ll << 31), "tc_gemm: too many output tiles");
+  const int grid = (int)std::min<int64_t>(total, sm_count());
   tc_gemm_kernel<A_MN, B_MN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "tc_gemm launch failed");
 }
@@ -326,14 +391,15 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), kBK) : make_map(b.data_ptr(), N, K, b.stride(0), kBN);
   auto st = c10::cuda::getCurrentCUDAStream().stream();
   // Few output tiles over a long contraction (weight gradients: K = tokens)
-  // leave most SMs idle; split K so about two CTAs per SM run, each over at
-  // least 8 K steps, into fp32 partials that are summed afterwards.
+  // leave most SMs idle; split K into about two work items per SM, each over
+  // at least 8 K steps, into fp32 partials that are summed afterwards.
   const int64_t KT = (K + kBK - 1) / kBK;
   const int64_t tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
   int64_t splits = 1;
   if (tiles < 148 && KT >= 16) splits = std::min<int64_t>(KT / 8, (296 + tiles - 1) / tiles);
   g.k_steps = (int)((KT + splits - 1) / splits);
   splits = (KT + g.k_steps - 1) / g.k_steps;
+  g.splits = (int)splits;
   torch::Tensor partial;
   if (splits > 1) {
     partial = torch::empty({splits, M, N}, c.options().dtype(torch::kFloat32));

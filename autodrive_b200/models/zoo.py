@@ -40,6 +40,7 @@ from torch.nn import functional as F
 
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
+from ..ops.layernorm import FusedLayerNorm
 from ..ops.tc_linear import _TcLinearFn, tensorize
 
 _SDPA_BACKENDS = [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.MATH]
@@ -233,6 +234,67 @@ class DeepSetsPolicy(nn.Module):
         return self.actor(h), self.critic(h).squeeze(-1)
 
 
+def _key_padding_bias(padding: Tensor, heads: int, dtype: torch.dtype) -> Tensor:
+    """Additive key-padding bias [b, heads, t, t] (a broadcast view) whose row
+    storage is padded to 16 elements, the alignment the attention kernel
+    needs for its bias rows."""
+    b, t = padding.shape
+    tp = (t + 15) // 16 * 16
+    full = torch.zeros((b, 1, 1, tp), device=padding.device, dtype=dtype)
+    bias = full[..., :t]
+    bias.masked_fill_(padding[:, None, None, :], -torch.inf)
+    return bias.expand(b, heads, t, t)
+
+
+class _PackedAttention(torch.autograd.Function):
+    """Multi-head self-attention over a packed projection qkv (= [..., 3,
+    heads, dh]) on PyTorch's memory-efficient attention kernel, called in its
+    native [b, t, heads, dh] layout. Two forms:
+
+    * padded: qkv [b, t, 3d] with an additive key-padding bias;
+    * variable length: qkv [total, 3d] holding the valid tokens of all
+      samples back to back, sample i at rows cu[i]:cu[i+1] (no bias).
+
+    Queries, keys and values are strided views of qkv, the output comes back
+    without a transpose, and the backward asks for dq, dk, dv in one shared
+    [..., 3, heads, dh] buffer, which is returned as d(qkv) without a
+    stacking copy."""
+
+    @staticmethod
+    def forward(ctx, qkv: Tensor, bias, heads: int, cu=None, max_len: int = 0) -> Tensor:
+        shape = qkv.shape
+        x = qkv.view(*((1,) if cu is not None else ()), *shape[:-1], 3, heads, shape[-1] // (3 * heads))
+        q, k, v = x.select(-3, 0), x.select(-3, 1), x.select(-3, 2)
+        out, lse, seed, offset, _, _ = torch.ops.aten._efficient_attention_forward(
+            q, k, v, bias, cu, cu, max_len if cu is not None else None, max_len if cu is not None else None,
+            0.0, 0, True)
+        ctx.heads, ctx.max_len = heads, max_len
+        ctx.save_for_backward(qkv, bias, out, lse, seed, offset, cu)
+        return out.reshape(*shape[:-1], shape[-1] // 3)
+
+    @staticmethod
+    def backward(ctx, grad: Tensor):
+        qkv, bias, out, lse, seed, offset, cu = ctx.saved_tensors
+        shape, h = qkv.shape, ctx.heads
+        d3 = shape[-1]
+        x = qkv.view(*((1,) if cu is not None else ()), *shape[:-1], 3, h, d3 // (3 * h))
+        q, k, v = x.select(-3, 0), x.select(-3, 1), x.select(-3, 2)
+        t = q.shape[1]
+        ml = ctx.max_len if cu is not None else t
+        gq, gk, gv, _ = torch.ops.aten._efficient_attention_backward(
+            grad.reshape(out.shape).contiguous().to(out.dtype), q, k, v, bias, out, cu, cu, ml, ml, lse,
+            0.0, seed, offset, 0, False, shared_storage_dqdkdv=True)
+        d, es = d3 // 3, gq.element_size()
+        packed = (gq.stride()[1:] == (d3, d3 // (3 * h), 1) and gk.stride() == gq.stride()
+                  and gv.stride() == gq.stride() and (gq.shape[0] == 1 or gq.stride(0) == t * d3)
+                  and gk.data_ptr() == gq.data_ptr() + d * es and gv.data_ptr() == gq.data_ptr() + 2 * d * es)
+        if packed:
+            gqkv = gq.as_strided(shape, qkv.stride())
+        else:
+            gqkv = torch.stack((gq, gk, gv), -3).reshape(shape)
+        return gqkv, None, None, None, None
+
+
 class SelfAttention(nn.Module):
     """Multi-head self-attention with key padding; projections packed as
     ``in_proj_weight`` [3d, d] and ``out_proj`` like nn.MultiheadAttention."""
@@ -246,9 +308,18 @@ class SelfAttention(nn.Module):
         nn.init.xavier_uniform_(self.in_proj_weight)
         nn.init.zeros_(self.out_proj.bias)
 
+    def forward_packed(self, x: Tensor, cu: Tensor, max_len: int) -> Tensor:
+        """Attention within each sample of packed valid tokens x [total, d]
+        (sample i at rows cu[i]:cu[i+1]); CUDA, bf16 / fp16 projections."""
+        qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
+        return self.out_proj(_PackedAttention.apply(qkv, None, self.heads, cu, max_len))
+
     def forward(self, x: Tensor, padding: Tensor) -> Tensor:
         b, t, d = x.shape
         qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
+        if qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16) and (d // self.heads) % 8 == 0:
+            o = _PackedAttention.apply(qkv, _key_padding_bias(padding, self.heads, qkv.dtype), self.heads)
+            return self.out_proj(o)
         q, k, v = qkv.view(b, t, 3, self.heads, d // self.heads).permute(2, 0, 3, 1, 4)
         bias = torch.zeros((b, 1, 1, t), device=x.device, dtype=q.dtype).masked_fill(padding[:, None, None, :], -torch.inf)
         # the memory-efficient kernel takes the padding bias directly; the cuDNN
@@ -261,10 +332,14 @@ class SelfAttention(nn.Module):
 class EntityAttentionBlock(nn.Module):
     def __init__(self, dim: int = 64, heads: int = 4, ff: int = 128, tensor_cores: bool = False):
         super().__init__()
-        self.norm_attention = nn.LayerNorm(dim)
+        self.norm_attention = FusedLayerNorm(dim)
         self.attention = SelfAttention(dim, heads, tensor_cores)
-        self.norm_feedforward = nn.LayerNorm(dim)
+        self.norm_feedforward = FusedLayerNorm(dim)
         self.feedforward = nn.Sequential(nn.Linear(dim, ff), nn.GELU(), nn.Linear(ff, dim))
+
+    def forward_packed(self, tokens: Tensor, cu: Tensor, max_len: int) -> Tensor:
+        tokens = tokens + self.attention.forward_packed(self.norm_attention(tokens), cu, max_len)
+        return tokens + self.feedforward(self.norm_feedforward(tokens))
 
     def forward(self, tokens: Tensor, padding: Tensor) -> Tensor:
         tokens = tokens + self.attention(self.norm_attention(tokens), padding)
@@ -285,7 +360,7 @@ class EntityAttentionPolicy(nn.Module):
         self.scalar_encoder = nn.Sequential(nn.Linear(scalar_dim, dim), nn.Tanh())
         self.entity_encoder = nn.Sequential(nn.Linear(12, dim), nn.GELU())
         self.blocks = nn.ModuleList(EntityAttentionBlock(dim, heads, ff, tensor_cores) for _ in range(blocks))
-        head, width = [nn.LayerNorm(dim)], dim
+        head, width = [FusedLayerNorm(dim)], dim
         for i, hid in enumerate(head_hidden):
             head += [nn.Linear(width, hid), nn.Tanh() if i == len(head_hidden) - 1 else nn.GELU()]
             width = hid
@@ -293,7 +368,39 @@ class EntityAttentionPolicy(nn.Module):
         self.actor = nn.Linear(width, action_dim)
         self.critic = nn.Linear(width, 1)
 
+    def _packed_ok(self, inputs: dict) -> bool:
+        x = inputs["entities"]
+        dh = self.blocks[0].attention.dim // self.blocks[0].attention.heads if len(self.blocks) else 0
+        return (x.is_cuda and len(self.blocks) > 0 and dh % 8 == 0 and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") in (torch.bfloat16, torch.float16))
+
+    def _forward_packed(self, inputs: dict) -> tuple[Tensor, Tensor]:
+        """The same network on the valid tokens only, packed back to back
+        (context token first in each sample). Padding tokens never act as
+        keys and their outputs are discarded, so the valid tokens' results
+        are those of the padded form; the linear layers and the attention
+        then cost what the held tracks cost, not what the slot count does."""
+        mask = inputs["entity_mask"].bool()
+        b, e = mask.shape
+        t = e + 1
+        valid = torch.cat((mask.new_ones((b, 1)), mask), 1)
+        counts = valid.sum(1, dtype=torch.int32)
+        cu = F.pad(counts.cumsum(0, dtype=torch.int32), (1, 0))
+        max_len = int(counts.max())
+        rows = valid.reshape(-1).nonzero().squeeze(1)
+        ents = torch.cat((inputs["entities"].new_zeros((b, 1, inputs["entities"].shape[-1])), inputs["entities"]), 1)
+        tokens = self.entity_encoder(ents.reshape(b * t, -1)[rows])
+        first = cu[:-1].long()
+        ctx = self.scalar_encoder(inputs["scalars"])
+        tokens = tokens.index_put((first,), ctx.to(tokens.dtype))
+        for blk in self.blocks:
+            tokens = blk.forward_packed(tokens, cu, max_len)
+        h = self.fusion(tokens[first])
+        return self.actor(h), self.critic(h).squeeze(-1)
+
     def forward(self, inputs: dict) -> tuple[Tensor, Tensor]:
+        if self._packed_ok(inputs):
+            return self._forward_packed(inputs)
         mask = inputs["entity_mask"].bool()
         ents = inputs["entities"].masked_fill(~mask[..., None], 0.)
         ctx = self.scalar_encoder(inputs["scalars"])[:, None]

@@ -29,12 +29,25 @@ def _pad8(n: int) -> int:
 
 
 def _bf16_padded(x: torch.Tensor, cols: int, rows: int | None = None) -> torch.Tensor:
+    """`x` as a contiguous, 16-byte aligned bf16 [rows, cols] operand; zero
+    padding only where the shape grows (no copy when `x` already qualifies)."""
     r = x.shape[0] if rows is None else rows
-    if x.dtype == torch.bfloat16 and x.shape[1] == cols and r == x.shape[0] and x.is_contiguous():
-        return x
+    if x.shape[1] == cols and r == x.shape[0]:
+        y = x.to(torch.bfloat16).contiguous()
+        if y.data_ptr() % 16 == 0:
+            return y
+        return y.clone()
     out = torch.zeros((r, cols), dtype=torch.bfloat16, device=x.device)
     out[:x.shape[0], :x.shape[1]] = x
     return out
+
+
+def _result_dtype(x: torch.Tensor) -> torch.dtype:
+    """Output dtype of a linear layer on `x`: the autocast dtype inside a CUDA
+    autocast region (as for nn.Linear), else x's own dtype."""
+    if x.is_cuda and torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
 
 
 class _Status:
@@ -62,6 +75,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
 
 
 class _TcLinearFn(torch.autograd.Function):
+    """Forward and both gradients on the tensor-core GEMM. A bf16 result (bf16
+    input, or a bf16 autocast region) comes straight out of the GEMM epilogue,
+    as does a bf16 input gradient: no fp32 intermediate and no cast pass."""
+
     @staticmethod
     def forward(ctx, x, weight, bias, act):
         out_f, in_f = weight.shape
@@ -70,30 +87,35 @@ class _TcLinearFn(torch.autograd.Function):
         in_p, out_p = _pad8(in_f), _pad8(out_f)
         xb = _bf16_padded(x2, in_p)
         wb = _bf16_padded(weight.detach(), in_p, rows=out_p)
-        y = gemm(xb, wb[:out_f], bias=None if bias is None else bias.detach().float().contiguous(), act=act)
+        target = _result_dtype(x)
+        y = gemm(xb, wb[:out_f], bias=None if bias is None else bias.detach().float().contiguous(), act=act,
+                 out_dtype=torch.bfloat16 if target == torch.bfloat16 else torch.float32)
         ctx.act = act
         ctx.shapes = (in_f, out_f, in_p, out_p, lead)
+        ctx.x_dtype = x.dtype
         ctx.has_bias = bias is not None
         ctx.save_for_backward(xb, wb, y if act in ("tanh", "relu") else torch.empty(0, device=x.device))
-        return y.reshape(*lead, out_f).to(x.dtype)
+        y = y.reshape(*lead, out_f)
+        return y if y.dtype == target else y.to(target)
 
     @staticmethod
     def backward(ctx, gy):
         xb, wb, y = ctx.saved_tensors
         in_f, out_f, in_p, out_p, lead = ctx.shapes
-        g = gy.reshape(-1, out_f).float()
+        g = gy.reshape(-1, out_f)
         if ctx.act == "tanh":
-            g = g * (1 - y * y)
+            g = g.float() * (1 - y.float().square())
         elif ctx.act == "relu":
-            g = g * (y > 0)
+            g = g.float() * (y > 0)
         gb = _bf16_padded(g, out_p)
         gx = gw = gbias = None
         if ctx.needs_input_grad[0]:
-            gx = gemm(gb, wb, b_mn=True)[:, :in_f].reshape(*lead, in_f)
+            gx_dtype = torch.bfloat16 if ctx.x_dtype == torch.bfloat16 else torch.float32
+            gx = gemm(gb, wb, b_mn=True, out_dtype=gx_dtype)[:, :in_f].reshape(*lead, in_f)
         if ctx.needs_input_grad[1]:
             gw = gemm(gb, xb, a_mn=True, b_mn=True)[:out_f, :in_f]
         if ctx.has_bias and ctx.needs_input_grad[2]:
-            gbias = g.sum(0)
+            gbias = g.sum(0, dtype=torch.float32)
         return gx, gw, gbias, None
 
 

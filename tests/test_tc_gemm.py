@@ -27,7 +27,9 @@ def test_tc_linear_cpu_matches_linear():
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
 @pytest.mark.parametrize("mnk", [(128, 128, 64), (300, 200, 152), (1000, 72, 1024), (64, 520, 40),
-                                 (256, 136, 40000)])   # the last one runs split-K
+                                 (256, 136, 40000),    # split-K
+                                 (4096, 1024, 256),    # 256 tiles: two per persistent CTA
+                                 (20000, 384, 136)])   # 471 tiles: both accumulators reused
 def test_gemm_majors_match_fp32(a_mn, b_mn, mnk):
     m, n, k = mnk
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
@@ -100,3 +102,27 @@ def test_tensorized_mlp_trains():
         opt.step()
         first = first if first is not None else loss.item()
     assert loss.item() < .2 * first
+
+
+@pytest.mark.gpu
+def test_tc_linear_bf16_autocast_outputs_and_grads():
+    """Inside a bf16 autocast region the layer returns bf16 straight from the
+    GEMM epilogue and a bf16 input receives a bf16 gradient."""
+    torch.manual_seed(5)
+    ref = nn.Linear(256, 520).cuda()
+    tl = TcLinear(256, 520).cuda()
+    tl.load_state_dict(ref.state_dict())
+    x = torch.randn(3000, 256, device="cuda").bfloat16().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = tl(x)
+    assert y.dtype == torch.bfloat16
+    y_ref = x.detach().float() @ ref.weight.T + ref.bias
+    assert (y.float() - y_ref).abs().max().item() < 5e-2 * max(1., y_ref.abs().max().item())
+    w = torch.randn_like(y_ref)
+    (y.float() * w).sum().backward()
+    assert x.grad.dtype == torch.bfloat16
+    gx_ref = w @ ref.weight
+    gw_ref = w.T @ x.detach().float()
+    for got, want in ((x.grad.float(), gx_ref), (tl.weight.grad, gw_ref), (tl.bias.grad, w.sum(0))):
+        rel = (got - want).norm().item() / max(want.norm().item(), 1e-12)
+        assert rel < 2e-2, rel

@@ -88,3 +88,83 @@ def test_tensor_core_zoo_matches_fp32(arch):
     assert (v1 - v2).abs().max().item() < 5e-2 * max(1., v1.abs().max().item())
     (l2.square().mean() + v2.square().mean()).backward()
     assert all(torch.isfinite(p.grad).all() for p in tcp.parameters() if p.grad is not None)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,dh", [(4, 64), (4, 16)])
+def test_packed_attention_matches_fp32(heads, dh):
+    """The packed-projection attention (forward and d(qkv)) against fp32
+    softmax attention with the same key padding."""
+    from autodrive_b200.models.zoo import _PackedAttention, _key_padding_bias
+    torch.manual_seed(6)
+    b, t = 24, 101
+    d = heads * dh
+    qkv = (torch.randn(b, t, 3 * d, device="cuda") * .5).bfloat16().requires_grad_(True)
+    padding = torch.rand(b, t, device="cuda") > .6
+    padding[:, 0] = False                      # the context token is always valid
+    out = _PackedAttention.apply(qkv, _key_padding_bias(padding, heads, qkv.dtype), heads)
+    x = qkv.detach().float().requires_grad_(True)
+    q, k, v = x.view(b, t, 3, heads, dh).permute(2, 0, 3, 1, 4)
+    s = (q @ k.transpose(-1, -2)) / dh ** .5
+    s = s.masked_fill(padding[:, None, None, :], -torch.inf)
+    ref = (s.softmax(-1) @ v).transpose(1, 2).reshape(b, t, d)
+    assert out.shape == (b, t, d)
+    assert (out.float() - ref).abs().max().item() < 3e-2
+    w = torch.randn_like(ref)
+    (out.float() * w).sum().backward()
+    (ref * w).sum().backward()
+    rel = (qkv.grad.float() - x.grad).norm().item() / x.grad.norm().item()
+    assert rel < 3e-2, rel
+
+
+@pytest.mark.gpu
+def test_entity_attention_bf16_autocast_matches_fp32():
+    torch.manual_seed(7)
+    ref = PerceptionActorCritic("entity_attention_256", tensor_cores=False).cuda()
+    tcp = PerceptionActorCritic("entity_attention_256", tensor_cores=True).cuda()
+    tcp.load_state_dict(ref.state_dict())
+    b, e = 64, 120
+    g = torch.Generator(device="cuda").manual_seed(2)
+    d = {"scalars": torch.randn(b, 137, device="cuda", generator=g) * .5,
+         "entities": torch.randn(b, e, 12, device="cuda", generator=g) * .3,
+         "entity_mask": torch.rand(b, e, device="cuda", generator=g) > .3}
+    l1, _, v1 = ref(d)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        l2, _, v2 = tcp(d)
+    assert (l1 - l2.float()).abs().max().item() < 8e-2 * max(1., l1.abs().max().item())
+    assert (v1 - v2.float()).abs().max().item() < 8e-2 * max(1., v1.abs().max().item())
+    (l1.square().mean() + v1.square().mean()).backward()
+    (l2.float().square().mean() + v2.float().square().mean()).backward()
+    num = sum((p.grad - q.grad).square().sum() for p, q in zip(ref.parameters(), tcp.parameters()) if p.grad is not None)
+    den = sum(p.grad.square().sum() for p in ref.parameters() if p.grad is not None)
+    assert (num / den).sqrt().item() < 8e-2
+
+
+@pytest.mark.gpu
+def test_entity_attention_packed_tokens_match_padded():
+    """The variable-length form over valid tokens only gives the padded
+    form's outputs and gradients (both in bf16 autocast)."""
+    torch.manual_seed(8)
+    net = PerceptionActorCritic("entity_attention_256", tensor_cores=True).cuda()
+    b, e = 48, 150
+    g = torch.Generator(device="cuda").manual_seed(3)
+    mask = torch.rand(b, e, device="cuda", generator=g) < torch.rand(b, 1, device="cuda", generator=g)
+    mask[0] = False                            # a sample with no valid entity
+    d = {"scalars": torch.randn(b, 137, device="cuda", generator=g) * .5,
+         "entities": torch.randn(b, e, 12, device="cuda", generator=g) * .3, "entity_mask": mask}
+    pol = net.network
+    assert pol._packed_ok.__func__ is not None
+    outs, grads = [], []
+    for packed in (True, False):
+        net.zero_grad()
+        pol._packed_ok = (lambda _inputs, p=packed: p)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, _, value = net(d)
+        (logits.float().square().mean() + value.float().square().mean()).backward()
+        outs.append((logits.float(), value.float()))
+        grads.append(torch.cat([p.grad.flatten() for p in net.parameters() if p.grad is not None]))
+    del pol._packed_ok
+    for a, b_ in zip(*outs):
+        assert (a - b_).abs().max().item() < 3e-2 * max(1., b_.abs().max().item())
+    rel = (grads[0] - grads[1]).norm().item() / grads[1].norm().item()
+    assert rel < 3e-2, rel
