@@ -246,6 +246,16 @@ def _key_padding_bias(padding: Tensor, heads: int, dtype: torch.dtype) -> Tensor
     return bias.expand(b, heads, t, t)
 
 
+def _has_efficient_attention_ops() -> bool:
+    """PyTorch's memory-efficient attention entry points (private aten ops
+    that the packed and variable-length paths call directly)."""
+    return hasattr(torch.ops.aten, "_efficient_attention_forward") and \
+        hasattr(torch.ops.aten, "_efficient_attention_backward")
+
+
+_EFFICIENT_OPS = _has_efficient_attention_ops()
+
+
 class _PackedAttention(torch.autograd.Function):
     """Multi-head self-attention over a packed projection qkv (= [..., 3,
     heads, dh]) on PyTorch's memory-efficient attention kernel, called in its
@@ -317,7 +327,7 @@ class SelfAttention(nn.Module):
     def forward(self, x: Tensor, padding: Tensor) -> Tensor:
         b, t, d = x.shape
         qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
-        if qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16) and (d // self.heads) % 8 == 0:
+        if _EFFICIENT_OPS and qkv.is_cuda and qkv.dtype in (torch.bfloat16, torch.float16) and (d // self.heads) % 8 == 0:
             o = _PackedAttention.apply(qkv, _key_padding_bias(padding, self.heads, qkv.dtype), self.heads)
             return self.out_proj(o)
         q, k, v = qkv.view(b, t, 3, self.heads, d // self.heads).permute(2, 0, 3, 1, 4)
@@ -371,7 +381,8 @@ class EntityAttentionPolicy(nn.Module):
     def _packed_ok(self, inputs: dict) -> bool:
         x = inputs["entities"]
         dh = self.blocks[0].attention.dim // self.blocks[0].attention.heads if len(self.blocks) else 0
-        return (x.is_cuda and len(self.blocks) > 0 and dh % 8 == 0 and torch.is_autocast_enabled("cuda")
+        return (_EFFICIENT_OPS and x.is_cuda and len(self.blocks) > 0 and dh % 8 == 0
+                and torch.is_autocast_enabled("cuda")
                 and torch.get_autocast_dtype("cuda") in (torch.bfloat16, torch.float16))
 
     def _forward_packed(self, inputs: dict) -> tuple[Tensor, Tensor]:
