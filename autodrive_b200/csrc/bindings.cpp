@@ -74,9 +74,9 @@ SimParams params_from_dict(const py::dict& d) {
   I(n) I(R) I(P) I(substeps) I(contact_iterations) I(sweep_steps) I(dt) I(field_length) I(field_width)
   I(alliance_depth) I(wheel_radius) I(steer_current_limit) I(steer_rate_limit) I(steer_acceleration)
   I(motor_efficiency) I(battery_voltage) I(stall_torque) I(stall_current) I(free_speed_rpm) I(free_current)
-  I(nominal_voltage) I(module_x) I(module_y) I(fuel_physics) I(fr) I(fm) I(fk) I(fc) I(fmu) I(froll)
-  I(robot_height) I(max_comp) I(pair_damping) I(sleep) I(sleep_time) I(sleep_speed) I(sleep_ang)
-  I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule)
+  I(nominal_voltage) I(module_x) I(module_y) I(fuel_physics) I(fr) I(fm) I(fk) I(fc) I(fmu) I(froll) I(fg)
+  I(robot_height) I(max_comp) I(pair_damping) I(sleep) I(sleep_islands) I(sleep_time) I(sleep_speed) I(sleep_ang)
+  I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule) I(counter_defense)
   I(perception_interval) I(opponent_kind) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
   I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(stereo_tracks) I(sweeping) I(raster_lookahead) I(replan_interval)
   I(teammate_coordination) I(normalize_obs) I(horizon) I(max_speed_nominal) I(max_omega_nominal)

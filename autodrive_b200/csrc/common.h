@@ -106,6 +106,15 @@ AD_HD float clampf(float v, float lo, float hi) { return fminf(fmaxf(v, lo), hi)
 AD_HD float sgnf(float v) { return v > 0.f ? 1.f : (v < 0.f ? -1.f : 0.f); }
 AD_HD float sqr(float v) { return v * v; }
 AD_HD int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+// Product rounded on its own (never fused into a following add), so device and
+// host round a*b+c the same way.
+AD_HD float mul_rn(float a, float b) {
+#if defined(__CUDA_ARCH__)
+  return __fmul_rn(a, b);
+#else
+  return a * b;
+#endif
+}
 AD_HD float float_from_bits(uint32_t u) {
 #if defined(__CUDA_ARCH__)
   return __uint_as_float(u);

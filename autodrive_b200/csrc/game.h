@@ -20,7 +20,11 @@
 namespace ad {
 
 enum Mode : int { MODE_NONE = 0, MODE_NN = 1, MODE_DET = 2, MODE_DIRECT = 3 };
-enum OpponentKind : int { OPP_OFFENSE = 0, OPP_MIRROR, OPP_CUTOFF, OPP_VELOCITY_INTERCEPT, OPP_RANDOM };
+enum OpponentKind : int {
+  OPP_OFFENSE = 0, OPP_MIRROR, OPP_CUTOFF, OPP_VELOCITY_INTERCEPT, OPP_RANDOM,
+  // scripted defenders of the two-robot counter-defense task (slot 1)
+  OPP_DEF_INTERCEPT, OPP_DEF_LANE_BLOCK, OPP_DEF_FUEL_DENIAL, OPP_DEF_SHADOW, OPP_DEF_HUB_GUARD
+};
 
 // Accessor helpers for global state (env e, robot r, piece i).
 struct G {
@@ -280,6 +284,70 @@ AD_HD void attacker_objective(G& g, int r, const int32_t* possession, float& gx,
       gy = g.ty(r, i);
     }
   }
+}
+
+// Waypoint of a scripted defender (robot r) against `attacker`, built from
+// r's own pose estimate and its track of the attacker only
+// (frc_defense/tensor_defense_opponent.py:176-214): intercept ahead of the
+// attacker's motion (look-ahead = time to reach it, at most 1.25 s, plus
+// 0.55 m along its heading), block the attacker's lane to its HUB (40 % of
+// the way, at most 1 m), deny the nearest perceived FUEL (else block),
+// shadow 0.35 s ahead of it, or guard the HUB front along that lane. Without
+// a track (or, for FUEL denial, a FUEL candidate) the defender holds.
+AD_HD void defense_target(G& g, int r, int attacker, int kind, bool fuel_valid, int fuel_index, float& tx,
+                          float& ty) {
+  const SimParams& sp = g.sp;
+  World& w = g.w;
+  const size_t er = g.er(r);
+  const float* dp = g.ppose(r);
+  const float* ap = w.o_pose + er * 3;
+  const float* av = w.o_vel + er * 3;
+  bool tracked = w.o_valid[er] != 0;
+  const float vx = av[0], vy = av[1];
+  const float spd = sqrtf(vx * vx + vy * vy);
+  const float tox = dp[0] - ap[0], toy = dp[1] - ap[1];
+  const float dist = sqrtf(tox * tox + toy * toy), tn = fmaxf(dist, 1e-6f);
+  const float hx = spd > .15f ? vx / fmaxf(spd, .15f) : tox / tn;
+  const float hy = spd > .15f ? vy / fmaxf(spd, .15f) : toy / tn;
+  const float eta = clampf(dist / fmaxf(g.param(r, RP_SPEED), .1f), 0.f, 1.25f);
+  const int team = sp.team[attacker];
+  const float hubx = sp.hub_x[team], huby = sp.hub_y[team];
+  float lx = hubx - ap[0], ly = huby - ap[1];
+  const float hd = fmaxf(sqrtf(lx * lx + ly * ly), 1e-6f);
+  lx /= hd;
+  ly /= hd;
+  const float reach = fminf(hd * .4f, 1.f);
+  const float bx = ap[0] + lx * reach, by = ap[1] + ly * reach;
+  const float L = g.param(r, RP_LENGTH), W = g.param(r, RP_WIDTH);
+  const float guard = .595f + .5f * sqrtf(L * L + W * W) + .15f;
+  switch (kind) {
+    case OPP_DEF_FUEL_DENIAL:
+      tx = fuel_valid ? g.tx(r, fuel_index) : bx;
+      ty = fuel_valid ? g.ty(r, fuel_index) : by;
+      tracked = tracked || fuel_valid;
+      break;
+    case OPP_DEF_LANE_BLOCK:
+      tx = bx;
+      ty = by;
+      break;
+    case OPP_DEF_SHADOW:
+      tx = ap[0] + vx * .35f;
+      ty = ap[1] + vy * .35f;
+      break;
+    case OPP_DEF_HUB_GUARD:
+      tx = hubx - lx * guard;
+      ty = huby - ly * guard;
+      break;
+    default:  // intercept
+      tx = ap[0] + vx * eta + hx * .55f;
+      ty = ap[1] + vy * eta + hy * .55f;
+  }
+  if (!tracked) {
+    tx = dp[0];
+    ty = dp[1];
+  }
+  tx = clampf(tx, 0.f, sp.field_length);
+  ty = clampf(ty, 0.f, sp.field_width);
 }
 
 // ---------------------------------------------------------------------------
@@ -897,7 +965,11 @@ AD_HD void control_robot(G& g, int r, const int32_t* actions, const int32_t* pos
                        fdx, fdy, tx, ty, cs);
   }
   g.latch(r, RL_RASTER_SWEEP) = raster_sweep ? 1 : 0;
-  if (sp.R == 2 && r == 1 && mode == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
+  if (sp.R == 2 && r == 1 && mode == MODE_DET && sp.opponent_kind >= OPP_DEF_INTERCEPT) {
+    // scripted defender of the counter-defense task: a waypoint from its
+    // tracks, reached through the route planner and path follower
+    defense_target(g, r, 0, sp.opponent_kind, cand_valid[0], top.i[0], tx, ty);
+  } else if (sp.R == 2 && r == 1 && mode == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
     // scripted two-robot attacker variants steer straight at a derived point
     // (frc_defense/tensor_defense_step.py:108-180)
     float gx, gy;
@@ -1233,7 +1305,8 @@ AD_HD void synthesize_commands(G& g, const int32_t* possession) {
     omega[r] = om;
   }
   avoid_contention(g, cmd);
-  if (sp.R == 2 && sp.mode[1] == MODE_DET && sp.opponent_kind != OPP_OFFENSE) {
+  if (sp.R == 2 && sp.mode[1] == MODE_DET && sp.opponent_kind != OPP_OFFENSE &&
+      sp.opponent_kind < OPP_DEF_INTERCEPT) {
     const size_t er = g.er(1);
     const float* p = g.ppose(1);
     const float* tg = w.c_target + er * 2;

@@ -79,6 +79,18 @@ int scratch_for_current_device(float** out) {
   return AD_NOALLOC_OK;
 }
 
+// A failed launch may mean the device was reset (the cached address is then
+// stale): drop the current device's cached address so the next call looks it
+// up again.
+int forget_scratch_after_failure() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    g_partials_addr[dev] = nullptr;
+  }
+  return AD_NOALLOC_CUDA_ERROR;
+}
+
 }  // namespace
 
 extern "C" int ad_adam_fused_noalloc(float* params, const float* grads, float* exp_avg, float* exp_avg_sq,
@@ -90,16 +102,19 @@ extern "C" int ad_adam_fused_noalloc(float* params, const float* grads, float* e
   if (blocks < 0) return AD_NOALLOC_BAD_ARGUMENT;
   if (blocks == 0) blocks = kDefaultBlocks;
   if (blocks > AD_NOALLOC_MAX_BLOCKS) return AD_NOALLOC_TOO_MANY_BLOCKS;
+  if (cudaPeekAtLastError() != cudaSuccess) return AD_NOALLOC_PENDING_ERROR;
   float* partial = nullptr;
   int status = scratch_for_current_device(&partial);
   if (status != AD_NOALLOC_OK) return status;
   const float bias1 = 1.f - (float)std::pow((double)beta1, (double)step);
   const float bias2 = 1.f - (float)std::pow((double)beta2, (double)step);
   noalloc_sumsq_kernel<<<blocks, kThreads, 0, stream>>>(grads, n, partial);
+  if (cudaGetLastError() != cudaSuccess) return forget_scratch_after_failure();
   noalloc_apply_kernel<<<blocks, kThreads, 0, stream>>>(params, grads, exp_avg, exp_avg_sq, n, partial, blocks,
                                                         max_grad_norm, lr, beta1, beta2, eps, weight_decay,
                                                         bias1, bias2, grad_norm_out);
-  return cudaGetLastError() == cudaSuccess ? AD_NOALLOC_OK : AD_NOALLOC_CUDA_ERROR;
+  if (cudaGetLastError() != cudaSuccess) return forget_scratch_after_failure();
+  return AD_NOALLOC_OK;
 }
 
 extern "C" const char* ad_adam_fused_noalloc_message(int status) {
@@ -110,6 +125,8 @@ extern "C" const char* ad_adam_fused_noalloc_message(int status) {
     case AD_NOALLOC_TOO_MANY_BLOCKS:
       return "blocks exceeds AD_NOALLOC_MAX_BLOCKS (1024): the static scratch array holds 1024 partial sums";
     case AD_NOALLOC_CUDA_ERROR: return "CUDA error while locating the scratch array or launching the kernels";
+    case AD_NOALLOC_PENDING_ERROR:
+      return "an earlier CUDA call on this thread left an error pending; nothing was launched";
     default: return "unknown status";
   }
 }

@@ -18,9 +18,17 @@
 //   * `blocks` is the number of partial sums (and CTAs) to use; 0 selects the
 //     default of 296. More than AD_NOALLOC_MAX_BLOCKS is rejected with
 //     AD_NOALLOC_TOO_MANY_BLOCKS before any work is launched.
+//   * `stream` must belong to the device that is current on the calling
+//     thread: the scratch address used is the current device's.
 //   * The first call on each device looks up the device address of the
 //     scratch array (cudaGetSymbolAddress) with that device current; make
-//     that first call outside any stream capture.
+//     that first call outside any stream capture. The address is cached per
+//     device ordinal; it is not valid after cudaDeviceReset, so a call whose
+//     launch fails drops the cached address and the next call looks it up
+//     again.
+//   * A CUDA error left pending by an earlier call on this thread is not
+//     attributed to this call: the call launches nothing and returns
+//     AD_NOALLOC_PENDING_ERROR (the error stays pending for its owner).
 //   * All calls share the one scratch array. Each call overwrites the
 //     entries it reads before reading them, so nothing carries over from the
 //     previous call, but calls that overlap on the GPU (different streams, or
@@ -37,6 +45,7 @@ enum AdNoallocStatus {
   AD_NOALLOC_BAD_ARGUMENT = 1,
   AD_NOALLOC_TOO_MANY_BLOCKS = 2,
   AD_NOALLOC_CUDA_ERROR = 3,
+  AD_NOALLOC_PENDING_ERROR = 4,
 };
 
 #ifdef __cplusplus

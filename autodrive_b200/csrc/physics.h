@@ -1172,7 +1172,7 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
       float wn = sqrtf(sqr(s.fang[0][i]) + sqr(s.fang[1][i]) + sqr(s.fang[2][i]));
       if (sqrtf(vx * vx + vy * vy + vz * vz) >= sp.sleep_speed || wn >= sp.sleep_ang) s.sleep[i] = 0;
       if (!s.sleep[i]) {
-        vz -= kG * h;
+        vz -= sp.fg * h;
         s.fvel[2][i] = vz;
         s.fpos[0][i] += vx * h;
         s.fpos[1][i] += vy * h;
@@ -1318,6 +1318,134 @@ AD_HD void fuel_pre(TickShared& s, const SimParams& sp, float h, const Group& g)
   PHASE_MARK_BY(s, 7, g.first);
 }
 
+// ---- island sleep (frc_defense/fuel_physics_sleep.py) ------------------------
+// Free spheres that touch (centre distance <= 2r) form islands (union-find,
+// roots linked towards the smaller index). An island is stable when one of
+// its spheres rests on its support and every sphere is quiet (speed and spin
+// under the sleep thresholds, no robot chassis within r + 2 mm below the
+// chassis top); a stable island's clock is its members' minimum clock plus
+// the substep, an unstable island's is zero, and the whole island sleeps once
+// the clock reaches sleep_time. A sleeping island touched by an awake sphere
+// merges with it and wakes as a whole. The partition and the per-island
+// minimum / flags do not depend on the order of unions, so the GPU and the
+// serial host twin decide the same.
+AD_HD int uf_find(int* parent, int i) {
+#if defined(__CUDA_ARCH__)
+  volatile int* p = parent;
+  while (true) {
+    const int q = p[i];
+    if (q == i) return i;
+    const int gq = p[q];
+    if (gq != q) p[i] = gq;   // path halving: only ever points to an ancestor
+    i = q;
+  }
+#else
+  while (parent[i] != i) {
+    parent[i] = parent[parent[i]];
+    i = parent[i];
+  }
+  return i;
+#endif
+}
+
+AD_HD void uf_unite(int* parent, int a, int b) {
+  while (true) {
+    a = uf_find(parent, a);
+    b = uf_find(parent, b);
+    if (a == b) return;
+    if (a < b) {
+      const int t = a;
+      a = b;
+      b = t;
+    }
+#if defined(__CUDA_ARCH__)
+    if (atomicCAS(&parent[a], a, b) == a) return;
+#else
+    parent[a] = b;
+    return;
+#endif
+  }
+}
+
+AD_HD void island_sleep(TickShared& s, const SimParams& sp, float h) {
+  const int P = sp.P;
+  // the Jacobi scratch (dv) is dead until the next substep's pair phase
+  int* parent = reinterpret_cast<int*>(s.dv[0]);
+  int* flags = reinterpret_cast<int*>(s.dv[1]);          // bit 0: a member is not quiet, bit 1: supported
+  uint32_t* minclk = reinterpret_cast<uint32_t*>(s.dv[2]);
+  const float r2 = 2.f * sp.fr;
+  PAR_FOR(i, P) {
+    parent[i] = i;
+    flags[i] = 0;
+    minclk[i] = 0x7f7fffffu;   // FLT_MAX; clocks are non-negative, so their bits order like the values
+  }
+  BARRIER();
+  PAR_FOR(i, P) {
+    if (!s.freem[i]) continue;
+    const float px = s.fpos[0][i], py = s.fpos[1][i], pz = s.fpos[2][i];
+    const float inv_cell = 1.f / sp.grid_cell, reach = r2 + 1e-4f;
+    const int x0 = clampi((int)floorf((px - reach) * inv_cell), 0, sp.grid_nx - 1);
+    const int x1 = clampi((int)floorf((px + reach) * inv_cell), 0, sp.grid_nx - 1);
+    const int y0 = clampi((int)floorf((py - reach) * inv_cell), 0, sp.grid_ny - 1);
+    const int y1 = clampi((int)floorf((py + reach) * inv_cell), 0, sp.grid_ny - 1);
+    for (int yy = y0; yy <= y1; ++yy) {
+      const int row = yy * sp.grid_nx;
+      const int m_end = s.cell_start[row + x1 + 1];
+      for (int m = s.cell_start[row + x0]; m < m_end; ++m) {
+        const int j = s.sorted[m];
+        if (j <= i) continue;
+        const float d2 = sqr(px - s.fpos[0][j]) + sqr(py - s.fpos[1][j]) + sqr(pz - s.fpos[2][j]);
+        if (d2 <= r2 * r2) uf_unite(parent, i, j);
+      }
+    }
+  }
+  BARRIER();
+  PAR_FOR(i, P) {
+    if (!s.freem[i]) continue;
+    const bool on_floor = s.fpos[2][i] < s.support[i] + sp.fr + .005f;
+    const float svz = s.fvel[2][i] - ((on_floor && !s.sleep[i]) ? sp.fg * h : 0.f);
+    const float sv = sqrtf(sqr(s.fvel[0][i]) + sqr(s.fvel[1][i]) + svz * svz);
+    const float wn = sqrtf(sqr(s.fang[0][i]) + sqr(s.fang[1][i]) + sqr(s.fang[2][i]));
+    bool quiet = sv < sp.sleep_speed && wn < sp.sleep_ang;
+    for (int r = 0; r < sp.R && quiet; ++r) {
+      const float dx = s.fpos[0][i] - s.pose[r * 3], dy = s.fpos[1][i] - s.pose[r * 3 + 1];
+      const float co = s.rtrig[r * 4 + 0], si = s.rtrig[r * 4 + 1];
+      float nx, ny, dist;
+      box_normal2(co * dx + si * dy, -si * dx + co * dy, .5f * rparam(s, r, RP_LENGTH),
+                  .5f * rparam(s, r, RP_WIDTH), nx, ny, dist);
+      if (dist <= sp.fr + .002f && s.fpos[2][i] < sp.robot_height + sp.fr) quiet = false;
+    }
+    const int root = uf_find(parent, i);
+    const int bits = (quiet ? 0 : 1) | (on_floor ? 2 : 0);
+#if defined(__CUDA_ARCH__)
+    if (bits) atomicOr(&flags[root], bits);
+    atomicMin(&minclk[root], float_bits(s.clock[i]));
+#else
+    flags[root] |= bits;
+    const uint32_t cb = float_bits(s.clock[i]);
+    if (cb < minclk[root]) minclk[root] = cb;
+#endif
+  }
+  BARRIER();
+  PAR_FOR(i, P) {
+    if (!s.freem[i]) continue;
+    const int root = uf_find(parent, i);
+    const int f = flags[root];
+    const bool stable = (f & 2) && !(f & 1);
+    const float elapsed = stable ? float_from_bits(minclk[root]) + h : 0.f;
+    const bool asleep = stable && elapsed >= sp.sleep_time;
+    s.clock[i] = elapsed;
+    s.sleep[i] = asleep ? 1 : 0;
+    if (asleep) {
+      for (int k = 0; k < 3; ++k) {
+        s.fvel[k][i] = 0.f;
+        s.fang[k][i] = 0.f;
+      }
+    }
+  }
+  BARRIER();
+}
+
 // FUEL phases coupled to the robots (chassis contacts with reciprocal robot
 // impulses), then terrain / walls / field boxes and sleep; whole CTA.
 AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
@@ -1430,13 +1558,13 @@ AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
         box_normal2(s.fpos[0][i] - bx.cx, s.fpos[1][i] - bx.cy, bx.hx, bx.hy, nx, ny, dist);
         static_contact_fuel(s, sp, i, V3{nx, ny, 0.f}, sp.fr - dist, low, h);
       }
-      // sleep update
+      // sleep update (per sphere; island mode decides below)
       if (!sp.sleep) {
         s.sleep[i] = 0;
-      } else {
+      } else if (!sp.sleep_islands) {
         float sup = s.support[i];
         bool on_floor = s.fpos[2][i] < sup + sp.fr + .005f;
-        float svz = s.fvel[2][i] - ((on_floor && !s.sleep[i]) ? kG * h : 0.f);
+        float svz = s.fvel[2][i] - ((on_floor && !s.sleep[i]) ? sp.fg * h : 0.f);
         float sv = sqrtf(sqr(s.fvel[0][i]) + sqr(s.fvel[1][i]) + svz * svz);
         float wn = sqrtf(sqr(s.fang[0][i]) + sqr(s.fang[1][i]) + sqr(s.fang[2][i]));
         bool quiet = sv < sp.sleep_speed && wn < sp.sleep_ang && on_floor;
@@ -1452,6 +1580,7 @@ AD_HD void fuel_post(TickShared& s, const SimParams& sp, float h) {
     }
   }
   BARRIER();
+  if (sp.sleep && sp.sleep_islands) island_sleep(s, sp, h);
   PHASE_MARK(s, 9);
 }
 

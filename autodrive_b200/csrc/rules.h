@@ -41,7 +41,7 @@ AD_HD void launch_piece(TickShared& s, const SimParams& sp, int i, float px, flo
   } else {
     float z = fmaxf(height, sp.fr);
     s.fpos[2][i] = z;
-    s.fvel[2][i] = (sp.fr - z) / flight + .5f * kG * flight;
+    s.fvel[2][i] = (sp.fr - z) / flight + .5f * sp.fg * flight;
   }
   s.fvel[0][i] = vx;
   s.fvel[1][i] = vy;

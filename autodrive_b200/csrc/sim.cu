@@ -252,6 +252,13 @@ AD_HD void tick_env(World& w, const SimParams& sp, TickShared& s, int e, uint32_
       else blue += sc;
     }
     for (int r = 0; r < sp.R; ++r) w.g_reward[g.er(r)] = sp.team[r] == 0 ? red - blue : blue - red;
+  } else if (sp.counter_defense) {
+    // counter-defense: the learner (slot 0) attacks; scores plus a small
+    // acquisition bonus and a per-tick cost (frc_defense/tensor_defense_step.py:198-203)
+    const float own = (float)g.rcount(0, RC_SCORED_EVENT);
+    const float acq = (float)g.rcount(0, RC_ACQUIRED_EVENT);
+    w.g_reward[g.er(0)] = own + .05f * acq - .001f;
+    w.g_reward[g.er(1)] = -own;
   } else {
     // two-robot defence: the learner (slot 0) is scored against the attacker (slot 1)
     float atk = (float)g.rcount(1, RC_SCORED_EVENT);
@@ -364,8 +371,7 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
   PlanScratch ps;
   float* f = reinterpret_cast<float*>(smem);
   ps.value = f;
-  ps.value2 = f + nc;
-  ps.path = f + 2 * nc;
+  ps.path = f + nc;
   ps.tmp = ps.path + kPathPoints * 2;
   ps.misc = reinterpret_cast<int*>(ps.tmp + kPathPoints * 2 + 4);
   ps.blocked = reinterpret_cast<uint8_t*>(ps.misc + 8);
@@ -429,7 +435,7 @@ std::vector<unsigned long long> sense_profile_read() {
 
 size_t plan_smem_bytes(const SimParams& sp) {
   const int nc = sp.plan_nx * sp.plan_ny;
-  return (size_t)(2 * nc + kPathPoints * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc + 16;
+  return (size_t)(nc + kPathPoints * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc + 16;
 }
 
 void validate_params(const SimParams& sp) {
@@ -543,11 +549,10 @@ void host_control(World w, const SimParams& sp, const int32_t* actions) {
 void host_plan(World w, const SimParams& sp, int force) {
   const int nc = sp.plan_nx * sp.plan_ny;
   host_parallel(sp.n * sp.R, [&](int, int b, int end) {
-    std::vector<float> fbuf(2 * nc + kPathPoints * 4 + 4);
+    std::vector<float> fbuf(nc + kPathPoints * 4 + 4);
     std::vector<uint8_t> blocked(nc);
     int misc[8];
-    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + 2 * nc,
-                   fbuf.data() + 2 * nc + kPathPoints * 2, misc};
+    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + kPathPoints * 2, misc};
     for (int row = b; row < end; ++row) {
       const int e = row / sp.R, r = row % sp.R;
       if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;

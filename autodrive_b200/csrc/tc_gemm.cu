@@ -24,8 +24,14 @@
 //           activation, fp32 or bf16 stores with bounds checks.
 // With two accumulators the epilogue of tile i overlaps the loads and MMAs
 // of tile i+1. Out-of-range tile parts are zero-filled by the TMA unit.
-// Every mbarrier wait is bounded in wall-clock time; a wait that runs out
-// sets a bit in a device status word and the CTA drains and exits.
+// Every mbarrier wait is bounded in wall-clock time (`wait_ns`, 2 s by
+// default); a wait that runs out sets a bit in a device status word
+// (1 producer/stage free, 2 MMA/stage loaded, 4 epilogue/accumulator full,
+// 8 MMA/accumulator free) and a shared failure flag that stops the other
+// roles. Before the CTA frees its TMEM and exits it drains what it already
+// issued: the producer waits for its last loads to land and the MMA warp
+// commits its issued MMAs to a drain barrier and waits for it (each wait
+// bounded by 200 ms; a drain that gives up sets bit 16 or 32).
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cuda.h>
@@ -45,7 +51,7 @@ constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kTileBytes = 128 * 128;        // one 128 x 64 bf16 operand tile
 constexpr uint32_t kStageBytes = 2 * kTileBytes;
-constexpr uint64_t kWaitNs = 2000000000ull;       // 2 s
+constexpr uint64_t kDrainNs = 200000000ull;       // 200 ms for in-flight copies / MMAs after a failure
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
 constexpr uint32_t kAccCols = 128;                // one fp32 accumulator: 128 lanes x 128 columns
 
@@ -61,6 +67,7 @@ struct GemmArgs {
   int splits;          // split-K slices (1: no split)
   int64_t split_stride;  // elements between the fp32 partial outputs of two slices
   int* status;
+  uint64_t wait_ns;    // limit of every pipeline wait
 };
 
 __device__ __forceinline__ float apply_act(float x, int act) {
@@ -143,6 +150,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   const uint32_t tempty0 = tfull0 + 16;                  // 2 mbarriers: accumulator read out
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kStages + 4));
   int* s_fail = reinterpret_cast<int*>(misc + 8 * (2 * kStages + 4) + 8);
+  const uint32_t drain = tc::smem_u32(misc + 8 * (2 * kStages + 4) + 16);  // MMA drain after a failure
   volatile int* fail = s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,6 +167,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       tc::mbar_init(tfull0 + 8 * a, 1);
       tc::mbar_init(tempty0 + 8 * a, 128);   // every epilogue thread arrives
     }
+    tc::mbar_init(drain, 1);
     tc::mbar_init_fence();
     *s_fail = 0;
   }
@@ -179,7 +188,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
       for (int kt = kb; kt < ke; ++kt, ++it) {
         const uint32_t s = it % kStages;
-        if (it >= kStages && !tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, kWaitNs)) {
+        if (it >= kStages && !tc::mbar_wait(empty0 + 8 * s, ((it / kStages) - 1) & 1, g.wait_ns)) {
           atomicOr(g.status, 1);
           atomicExch(s_fail, 1);
           break;
@@ -204,6 +213,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         }
       }
     }
+    if (*fail) {
+      // `it` loads were issued; every stage's latest one may still be in
+      // flight (earlier ones were consumed). Wait for them to land.
+      for (uint32_t i = it > (uint32_t)kStages ? it - kStages : 0u; i < it; ++i)
+        if (!tc::mbar_wait(full0 + 8 * (i % kStages), (i / kStages) & 1, kDrainNs)) atomicOr(g.status, 16);
+    }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer: tile lt accumulates into TMEM columns (lt & 1) * 128 ----
     const uint32_t id = tc::idesc_bf16(kBM, kBN, A_MN, B_MN);
@@ -213,7 +228,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       const TileCoord t = tile_of(w, tiles_n, tiles_m);
       const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
       const int acc = lt & 1;
-      if (lt >= 2 && !tc::mbar_wait(tempty0 + 8 * acc, ((lt >> 1) - 1) & 1, kWaitNs)) {
+      if (lt >= 2 && !tc::mbar_wait(tempty0 + 8 * acc, ((lt >> 1) - 1) & 1, g.wait_ns)) {
         atomicOr(g.status, 8);
         atomicExch(s_fail, 1);
         break;
@@ -223,7 +238,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       bool ok = true;
       for (int kt = kb; kt < ke; ++kt, ++it) {
         const uint32_t s = it % kStages;
-        if (!tc::mbar_wait(full0 + 8 * s, (it / kStages) & 1, kWaitNs)) {
+        if (!tc::mbar_wait(full0 + 8 * s, (it / kStages) & 1, g.wait_ns)) {
           atomicOr(g.status, 2);
           atomicExch(s_fail, 1);
           ok = false;
@@ -243,6 +258,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       tc::mma_commit(tfull0 + 8 * acc);   // accumulator complete (or nothing issued)
       if (!ok) break;
     }
+    if (*fail) {
+      // MMAs issued so far may still read shared memory / write TMEM
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0, kDrainNs)) atomicOr(g.status, 32);
+    }
   }
 
   if (warp >= 2) {
@@ -252,8 +272,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++lt) {
       const TileCoord t = tile_of(w, tiles_n, tiles_m);
       const int acc = lt & 1;
-      const bool got = tc::mbar_wait(tfull0 + 8 * acc, (lt >> 1) & 1, kWaitNs);
-      if (!got) atomicOr(g.status, 4);
+      const bool got = tc::mbar_wait(tfull0 + 8 * acc, (lt >> 1) & 1, g.wait_ns);
+      if (!got) {
+        atomicOr(g.status, 4);
+        atomicExch(s_fail, 1);
+      }
       if (!got || *fail) break;
       tc::tc_fence_after();
       const int row = t.m0 + 32 * q + lane;
@@ -339,7 +362,8 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cud
 // stored [K][N] (else [N][K]). Storage row strides must be multiples of 8
 // elements and the base pointers 16-byte aligned (TMA rules).
 void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c,
-             c10::optional<torch::Tensor> bias, int64_t act, bool accumulate, torch::Tensor status) {
+             c10::optional<torch::Tensor> bias, int64_t act, bool accumulate, torch::Tensor status,
+             int64_t wait_ns) {
   for (auto* t : {&a, &b, &c, &status})
     TORCH_CHECK(t->is_cuda() && t->dim() >= 1, "tc_gemm operands must be CUDA tensors");
   TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
@@ -358,6 +382,7 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   TORCH_CHECK(c.scalar_type() == torch::kFloat32 || c.scalar_type() == torch::kBFloat16, "output fp32 or bf16");
   TORCH_CHECK(!accumulate || c.scalar_type() == torch::kFloat32, "accumulate needs an fp32 output");
   TORCH_CHECK(status.scalar_type() == torch::kInt32, "status must be int32");
+  TORCH_CHECK(wait_ns >= 0, "wait_ns must be non-negative");
   TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "tc_gemm dimensions too large");
   if (M == 0 || N == 0) return;
   GemmArgs g{};
@@ -376,6 +401,7 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   g.act = (int)act;
   g.accumulate = accumulate ? 1 : 0;
   g.status = status.data_ptr<int>();
+  g.wait_ns = (uint64_t)wait_ns;
   if (K == 0) {  // empty contraction: C = act(bias) (or unchanged when accumulating zero)
     auto z = torch::zeros({M, N}, c.options().dtype(torch::kFloat32));
     if (g.bias) z += *bias;
@@ -431,5 +457,5 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
 void register_tc_gemm_ops(py::module& m) {
   m.def("tc_gemm", &tc_gemm, "bf16 tcgen05 GEMM C = op(A) op(B)^T (+bias, activation), TMA-fed, fp32 accumulate",
         py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("c"), py::arg("bias"),
-        py::arg("act"), py::arg("accumulate"), py::arg("status"));
+        py::arg("act"), py::arg("accumulate"), py::arg("status"), py::arg("wait_ns") = 2000000000ll);
 }

@@ -171,10 +171,11 @@ struct SimParams {
   float free_current = 2.f, nominal_voltage = 12.f, module_x = .36f, module_y = .36f;
   // fuel physics
   int fuel_physics = 1;         // 0: static FUEL (no contact dynamics)
-  float fr = .075f, fm = .215f, fk = 2000.f, fc = 40.f, fmu = .45f, froll = .20f;
+  float fr = .075f, fm = .215f, fk = 2000.f, fc = 40.f, fmu = .45f, froll = .20f, fg = 9.81f;
   float robot_height = .5f, max_comp = .5f;
   float pair_damping = 160.f;
   int sleep = 1;
+  int sleep_islands = 0;         // 1: whole contact islands sleep and wake together
   float sleep_time = .5f, sleep_speed = .025f, sleep_ang = .5f;
   float grid_cell = .2f;
   int grid_nx = 83, grid_ny = 41;
@@ -182,6 +183,7 @@ struct SimParams {
   // game rules
   float fuel_radius_rules = .0825f;   // intake/track geometry radius
   int two_robot_schedule = 0;   // 0: 3v3 REBUILT shifts; 1: two-robot 20 s + 30 s alternation
+  int counter_defense = 0;      // two-robot task: 1 = slot 0 attacks (learner), slot 1 defends (scripted)
   int opponent_kind = 0;        // two-robot attacker: 0 offense/adstar, 1 mirror, 2 cutoff,
                                 // 3 velocity_intercept, 4 random
   int perception_interval = 2;

@@ -442,6 +442,15 @@ ARCHITECTURES = {
 
 # raster resolution (rows, cols) each architecture expects
 FIELD_SHAPE = {"raster_cnn_large": (64, 128)}
+# perception-dictionary entries each architecture reads (a rollout stores only these)
+INPUT_KEYS = {
+    "baseline_mlp": ("scalars",), "residual_mlp": ("scalars",),
+    "deep_sets": ("scalars", "entities", "entity_mask"),
+    "entity_attention": ("scalars", "entities", "entity_mask"),
+    "entity_attention_256": ("scalars", "entities", "entity_mask"),
+    "full_field_cnn": ("scalars", "field"), "full_field_resnet": ("scalars", "field"),
+    "field_fno": ("scalars", "field"), "raster_cnn_large": ("scalars", "field"),
+}
 
 
 class PerceptionActorCritic(nn.Module):
@@ -462,6 +471,7 @@ class PerceptionActorCritic(nn.Module):
         if tensor_cores:
             tensorize(self.network)
         self.field_shape = FIELD_SHAPE.get(architecture, (32, 64))
+        self.input_keys = INPUT_KEYS[architecture]
 
     def forward(self, inputs: dict):
         logits, value = self.network(inputs)

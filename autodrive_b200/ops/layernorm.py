@@ -16,6 +16,7 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from ..utils import launches
 from .ext import require_extension
 
 WIDTHS = (64, 128, 256, 512)
@@ -26,6 +27,7 @@ class _LayerNormBf16Fn(torch.autograd.Function):
     def forward(ctx, x, weight, bias, eps):
         d = x.shape[-1]
         x2 = x.reshape(-1, d).to(torch.bfloat16).contiguous()
+        launches.add(1)
         y, mean, rstd = require_extension().layer_norm_bf16_fwd(x2, weight.detach().float().contiguous(),
                                                                 bias.detach().float().contiguous(), float(eps))
         ctx.save_for_backward(x2, weight, mean, rstd)
@@ -37,6 +39,7 @@ class _LayerNormBf16Fn(torch.autograd.Function):
         x2, weight, mean, rstd = ctx.saved_tensors
         d = x2.shape[-1]
         g = gy.reshape(-1, d).to(torch.bfloat16).contiguous()
+        launches.add(1)
         dx, dw, db = require_extension().layer_norm_bf16_bwd(g, x2, weight.detach().float().contiguous(), mean, rstd)
         dx = dx.reshape(ctx.in_shape)
         return (dx if ctx.in_dtype == torch.bfloat16 else dx.to(ctx.in_dtype)), dw, db, None

@@ -19,6 +19,7 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from ..utils import launches
 from .ext import require_extension
 
 ACTS = {None: 0, "none": 0, "tanh": 1, "relu": 2}
@@ -50,27 +51,113 @@ def _result_dtype(x: torch.Tensor) -> torch.dtype:
     return x.dtype
 
 
+class TensorCoreTimeout(RuntimeError):
+    """A bounded pipeline wait of the tcgen05 GEMM ran out; results of the
+    GEMMs since the last check are not valid."""
+
+
+_PHASES = ((1, "producer: stage free"), (2, "MMA: stage loaded"), (4, "epilogue: accumulator full"),
+           (8, "MMA: accumulator free"), (16, "drain of in-flight loads"), (32, "drain of in-flight MMAs"))
+
+
+def _describe(word: int) -> str:
+    return ", ".join(name for bit, name in _PHASES if word & bit) or f"status {word:#x}"
+
+
 class _Status:
-    tensors: dict = {}
+    """Per-device GEMM status word, read back without stalling the stream.
+
+    Every GEMM ORs a bit into the word when one of its bounded waits runs
+    out. Every `poll_every` launches (and at `check_gemm_status`) the word is
+    copied into pinned host memory behind an event; a later call that finds
+    the event complete reads it, clears the word and raises
+    `TensorCoreTimeout` naming the failed phases.
+    """
+    poll_every = 64
+    _state: dict = {}
+
+    @classmethod
+    def _entry(cls, device):
+        key = str(device)
+        e = cls._state.get(key)
+        if e is None:
+            word = torch.zeros(1, dtype=torch.int32, device=device)
+            host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+            e = {"word": word, "host": host, "event": None, "launches": 0}
+            cls._state[key] = e
+        return e
 
     @classmethod
     def get(cls, device) -> torch.Tensor:
-        key = str(device)
-        if key not in cls.tensors:
-            cls.tensors[key] = torch.zeros(1, dtype=torch.int32, device=device)
-        return cls.tensors[key]
+        return cls._entry(device)["word"]
+
+    @classmethod
+    def _consume(cls, e, block: bool) -> None:
+        ev = e["event"]
+        if ev is None:
+            return
+        if not block and not ev.query():
+            return
+        ev.synchronize()
+        e["event"] = None
+        value = int(e["host"][0])
+        if value:
+            e["word"].zero_()
+            raise TensorCoreTimeout(f"tcgen05 GEMM wait ran out ({_describe(value)})")
+
+    @classmethod
+    def _post(cls, e) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return
+        e["host"].copy_(e["word"], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        e["event"] = ev
+
+    @classmethod
+    def after_launch(cls, device) -> None:
+        e = cls._entry(device)
+        e["launches"] += 1
+        if e["event"] is not None:
+            cls._consume(e, block=False)
+        if e["event"] is None and e["launches"] % cls.poll_every == 0:
+            cls._post(e)
+
+    @classmethod
+    def check(cls, device, block: bool = True) -> None:
+        e = cls._entry(device)
+        cls._consume(e, block=True)
+        if torch.cuda.is_current_stream_capturing():
+            return
+        cls._post(e)
+        if block:
+            cls._consume(e, block=True)
+
+
+def check_gemm_status(device=None, block: bool = True) -> None:
+    """Raise `TensorCoreTimeout` if a tcgen05 GEMM on `device` (default: the
+    current CUDA device) reported a timed-out wait since the last check. With
+    block=False only an already finished read-back is examined and a new one
+    is queued."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    _Status.check(dev, block)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, bias=None, act=None,
-         out: torch.Tensor | None = None, accumulate: bool = False, out_dtype=torch.float32) -> torch.Tensor:
+         out: torch.Tensor | None = None, accumulate: bool = False, out_dtype=torch.float32,
+         wait_ns: int = 2_000_000_000) -> torch.Tensor:
     """C = op(A) op(B)^T on the tensor cores; A is [M,K] (or [K,M] when a_mn),
-    B is [N,K] (or [K,N] when b_mn); both bf16 with row strides % 8 == 0."""
+    B is [N,K] (or [K,N] when b_mn); both bf16 with row strides % 8 == 0.
+    `wait_ns` bounds every pipeline wait inside the kernel (tests shorten it
+    to make a wait run out); timeouts surface through `check_gemm_status`."""
     ext = require_extension()
     m = a.shape[1] if a_mn else a.shape[0]
     n = b.shape[1] if b_mn else b.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
-    ext.tc_gemm(a, a_mn, b, b_mn, out, bias, ACTS[act], accumulate, _Status.get(a.device))
+    ext.tc_gemm(a, a_mn, b, b_mn, out, bias, ACTS[act], accumulate, _Status.get(a.device), int(wait_ns))
+    launches.add(1)
+    _Status.after_launch(a.device)
     return out
 
 

@@ -21,6 +21,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import require_extension
+from ..utils import launches
 from . import dist as pdist
 
 
@@ -70,6 +71,7 @@ class FusedAllReduceAdam:
         opt = self.opt
         opt.flat.sync_grads()
         opt.step_count += 1
+        launches.add(1)
         self.ext.peer_comm_step(self.comm, self.m, self.v, opt.last_norm, opt.step_count, opt.lr,
                                 opt.betas[0], opt.betas[1], opt.eps, opt.weight_decay, opt.max_grad_norm,
                                 self.max_wait_iters)
@@ -102,6 +104,9 @@ class FusedAllReduceAdam:
                 self._status_event = torch.cuda.Event()
             self._status_event.record()
         if code:
+            # the word is cleared so a caller that recovers (or a later check)
+            # sees only new expiries
+            self.comm.status.zero_()
             phase = {1: "gradients-ready", 2: "norm exchange", 4: "completion", 8: "stats exchange",
                      16: "parameter broadcast"}.get(code, str(code))
             raise PeerCommError(f"peer all-reduce wait expired in the {phase} barrier on rank {self.rank}")

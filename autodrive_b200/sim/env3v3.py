@@ -484,30 +484,41 @@ class TensorThreeVsThreeEnv:
         self._last_obs = self.ws["obs"]
         return self._last_obs, rewards, done, truncated, info
 
-    def step_held(self, actions, ticks: int, *, use_graph: bool = True):
+    def step_held(self, actions, ticks: int, *, use_graph: bool = True, observe_every_tick: bool = False):
         """Advance every world `ticks` ticks under one held action and build
         the final observation; returns (obs, summed rewards, truncated).
+
+        `observe_every_tick` builds the strategic observation after every
+        tick instead of only after the last one (the intermediate ones are
+        overwritten; this is the cost of a rollout that records observations
+        at the physics rate).
 
         On CUDA the interval is captured once as a CUDA graph (control, plan
         and tick kernels per tick plus observe) and replayed afterwards.
         """
         self._set_actions(actions)
         ticks = int(ticks)
+        observe_every_tick = bool(observe_every_tick)
+
+        def interval(reward_buf):
+            for k in range(ticks):
+                self._launch_tick()
+                reward_buf.add_(self.ws["g_reward"])
+                if observe_every_tick and k < ticks - 1:
+                    self.ws.sim.observe()
+            self.ws.sim.observe()
+
         if self.device.type == "cuda" and use_graph:
-            key = ("held", ticks)
+            key = ("held", ticks, observe_every_tick)
             entry = self._graphs.get(key)
             if entry is None:
                 reward_buf = torch.zeros((self.n, NUM_ROBOTS), device=self.device)
                 stream = torch.cuda.Stream(device=self.device)
                 stream.wait_stream(torch.cuda.current_stream(self.device))
-                # warm the launch path (attribute setup) outside capture
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph, stream=stream):
                     reward_buf.zero_()
-                    for _ in range(ticks):
-                        self._launch_tick()
-                        reward_buf.add_(self.ws["g_reward"])
-                    self.ws.sim.observe()
+                    interval(reward_buf)
                 entry = (graph, reward_buf)
                 self._graphs[key] = entry
             graph, reward_buf = entry
@@ -516,10 +527,7 @@ class TensorThreeVsThreeEnv:
             rewards = reward_buf
         else:
             rewards = torch.zeros((self.n, NUM_ROBOTS), device=self.device)
-            for _ in range(ticks):
-                self._launch_tick()
-                rewards += self.ws["g_reward"]
-            self.ws.sim.observe()
+            interval(rewards)
         truncated = self.steps >= self.horizon
         self._last_obs = self.ws["obs"]
         return self._last_obs, rewards, truncated

@@ -1,7 +1,24 @@
-"""Two-robot REBUILT defense environment (`TensorDefenseEnv`).
+"""Two-robot REBUILT environment (`TensorDefenseEnv`).
 
-Slot 0 is the learner (defense) and slot 1 the scripted attacker, as in
-frc_defense/tensor_sim.py:82-398 with task="defense". Action modes:
+Slot 0 is the learner and slot 1 the scripted opponent
+(frc_defense/tensor_sim.py:82-398). Tasks:
+
+* ``counter_defense`` (default): the learner attacks (collects and scores
+  FUEL) against a scripted defender; reward = own scores + 0.05 per
+  acquisition - 0.001 per tick. Defenders (``opponent=``): ``guard`` (the
+  default, alias ``adstar_defender``) runs ``defense_mode`` (``INTERCEPT``
+  default, ``LANE_BLOCK``, ``FUEL_DENIAL``, ``SHADOW``, ``HUB_GUARD``), or
+  one of those modes by name (``intercept``, ``lane_block``, ``fuel_denial``,
+  ``shadow``, ``hub_guard``); ``cutoff`` / ``velocity_intercept`` alias
+  ``intercept``, ``mirror`` / ``pursuit`` alias ``shadow``, and ``random``
+  drives random velocity commands. A defender builds its waypoint from its
+  own tracks of the attacker and reaches it through the route planner
+  (frc_defense/tensor_defense_opponent.py:176-214).
+* ``defense``: the learner defends against a scripted attacker; reward =
+  -attacker scores - 0.02 per attacker acquisition - 0.001 per tick + a
+  lane-position bonus.
+
+Action modes:
 
 * ``strategic`` (default, 8 categorical actions, 137 observations):
   collect x4 / shoot / defend / ferry / hold, executed by the native
@@ -11,12 +28,21 @@ frc_defense/tensor_sim.py:82-398 with task="defense". Action modes:
 * ``tactical`` (2 continuous actions, 38 observations): a normalised field
   waypoint offset followed through the route planner.
 
-Opponents (``opponent=``): ``offense`` (full scripted game strategy with route
-planning; ``adstar`` and ``guard`` alias it), ``mirror``, ``cutoff``,
-``velocity_intercept``, ``random``. ``static_opponent_fraction`` parks the
-attacker in a random share of worlds. Control and observation latency rings
-(``max_control_latency_steps`` / ``max_observation_latency_steps``) delay the
-learner's actions and observations by a per-episode number of ticks.
+Defense-task attackers (``opponent=``): ``offense`` (full scripted game
+strategy with route planning; ``adstar``, ``guard`` and ``pursuit`` alias it),
+``mirror``, ``cutoff``, ``velocity_intercept``, ``random``.
+``static_opponent_fraction`` parks the opponent in a random share of worlds.
+Control and observation latency rings (``max_control_latency_steps`` /
+``max_observation_latency_steps``) delay the learner's actions and
+observations by a per-episode number of ticks. With ``randomize``, the
+first 18 observation features get Gaussian noise (``observation_noise``,
+default 0.01) and then dropout (``observation_dropout``, default 0.02), as
+in frc_defense/tensor_defense_observation.py:507-515. In the direct and
+tactical modes an episode terminates when the attacker comes within
+``goal_radius`` (0.5 m; randomised to 0.3-0.8 m per episode with
+``randomize``) of its objective, with a 10-point penalty (defense) or bonus
+(counter-defense). ``adstar_spawn_hint`` (default on) places the defender on
+the attacker's line to its HUB at reset; off, both robots spawn uniformly.
 """
 from __future__ import annotations
 
@@ -34,22 +60,42 @@ from .robots import RobotView
 from .world import SwerveParameters, WorldState, build_params, fuel_config
 
 OPPONENT_KINDS = {"offense": 0, "adstar": 0, "guard": 0, "pursuit": 0, "mirror": 1, "cutoff": 2,
-                  "velocity_intercept": 3, "intercept": 3, "random": 4}
+                  "velocity_intercept": 3, "random": 4}
+DEFENSE_MODES = {"INTERCEPT": 5, "LANE_BLOCK": 6, "FUEL_DENIAL": 7, "SHADOW": 8, "HUB_GUARD": 9}
+# counter-defense opponent names -> scripted defender (frc_defense/tensor_defense_step.py:110-119)
+COUNTER_DEFENSE_ALIASES = {"cutoff": "intercept", "mirror": "shadow", "velocity_intercept": "intercept",
+                           "pursuit": "shadow", "guard": "adstar_defender"}
+COUNTER_DEFENSE_KINDS = ("adstar_defender", "intercept", "lane_block", "fuel_denial", "shadow", "hub_guard",
+                         "random")
 ACTION_MODES = {"direct": (3, 35), "tactical": (2, 38), "strategic": (8, 137)}
 
 
 class TensorDefenseEnv:
-    def __init__(self, num_envs=1, task="defense", device="cuda", seed=0, opponent="offense", **kwargs):
+    def __init__(self, num_envs=1, task="counter_defense", device="cuda", seed=0, opponent="guard", **kwargs):
         if task not in ("defense", "counter_defense"):
             raise ValueError("task must be counter_defense or defense")
-        if task != "defense":
-            raise ValueError("this simulator trains the defense task; counter_defense is not provided")
-        kind = opponent.get("value", opponent.get("mode", "offense")) if isinstance(opponent, dict) else opponent
-        kind = str(kind or "offense").lower()
+        kind = opponent.get("value", opponent.get("mode", "guard")) if isinstance(opponent, dict) else opponent
+        kind = str(kind or "guard").lower()
         if kind == "learned":
             raise ValueError("learned opponents are no longer supported; use a deterministic opponent")
-        if kind not in OPPONENT_KINDS:
-            raise ValueError(f"unknown opponent {kind!r}")
+        default_mode = (opponent.get("mode", "INTERCEPT") if isinstance(opponent, dict) else "INTERCEPT")
+        selected = kwargs.pop("defense_mode", default_mode if task == "counter_defense" else None)
+        self.defense_mode = None if selected is None else str(selected).upper()
+        if self.defense_mode is not None and self.defense_mode not in DEFENSE_MODES:
+            raise ValueError("defense_mode must be INTERCEPT, LANE_BLOCK, FUEL_DENIAL, SHADOW, or HUB_GUARD")
+        if task == "counter_defense":
+            kind = COUNTER_DEFENSE_ALIASES.get(kind, kind)
+            if kind not in COUNTER_DEFENSE_KINDS:
+                raise ValueError(f"opponent {kind!r} is not a scripted defender of the counter-defense task")
+            if kind == "random":
+                opponent_code = OPPONENT_KINDS["random"]
+            else:
+                opponent_code = DEFENSE_MODES[self.defense_mode if kind == "adstar_defender" else kind.upper()]
+        else:
+            if kind not in OPPONENT_KINDS:
+                raise ValueError(f"unknown opponent {kind!r} for the defense task")
+            opponent_code = OPPONENT_KINDS[kind]
+        self.opponent_code = opponent_code
         config_path = os.environ.get("FRC_DRIVETRAIN_CONFIG")
         drivetrain = None
         if config_path:
@@ -77,7 +123,15 @@ class TensorDefenseEnv:
         self.fuel_count = int(kwargs.pop("fuel_count", 504))
         preload = kwargs.pop("preloaded_per_robot", None)
         self.preloaded_per_robot = int(preload or 0)
-        if not 96 + 6 * self.preloaded_per_robot <= self.fuel_count <= 600:
+        # "staged": depot arrays + neutral-zone array (the match layout);
+        # "uniform": every piece at a uniformly random floor position each reset
+        self.fuel_layout = str(kwargs.pop("fuel_layout", "staged"))
+        if self.fuel_layout not in ("staged", "uniform"):
+            raise ValueError("fuel_layout must be 'staged' or 'uniform'")
+        if self.fuel_layout == "uniform":
+            if not 1 <= self.fuel_count <= 600:
+                raise ValueError("fuel_count must be 1 through 600")
+        elif not 96 + 6 * self.preloaded_per_robot <= self.fuel_count <= 600:
             raise ValueError("fuel_count must be 96 + 6*preloaded_per_robot through 600")
         self.dt = float(kwargs.pop("dt", .02))
         self.horizon = int(kwargs.pop("horizon", 8000))
@@ -107,10 +161,18 @@ class TensorDefenseEnv:
                     lateral_friction=float(kwargs.pop("lateral_friction", 1.2)),
                     yaw_inertia_multiplier=float(kwargs.pop("yaw_inertia_multiplier", 1.5)))
         layout = kwargs.pop("field_layout", "2026_rebuilt")
-        for ignored in ("reuse_strategic_own_candidates", "squared_fuel_candidate_distance",
-                        "skip_strategic_offense_metric_objective", "observation_noise",
-                        "observation_dropout", "adstar_spawn_hint", "goal_radius", "defense_mode"):
-            kwargs.pop(ignored, None)
+        self.observation_noise = float(kwargs.pop("observation_noise", .01))
+        self.observation_dropout = float(kwargs.pop("observation_dropout", .02))
+        if not (self.observation_noise >= 0 and 0 <= self.observation_dropout < 1):
+            raise ValueError("observation_noise must be >= 0 and observation_dropout in [0, 1)")
+        self.adstar_spawn_hint = bool(kwargs.pop("adstar_spawn_hint", True))
+        self.base_goal_radius = float(kwargs.pop("goal_radius", .5))
+        # reference options that only select among equivalent implementations
+        # of the same computation (candidate reuse, squared distances, skipping
+        # a metric-only objective) change nothing here
+        for equivalent in ("reuse_strategic_own_candidates", "squared_fuel_candidate_distance",
+                           "skip_strategic_offense_metric_objective"):
+            kwargs.pop(equivalent, None)
         if kwargs:
             raise TypeError(f"unexpected TensorDefenseEnv options: {sorted(kwargs)}")
         self.field_boxes = fieldmod.qualification_field(layout, field_length, field_width)
@@ -126,10 +188,11 @@ class TensorDefenseEnv:
             n=self.n, robots=2, pieces=self.fuel_count, dt=self.dt, field_length=field_length,
             field_width=field_width, boxes=[b.as_tensor() for b in solids],
             bumps=[b.as_tensor() for b in bumps], hubs=hubs, team=(0, 1), mode=(learner_mode, 2),
-            role=(1, 0), kind=(0, 0), capacity=(self.fuel_capacity, self.fuel_capacity),
+            role=(0, 1) if task == "counter_defense" else (1, 0), kind=(0, 0),
+            counter_defense=1 if task == "counter_defense" else 0, capacity=(self.fuel_capacity, self.fuel_capacity),
             score_interval=(self.score_interval, self.score_interval), fuel=self.fuel_config,
             swerve=swerve, base_speed=base["speed"], base_omega=base["omega"], seed=int(seed or 0),
-            two_robot_schedule=1, opponent_kind=OPPONENT_KINDS[kind], perception_range=self.perception_range,
+            two_robot_schedule=1, opponent_kind=opponent_code, perception_range=self.perception_range,
             perception_fov=math.radians(fov) * .5, track_timeout=self.perception_track_timeout,
             replan_interval=replan, normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=.3, plan_nx=math.ceil(field_length / .3), plan_ny=math.ceil(field_width / .3),
@@ -151,6 +214,9 @@ class TensorDefenseEnv:
             "max_acceleration": base["accel"], "max_omega": base["omega"], "max_alpha": base["alpha"],
             "swerve": asdict(swerve)}
         self.generator = torch.Generator(device="cpu").manual_seed(int(seed or 0))
+        self.obs_generator = torch.Generator(device=self.device).manual_seed(int(seed or 0) + 0x0B5)
+        self.attacker = 0 if task == "counter_defense" else 1
+        self.goal_radius = torch.full((self.n,), self.base_goal_radius, device=self.device)
         self._episode = 0
         L = self.max_control_latency_steps + 1
         self.action_history = torch.zeros((self.n, L, 3), device=self.device)
@@ -195,14 +261,19 @@ class TensorDefenseEnv:
         pose[..., 0] = margin + self._rand((self.n, 2)) * (L - 2 * margin)
         pose[..., 1] = margin + self._rand((self.n, 2)) * (W - 2 * margin)
         pose[..., 2] = (2 * self._rand((self.n, 2)) - 1) * math.pi
-        # place the defender on the attacker's line to its HUB, 1.25-2.75 m ahead
-        hub = self.hub_centers[1]
-        d = hub[None] - pose[:, 1, :2]
-        dn = d.norm(dim=-1, keepdim=True).clamp_min(1e-6)
-        along = 1.25 + 1.5 * self._rand((self.n, 1))
-        place = pose[:, 1, :2] + d / dn * along.minimum(dn * .8) + (self._rand((self.n, 2)) - .5) * .18
-        pose[:, 0, 0] = place[:, 0].clamp(margin, L - margin)
-        pose[:, 0, 1] = place[:, 1].clamp(margin, W - margin)
+        atk, dfd = self.attacker, 1 - self.attacker
+        if self.adstar_spawn_hint:
+            # place the defender on the attacker's line to its HUB, 1.25-2.75 m ahead
+            hub = self.hub_centers[atk]
+            d = hub[None] - pose[:, atk, :2]
+            dn = d.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+            along = 1.25 + 1.5 * self._rand((self.n, 1))
+            place = pose[:, atk, :2] + d / dn * along.minimum(dn * .8) + (self._rand((self.n, 2)) - .5) * .18
+            pose[:, dfd, 0] = place[:, 0].clamp(margin, L - margin)
+            pose[:, dfd, 1] = place[:, 1].clamp(margin, W - margin)
+        radius = (.3 + self._rand(self.n) * .5) if self.randomize else torch.full(
+            (self.n,), self.base_goal_radius, device=self.device)
+        self.goal_radius = torch.where(m, radius, self.goal_radius)
         ws["r_pose"].copy_(torch.where(m[:, None, None], pose, ws["r_pose"]))
         if self.randomize:
             vel = torch.zeros((self.n, 2, 3), device=self.device)
@@ -211,25 +282,31 @@ class TensorDefenseEnv:
             ws["r_vel"].copy_(torch.where(m[:, None, None], vel, ws["r_vel"]))
         ws["est_pose"].copy_(torch.where(m[:, None, None], ws["r_pose"], ws["est_pose"]))
         ws["policy_pose"].copy_(torch.where(m[:, None, None], ws["r_pose"], ws["policy_pose"]))
-        # FUEL: depots, neutral array; uniform field scatter for the remainder
+        # FUEL: depots + neutral array, or a uniform scatter over the floor
         P = self.fuel_count
-        xy = torch.zeros((P, 2))
-        active = torch.zeros(P, dtype=torch.uint8)
-        depots = {b.name: b for b in self.field_boxes if b.kind == "depot"}
-        for begin, name in ((0, "red_depot"), (24, "blue_depot")):
-            dd = depots[name]
-            pts = fieldmod.grid_array_points(24, dd.x - dd.length / 2, dd.x + dd.length / 2,
-                                             dd.y - dd.width / 2, dd.y + dd.width / 2)
-            xy[begin:begin + 24] = torch.tensor(pts)
-        active[:48] = 1
-        neutral = P - 96
-        pts = fieldmod.grid_array_points(neutral, 8.27 - .915, 8.27 + .915, 4.035 - 2.615, 4.035 + 2.615)
-        xy[96:] = torch.tensor(pts)
-        active[96:] = 1
+        r = self.fuel_config.radius if self.fuel_config else .075
+        if self.fuel_layout == "uniform":
+            active = torch.ones(P, dtype=torch.uint8)
+            u = self._rand((self.n, P, 2))
+            xyd = torch.stack((r + u[..., 0] * (L - 2 * r), r + u[..., 1] * (W - 2 * r)), -1)
+        else:
+            xy = torch.zeros((P, 2))
+            active = torch.zeros(P, dtype=torch.uint8)
+            depots = {b.name: b for b in self.field_boxes if b.kind == "depot"}
+            for begin, name in ((0, "red_depot"), (24, "blue_depot")):
+                dd = depots[name]
+                pts = fieldmod.grid_array_points(24, dd.x - dd.length / 2, dd.x + dd.length / 2,
+                                                 dd.y - dd.width / 2, dd.y + dd.width / 2)
+                xy[begin:begin + 24] = torch.tensor(pts)
+            active[:48] = 1
+            neutral = P - 96
+            pts = fieldmod.grid_array_points(neutral, 8.27 - .915, 8.27 + .915, 4.035 - 2.615, 4.035 + 2.615)
+            xy[96:] = torch.tensor(pts)
+            active[96:] = 1
+            xyd = xy.to(self.device)[None].expand(self.n, -1, -1)
         fpos = torch.zeros((self.n, 3, P), device=self.device)
-        xyd = xy.to(self.device)[None].expand(self.n, -1, -1)
         fpos[:, 0], fpos[:, 1] = xyd[..., 0], xyd[..., 1]
-        fpos[:, 2] = self.fuel_config.radius if self.fuel_config else .075
+        fpos[:, 2] = r
         ws["f_pos"].copy_(torch.where(m[:, None, None], fpos, ws["f_pos"]))
         for name in ("f_vel", "f_ang"):
             ws[name].masked_fill_(m[:, None, None], 0.)
@@ -276,13 +353,40 @@ class TensorDefenseEnv:
         shifted = torch.cat((raw[:, None], self.observation_history[:, :-1]), 1)
         active = self.ws["active"].bool()
         self.observation_history.copy_(torch.where(active[:, None, None], shifted, self.observation_history))
-        return self.observation_history.gather(
+        obs = self.observation_history.gather(
             1, self.observation_delay[:, None, None].expand(-1, 1, self.obs_dim)).squeeze(1)
+        if self.randomize and self.observation_noise > 0:
+            obs[:, :18].add_(torch.randn((self.n, 18), device=self.device, generator=self.obs_generator)
+                             * self.observation_noise)
+        if self.randomize and self.observation_dropout > 0:
+            keep = torch.rand((self.n, 18), device=self.device, generator=self.obs_generator) >= self.observation_dropout
+            obs[:, :18].mul_(keep)
+        return obs
+
+    def _attacker_goal(self) -> torch.Tensor:
+        """The attacker's objective (frc_defense/tensor_sim.py:354-370): its HUB
+        approach ring when carrying FUEL to an active HUB, else its nearest
+        perceived FUEL track, else the approach ring."""
+        ws, a = self.ws, self.attacker
+        pos = ws["r_pose"][:, a, :2]
+        hub = self.hub_centers[a][None]
+        d = pos - hub
+        d = d / d.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+        size = ws["r_param"][:, a, :2]
+        approach = hub + d * (.595 + .5 * size.square().sum(-1).sqrt() + .02)[:, None]
+        tracks = ws["t_pos"][:, a].transpose(1, 2)
+        dist = (tracks - pos[:, None]).norm(dim=-1).masked_fill(~ws["t_mask"][:, a].bool(), float("inf"))
+        nearest, idx = dist.min(-1)
+        piece = tracks[torch.arange(self.n, device=self.device), idx]
+        carrying = ((ws["f_owner"] == a) & ws["f_active"].bool()).any(-1)
+        score = carrying & ws["g_hub"][:, a].bool()
+        return torch.where(score[:, None], approach, torch.where(torch.isfinite(nearest)[:, None], piece, approach))
 
     def reset(self, seed=None, options=None):
         if seed is not None:
             self.generator.manual_seed(int(seed))
             self.sim.generator.manual_seed(int(seed))
+            self.obs_generator.manual_seed(int(seed) + 0x0B5)
         self._graphs.clear()
         allm = torch.ones(self.n, dtype=torch.bool, device=self.device)
         self.ws["active"].fill_(1)
@@ -291,7 +395,8 @@ class TensorDefenseEnv:
         obs = self._observe_learner()
         self.observation_history.copy_(obs[:, None].expand_as(self.observation_history))
         self._last_observation = obs
-        return obs, {"field_layout": "2026_rebuilt", "goal_radius": torch.full((self.n,), .595, device=self.device)}
+        radius = torch.full((self.n,), .595, device=self.device) if self.action_mode == "strategic" else self.goal_radius
+        return obs, {"field_layout": "2026_rebuilt", "goal_radius": radius}
 
     def reset_done(self, mask):
         if self.device.type != "cpu" and (not isinstance(mask, torch.Tensor) or mask.device != self.device):
@@ -355,6 +460,12 @@ class TensorDefenseEnv:
         reward = self.ws["g_reward"][:, 0] * active
         truncated = active & (self.steps >= self.horizon)
         terminated = torch.zeros_like(active)
+        if self.action_mode != "strategic":
+            # direct / tactical episodes end when the attacker reaches its objective
+            goal = self._attacker_goal()
+            reached = (goal - self.ws["r_pose"][:, self.attacker, :2]).norm(dim=-1) < self.goal_radius
+            terminated = active & reached
+            reward = reward + terminated * (10. if self.task == "counter_defense" else -10.)
         if _capture_observation:
             obs = self._observe_learner()
             self._last_observation = torch.where(active[:, None], obs, self._last_observation)

@@ -70,8 +70,10 @@ class FuelPhysicsConfig:
     CUDA devices), ``"host"`` (the same routines on CPU threads) or ``"auto"``.
     Options that only tune the reference's pair-list caching (``cache``,
     ``skin``, ``max_neighbors``, ``contact_mode``, ``compact_capacity``,
-    ``robot_broadphase``) are accepted for compatibility: the kernel rebuilds an
-    exact uniform grid every substep, so they do not change results.
+    ``broadphase``, ``robot_broadphase``) are accepted for compatibility: the
+    kernel rebuilds an exact uniform grid every substep, so they do not change
+    results. ``sleep_islands`` sleeps and wakes whole contact islands.
+    ``solver="colored"`` is rejected (the kernel's solver is Jacobi).
     """
     radius: float = .075
     mass: float = .215
@@ -132,6 +134,9 @@ class FuelPhysicsConfig:
             raise ValueError("contact and sleep coefficients must be nonnegative")
         if self.grid_cell < 2 * self.radius:
             raise ValueError("grid_cell must be at least the sphere diameter")
+        if self.solver == "colored":
+            raise ValueError("solver='colored' (sequential colour passes) is not available: the FUEL kernel "
+                             "solves contacts with owner-computes Jacobi; use solver='jacobi'")
 
     @property
     def effective_substeps(self) -> int:
@@ -183,9 +188,10 @@ def build_params(*, n: int, robots: int, pieces: int, dt: float, field_length: f
         free_speed_rpm=swerve.free_speed_rpm, free_current=swerve.free_current_a,
         nominal_voltage=swerve.nominal_voltage, module_x=swerve.module_x_offset,
         module_y=swerve.module_y_offset,
-        fuel_physics=1 if fuel_on else 0, fr=fc.radius, fm=fc.mass, fk=fc.stiffness,
+        fuel_physics=1 if fuel_on else 0, fr=fc.radius, fm=fc.mass, fk=fc.stiffness, fg=fc.gravity,
         fc=fc.damping, fmu=fc.friction, froll=fc.rolling_friction, robot_height=fc.robot_height,
         max_comp=fc.max_compression_fraction, sleep=1 if fc.sleep else 0,
+        sleep_islands=1 if (fc.sleep and fc.sleep_islands) else 0,
         sleep_time=fc.sleep_time, sleep_speed=fc.sleep_speed, sleep_ang=fc.sleep_angular_speed,
         grid_cell=cell, grid_nx=math.ceil(field_length / cell), grid_ny=math.ceil(field_width / cell),
         colored_solver=1 if fc.solver == "colored" else 0,

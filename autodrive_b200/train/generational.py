@@ -21,7 +21,7 @@ from typing import Any
 import torch
 
 from ..parallel import dist as pdist
-from .evaluation import SCRIPTED_BASELINES, evaluate_once
+from .evaluation import SCRIPTED_BASELINES, evaluate_3v3_once, evaluate_once
 from .ppo import atomic_json, train_once
 
 
@@ -140,11 +140,18 @@ def generational_train(task: str, generations: int, output, *, seed: int = 7, nu
                 continue
             scenario_seed = 500_000 + generation * 1009
             eval_dir = out / "generation-evaluations" / f"generation-{number:04d}"
-            specs = [{"name": m, "mode": m} for m in SCRIPTED_BASELINES]
+            if env_kind == "3v3":   # the 3v3 defenders always face the deterministic offense
+                specs = [{"name": "deterministic_offense", "mode": "deterministic_offense"}]
+            else:
+                specs = [{"name": m, "mode": m} for m in SCRIPTED_BASELINES]
 
             def run(index, s, _stream):
                 path = eval_dir / f"{s['name']}.json"
                 try:
+                    if env_kind == "3v3":
+                        return evaluate_3v3_once(checkpoint, evaluation_episodes, scenario_seed,
+                                                 evaluation_episodes, state.device, path, horizon,
+                                                 strategic_rate_hz, fuel_physics=fuel_physics), None
                     return evaluate_once(checkpoint, task, evaluation_episodes, scenario_seed,
                                          evaluation_episodes, state.device, s["mode"], path, horizon,
                                          strategic_rate_hz, fuel_physics=fuel_physics), None

@@ -13,6 +13,7 @@ import torch
 from torch import nn
 
 from ..ops import require_extension
+from ..utils import launches
 
 
 class FlatParameters:
@@ -88,6 +89,7 @@ class FusedAdam:
     def step(self) -> torch.Tensor:
         self.flat.sync_grads()
         self.step_count += 1
+        launches.add(2)   # partial sums of squares + clip / Adam
         self.ext.adam_fused(self.flat.flat, self.flat.grad, self.m, self.v, self.partial, self.last_norm,
                             self.step_count, self.lr, self.betas[0], self.betas[1], self.eps,
                             self.weight_decay, self.max_grad_norm)

@@ -29,7 +29,7 @@ from ..utils import trace
 from ..parallel import dist as pdist
 from ..parallel.grad_sync import GradientSync, sync_parameters
 from .optim import FusedAdam
-from .rollout import DefenseAgents, StrategicClock, ThreeVsThreeAgents, gae_advantages
+from .rollout import DefenseAgents, StrategicClock, ThreeVsThreeAgents, gae_advantages, stack_inputs
 
 OBS_NORMALIZATION = "fixed_physical_scale_v1"
 DEFENSE_TRAINING_OPPONENTS = ("offense", "adstar", "mirror", "cutoff", "velocity_intercept")
@@ -80,21 +80,22 @@ def atomic_save(path: Path, value: dict) -> None:
 
 def make_env(kind: str, num_envs: int, device, seed: int, opponent: str, horizon: int,
              architecture: str = "strategic_adstar", fuel_physics=True, static_opponent_fraction: float = 0.,
-             **env_kwargs):
+             observe_every_tick: bool = False, **env_kwargs):
     """Environment factory (frc_defense/tensor_training_runtime.py:156-178). Extra keywords go to
-    the 3v3 environment (FUEL count, perception interval, planner resolution, ...)."""
+    the 3v3 environment (FUEL count, perception interval, planner resolution, ...);
+    `observe_every_tick` makes the 3v3 agents build observations at the physics rate."""
     if kind == "3v3":
         from ..sim.env3v3 import TensorThreeVsThreeEnv
         env = TensorThreeVsThreeEnv(num_envs=num_envs, device=device, seed=seed, horizon=horizon,
                                     control_modes=("deterministic",) * 3 + ("nn",) * 3,
                                     fuel_physics=fuel_physics, **env_kwargs)
-        return ThreeVsThreeAgents(env)
+        return ThreeVsThreeAgents(env, observe_every_tick)
     from ..sim.env_defense import TensorDefenseEnv
     mode = {"direct": "direct", "tactical_adstar": "tactical", "strategic_adstar": "strategic"}.get(
         architecture, architecture)
     env = TensorDefenseEnv(num_envs=num_envs, task="defense", device=device, seed=seed, opponent=opponent,
                            horizon=horizon, action_mode=mode, fuel_physics=fuel_physics,
-                           static_opponent_fraction=static_opponent_fraction)
+                           static_opponent_fraction=static_opponent_fraction, **env_kwargs)
     return DefenseAgents(env)
 
 
@@ -106,11 +107,23 @@ class PPOLearner:
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = build_policy(network, obs_dim, action_dim, action_kind).to(self.device)
+        from ..models.zoo import PerceptionActorCritic
+        # architecture-zoo networks read perception dictionaries and train in
+        # bf16 autocast on CUDA (fp32 master weights, fp32 accumulation)
+        self.perception = isinstance(self.model, PerceptionActorCritic)
+        if self.perception and self.device.type == "cuda":
+            cfg.bf16 = True
         if initial_state is not None:
             self.model.load_state_dict(initial_state)
-        sync_parameters(self.model, world)
         self.opt = FusedAdam(self.model, lr=cfg.learning_rate, eps=1e-5, max_grad_norm=cfg.max_grad_norm)
         self.sync = GradientSync(self.opt, world, cfg.grad_backend)
+        # every replica starts from rank 0's weights: one peer-memory broadcast
+        # kernel on the fused path, per-parameter collectives otherwise
+        if world > 1 and getattr(self.sync, "fused", None) is not None:
+            self.sync.fused.broadcast_parameters(0)
+            self.sync.fused.check()
+        else:
+            sync_parameters(self.model, world)
         self.world = world
         self.action_kind = action_kind
         self.action_dim = action_dim
@@ -129,11 +142,17 @@ class PPOLearner:
         self.tc.ensure_packed(self.weights_version)
         return self.tc
 
+    def _mask(self, obs):
+        if self.action_kind != "categorical":
+            return None
+        scalars = obs["scalars"] if isinstance(obs, dict) else obs
+        return scalars[:, -self.action_dim:] > .5
+
     @torch.no_grad()
-    def act(self, obs: torch.Tensor):
+    def act(self, obs):
         if self.tc is not None:
             return self._tc_ready().act(obs)
-        mask = obs[:, -self.action_dim:] > .5 if self.action_kind == "categorical" else None
+        mask = self._mask(obs)
         with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.cfg.bf16 and self.device.type == "cuda"):
             action, logp, value = self.model.sample(obs, action_mask=mask)
         return action, logp.float(), value.float(), mask
@@ -156,13 +175,15 @@ class PPOLearner:
         clip_frac = torch.zeros((), device=self.device)
         ent = torch.zeros((), device=self.device)
         samples, batches = 0, 0
+        obs_all = flat["obs"]
         for _ in range(cfg.epochs):
             perm = torch.randperm(n, device=self.device)
             for idx in perm.split(mb):
                 mask = flat["mask"][idx] if flat["mask"] is not None else None
+                obs = ({k: v[idx] for k, v in obs_all.items()} if isinstance(obs_all, dict) else obs_all[idx])
                 with torch.autocast(self.device.type, dtype=torch.bfloat16,
                                     enabled=cfg.bf16 and self.device.type == "cuda"):
-                    logp, entropy, value, _ = self.model.score(flat["obs"][idx], flat["actions"][idx], mask)
+                    logp, entropy, value, _ = self.model.score(obs, flat["actions"][idx], mask)
                 logp, entropy, value = logp.float(), entropy.float(), value.float()
                 logratio = logp - flat["logp"][idx]
                 ratio = logratio.exp()
@@ -187,6 +208,9 @@ class PPOLearner:
                 ent += entropy.mean().detach()
                 samples += int(idx.numel())
                 batches += 1
+        if self.perception and self.device.type == "cuda":
+            from ..ops.tc_linear import check_gemm_status
+            check_gemm_status(self.device, block=False)
         return {"approx_kl_sum": kl, "clip_fraction_sum": clip_frac, "entropy_sum": ent,
                 "samples": samples, "batches": batches}
 
@@ -234,8 +258,9 @@ def collect_rollout(agents, learner: PPOLearner, obs: torch.Tensor, steps: int, 
     dev = learner.device
     A, D = agents.n_agents, agents.obs_dim
     cont = learner.action_kind == "continuous"
+    dict_obs = isinstance(obs, dict)
     buf = {
-        "obs": torch.empty((steps, A, D), device=dev),
+        "obs": [] if dict_obs else torch.empty((steps, A, D), device=dev),
         "actions": torch.empty((steps, A, learner.action_dim) if cont else (steps, A), device=dev,
                                dtype=torch.float32 if cont else torch.long),
         "mask": None if cont else torch.empty((steps, A, learner.action_dim), device=dev, dtype=torch.bool),
@@ -249,7 +274,10 @@ def collect_rollout(agents, learner: PPOLearner, obs: torch.Tensor, steps: int, 
     ticks_total = 0
     horizon = agents.horizon
     for t in range(steps):
-        buf["obs"][t] = obs
+        if dict_obs:
+            buf["obs"].append(obs)
+        else:
+            buf["obs"][t] = obs
         action, logp, value, mask = learner.act(obs)
         if mask is not None:
             buf["mask"][t] = mask
@@ -273,7 +301,19 @@ def collect_rollout(agents, learner: PPOLearner, obs: torch.Tensor, steps: int, 
             episode_ticks[0] = 0
             next_obs = agents.reset_done(torch.ones(A, dtype=torch.bool, device=dev))
         obs = next_obs
+    if dict_obs:
+        buf["obs"] = stack_inputs(buf["obs"])
     return buf, obs, ticks_total
+
+
+def flatten_rollout(buf: dict, adv: torch.Tensor, obs_dim: int, action_dim: int, action_kind: str) -> dict:
+    """Rollout buffers [T, A, ...] -> one flat PPO batch [T*A, ...]."""
+    obs = buf["obs"] if isinstance(buf["obs"], dict) else buf["obs"].reshape(-1, obs_dim)
+    return {"obs": obs,
+            "actions": buf["actions"].reshape((-1, action_dim) if action_kind == "continuous" else (-1,)),
+            "mask": buf["mask"].reshape(-1, action_dim) if buf["mask"] is not None else None,
+            "logp": buf["logp"].reshape(-1), "adv": adv.reshape(-1),
+            "returns": (adv + buf["values"]).reshape(-1)}
 
 
 def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, device, opponent: str,
@@ -283,7 +323,8 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
                l2_coef: float = 1e-5, horizon: int = 8000, architecture: str = "strategic_adstar",
                curriculum: bool = True, strategic_rate_hz: float = 4., env_kind: str = "defense",
                network: str = "mlp", fuel_physics=True, grad_backend: str = "auto", bf16: bool = False,
-               status_context: dict | None = None, dist_state=None) -> dict[str, Any]:
+               status_context: dict | None = None, dist_state=None,
+               env_kwargs: dict | None = None) -> dict[str, Any]:
     if task != "defense":
         raise ValueError("only defense policies are trainable; offense is deterministic")
     if opponent not in (*DEFENSE_TRAINING_OPPONENTS, "mixed"):
@@ -298,10 +339,13 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
                     l2_coef=l2_coef, strategic_rate_hz=strategic_rate_hz, grad_backend=grad_backend, bf16=bf16)
     agents = make_env(env_kind, num_envs, dev, rank_seed, "offense" if opponent == "mixed" else opponent,
                       horizon, architecture, fuel_physics,
-                      STATIC_OPPONENT_FRACTION if env_kind == "defense" else 0.)
+                      STATIC_OPPONENT_FRACTION if env_kind == "defense" else 0., **(env_kwargs or {}))
     action_kind = agents.action_kind
     initial_state = None
-    if initial_checkpoint is not None:
+    # with the peer-memory broadcast, rank 0 alone reads the checkpoint and the
+    # learner's initial sync moves its weights to the other ranks
+    peer_broadcast = world > 1 and dev.type == "cuda" and grad_backend in ("auto", "p2p")
+    if initial_checkpoint is not None and (rank == 0 or not peer_broadcast):
         from ..utils.checkpoint import load_verified
         payload = load_verified(initial_checkpoint, map_location=dev)
         if payload.get("task") != "defense":
@@ -310,8 +354,14 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
             raise ValueError("initial checkpoint drivetrain configuration does not match this run")
         if payload.get("architecture", "direct") != architecture:
             raise ValueError("initial checkpoint architecture differs from this training run")
+        if payload.get("network", "mlp") != network:
+            raise ValueError("initial checkpoint network differs from this training run")
         initial_state = payload["model_state_dict"]
     learner = PPOLearner(agents.obs_dim, agents.action_dim, action_kind, dev, cfg, network, world, initial_state)
+    if learner.perception:
+        if not hasattr(agents, "use_perception"):
+            raise ValueError(f"network {network!r} reads perception inputs of the 3v3 environment; use env_kind='3v3'")
+        agents.use_perception(learner.model.field_shape, learner.model.input_keys)
     out = Path(output)
     if rank == 0:
         out.mkdir(parents=True, exist_ok=True)
@@ -346,11 +396,7 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
         with trace.stage("gae"):
             adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
                                  buf["next_values"], gamma, gae_lambda, stats)
-        flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim),
-                "actions": buf["actions"].reshape((-1, agents.action_dim) if action_kind == "continuous" else (-1,)),
-                "mask": buf["mask"].reshape(-1, agents.action_dim) if buf["mask"] is not None else None,
-                "logp": buf["logp"].reshape(-1), "adv": adv.reshape(-1),
-                "returns": (adv + buf["values"]).reshape(-1)}
+        flat = flatten_rollout(buf, adv, agents.obs_dim, agents.action_dim, action_kind)
         if action_kind == "categorical":
             action_counts += torch.bincount(flat["actions"], minlength=agents.action_dim).float()
         coef = entropy_coef * max(0., 1. - update / max(1, updates - 1))
@@ -385,7 +431,10 @@ def train_once(task: str, timesteps: int, output, *, seed: int, num_envs: int, d
                                       "action_distribution": dist_counts, "world_size": world})
         result = record
     scores, acquisitions = agents.score_counts()
+    import hashlib
+    digest = hashlib.sha256(learner.opt.flat.flat.detach().float().cpu().numpy().tobytes()).hexdigest()
     final = {**status_context, "status": "completed", "task": task, "opponent": opponent,
+             "parameters_sha256": digest,
              "architecture": architecture, "network": network, "checkpoint": str(checkpoint),
              **result, "history": history[-20:],
              "team_scores": scores.sum(0).tolist(), "acquisitions": acquisitions.sum(0).tolist(),
@@ -419,7 +468,10 @@ def checkpoint_payload(model, agents, architecture, network, action_kind, optimi
     payload = {"model_state_dict": model.state_dict(), "obs_dim": agents.obs_dim,
                "action_dim": agents.action_dim, "action_kind": action_kind, "architecture": architecture,
                "task": "defense", "observation_normalization": OBS_NORMALIZATION,
-               "drivetrain_config": agents.drivetrain_config, "network": network}
+               "drivetrain_config": agents.drivetrain_config, "network": network,
+               "env": "3v3" if isinstance(agents, ThreeVsThreeAgents) else "defense"}
+    if isinstance(agents, ThreeVsThreeAgents):
+        payload["observation_spec"] = "per-robot-3v3-v1"
     if optimizer is not None:
         payload["optimizer_state_dict"] = optimizer.state_dict()
     # provenance: SHA-256 tree digest of the weights, computed where they live

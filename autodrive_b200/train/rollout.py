@@ -10,6 +10,7 @@ from __future__ import annotations
 import torch
 
 from ..ops import require_extension
+from ..utils import launches
 
 
 def gae_advantages(rewards, dones, truncated, values, next_values, gamma: float, gae_lambda: float,
@@ -24,6 +25,7 @@ def gae_advantages(rewards, dones, truncated, values, next_values, gamma: float,
     adv = torch.empty_like(rewards)
     if stats is None:
         stats = torch.zeros(3, dtype=torch.float64, device=rewards.device)
+    launches.add(1)
     ext.gae(rewards.contiguous().float(), dones.contiguous().to(torch.uint8),
             truncated.contiguous().to(torch.uint8), values.contiguous().float(),
             next_values.contiguous().float(), adv, float(gamma), float(gae_lambda), stats)
@@ -41,6 +43,38 @@ def gae_reference(rewards, dones, truncated, values, next_values, gamma, gae_lam
         last = delta + gamma * gae_lambda * cont * last
         adv[t] = last
     return adv
+
+
+def trim_entities(inp: dict) -> dict:
+    """Drop FUEL-track tokens past the highest live track slot of the batch
+    (anonymous tracks fill slots from 0), rounded up to a multiple of 8, and
+    keep the four robot tokens: attention cost follows the tracks held."""
+    ent, mask = inp["entities"], inp["entity_mask"]
+    P = ent.shape[1] - 4
+    live = mask[:, :P].any(0)
+    k = int(live.nonzero().max()) + 1 if bool(live.any()) else 0
+    k = min(P, (k + 7) // 8 * 8)
+    if k == P:
+        return inp
+    keep = torch.cat((torch.arange(k, device=ent.device), torch.arange(P, P + 4, device=ent.device)))
+    return {**inp, "entities": ent[:, keep], "entity_mask": mask[:, keep]}
+
+
+def stack_inputs(rows: list[dict]) -> dict:
+    """Concatenate per-decision perception dictionaries along the batch,
+    zero-padding the FUEL-track tokens (invalid, masked) to the longest."""
+    if "entities" in rows[0]:
+        kmax = max(r["entities"].shape[1] for r in rows)
+        padded = []
+        for r in rows:
+            ent, mask = r["entities"], r["entity_mask"]
+            extra = kmax - ent.shape[1]
+            if extra:
+                ent = torch.cat((ent[:, :-4], ent.new_zeros((ent.shape[0], extra, ent.shape[2])), ent[:, -4:]), 1)
+                mask = torch.cat((mask[:, :-4], mask.new_zeros((mask.shape[0], extra)), mask[:, -4:]), 1)
+            padded.append({**r, "entities": ent, "entity_mask": mask})
+        rows = padded
+    return {k: torch.cat([r[k] for r in rows]) for k in rows[0]}
 
 
 class StrategicClock:
@@ -98,8 +132,9 @@ class DefenseAgents:
 class ThreeVsThreeAgents:
     """Neural-controlled slots of a TensorThreeVsThreeEnv as a flat agent batch."""
 
-    def __init__(self, env):
+    def __init__(self, env, observe_every_tick: bool = False):
         self.env = env
+        self.observe_every_tick = bool(observe_every_tick)
         self.slots = [i for i, m in enumerate(env.control_modes) if m == "nn"]
         if not self.slots:
             raise ValueError("the 3v3 environment has no neural-controlled robot slots")
@@ -109,8 +144,21 @@ class ThreeVsThreeAgents:
         self.horizon = env.horizon
         self.drivetrain_config = env.drivetrain_config
         self._full = torch.full((env.n, 6), 7, dtype=torch.int32, device=env.device)
+        self.perception = None
+        self.perception_keys = ()
 
-    def _agent_obs(self) -> torch.Tensor:
+    def use_perception(self, field_shape=(32, 64), keys=("scalars", "field", "entities", "entity_mask")):
+        """Observations become perception dictionaries (``PerceptionInputs``)
+        holding only `keys`, for the architecture-zoo networks."""
+        from ..models.perception import PerceptionInputs
+        self.perception = PerceptionInputs(self.env, self.slots, field_shape=field_shape)
+        self.perception_keys = tuple(keys)
+
+    def _agent_obs(self):
+        if self.perception is not None:
+            inp = self.perception()
+            inp = {k: inp[k] for k in self.perception_keys}
+            return trim_entities(inp) if "entities" in inp else inp
         return self.env.ws["obs"].index_select(1, self.slot_index).reshape(self.n_agents, 137)
 
     def reset(self) -> torch.Tensor:
@@ -121,7 +169,7 @@ class ThreeVsThreeAgents:
         self._full.index_copy_(1, self.slot_index,
                                action.reshape(self.env.n, len(self.slots)).to(torch.int32))
         ticks = min(ticks, max(1, remaining))
-        _, reward, truncated = self.env.step_held(self._full, ticks)
+        _, reward, truncated = self.env.step_held(self._full, ticks, observe_every_tick=self.observe_every_tick)
         reward = reward.index_select(1, self.slot_index).reshape(self.n_agents)
         truncated = truncated[:, None].expand(-1, len(self.slots)).reshape(self.n_agents)
         done = torch.zeros_like(truncated)

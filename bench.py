@@ -3,10 +3,12 @@
 Default workload (`--mode train`), one step = one PPO training iteration of
 the 3v3 defense configuration on every GPU:
   * TensorThreeVsThreeEnv, 2048 worlds per GPU, fuel physics on (400 FUEL,
-    64 robot+FUEL substeps per 20 ms tick), stereo perception and strategic
-    observations every tick, route replanning every 20 ticks on the
-    reference's 0.3 m grid (56 x 27 cells), three scripted offense robots and three learned
-    defenders sharing one 137->8 ActorCritic (random init, fp32);
+    64 robot+FUEL substeps per 20 ms tick), stereo perception and the
+    137-feature strategic observations built every tick, route replanning
+    every 20 ticks on a 0.1 m occupancy grid (166 x 81 cells), three scripted
+    offense robots and three learned defenders sharing one 137->8
+    ActorCritic (random init; fp32 master weights, bf16 tensor-core matmul
+    operands with fp32 accumulation);
   * a rollout of `--decisions` strategic decisions held 12/13 ticks each
     (4 Hz), the GAE kernel, then PPO with 4 epochs x 8 minibatches, gradient
     averaging over the ranks and the fused clip + Adam kernels.
@@ -25,7 +27,10 @@ the step's control inputs copied from pinned host memory every step and the
 step's result statistics read back to the host every step.
 
 `--impl reference` runs the unmodified reference package from baseline/_ref
-through its own public API on the same configuration.
+through its own public API on the same configuration: it first times two
+ticks of the reference's TensorThreeVsThreeEnv at a few worlds on this GPU,
+and when the full configuration projects past `--reference-budget-s` it
+prints an `unavailable` line carrying that calibration instead of a value.
 """
 from __future__ import annotations
 
@@ -38,12 +43,17 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "3v3 env-ticks/sec and PPO samples/sec, 1/2/4/8 B200, device-timed max over ranks"
 # The 3v3 full-match benchmark world: 400 FUEL, perception and strategic
-# observations every tick. Routes are planned on the 0.3 m grid (56 x 27)
-# that the reference's 3v3 environment always uses (it has no resolution
-# keyword), so both arms plan on the same grid; the finer 0.1 m grid is
-# available through `planner_resolution`. (The reference's own defaults are
-# 504 FUEL and perception every 2nd tick.)
-BENCH_ENV = {"fuel_count": 400, "perception_interval": 1, "planner_resolution": .3}
+# observations every tick, routes planned on a 0.1 m occupancy grid
+# (166 x 81 cells). The reference's 3v3 environment plans on a fixed 0.3 m
+# grid (it has no resolution keyword) and defaults to 504 FUEL with
+# perception every 2nd tick.
+BENCH_ENV = {"fuel_count": 400, "perception_interval": 1, "planner_resolution": .1}
+OBSERVE_EVERY_TICK = True
+BENCH_DESC = ("TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 400 FUEL, 64 substeps/tick, perception "
+              "and strategic observations every tick, AD*-style replanning every 20 ticks on a 0.1 m grid "
+              "166x81)")
+DTYPES = {"simulator": "fp32", "policy_matmul": "bf16 operands, fp32 accumulate (tcgen05)",
+          "master_weights_and_optimizer": "fp32"}
 
 
 def _dist_init():
@@ -93,16 +103,19 @@ def _timed(fn, steps, world):
 def run_train(args, rank, world, local):
     import torch
     sys.path.insert(0, HERE)
-    from autodrive_b200.train.ppo import PPOConfig, PPOLearner, collect_rollout, make_env
+    from autodrive_b200.train.ppo import PPOConfig, PPOLearner, collect_rollout, flatten_rollout, make_env
     from autodrive_b200.train.rollout import StrategicClock, gae_advantages
+    from autodrive_b200.utils import launches
     from autodrive_b200.utils.clocks import ClockSampler
     dev = torch.device("cuda", local)
     agents = make_env("3v3", args.envs, dev, args.seed + rank * 1_000_003, "offense", 8000, fuel_physics=True,
-                      **BENCH_ENV)
+                      observe_every_tick=OBSERVE_EVERY_TICK, **BENCH_ENV)
     samples = agents.n_agents * args.decisions
     cfg = PPOConfig(rollout_steps=args.decisions, epochs=args.epochs,
                     minibatch_size=samples // args.minibatches, grad_backend=args.grad_backend)
-    learner = PPOLearner(agents.obs_dim, agents.action_dim, "categorical", dev, cfg, "mlp", world)
+    learner = PPOLearner(agents.obs_dim, agents.action_dim, "categorical", dev, cfg, args.network, world)
+    if learner.perception:
+        agents.use_perception(learner.model.field_shape, learner.model.input_keys)
     state = {"obs": agents.reset(), "clock": StrategicClock(4.), "ep": [0], "ticks": 0}
     control_dev = torch.tensor([cfg.entropy_coef, 0.], device=dev)
     stats_dev = torch.zeros(4, device=dev)
@@ -126,9 +139,7 @@ def run_train(args, rank, world, local):
         stats = torch.zeros(3, dtype=torch.float64, device=dev)
         adv = gae_advantages(buf["rewards"], buf["dones"], buf["truncated"], buf["values"],
                              buf["next_values"], cfg.gamma, cfg.gae_lambda, stats)
-        flat = {"obs": buf["obs"].reshape(-1, agents.obs_dim), "actions": buf["actions"].reshape(-1),
-                "mask": buf["mask"].reshape(-1, agents.action_dim), "logp": buf["logp"].reshape(-1),
-                "adv": adv.reshape(-1), "returns": (adv + buf["values"]).reshape(-1)}
+        flat = flatten_rollout(buf, adv, agents.obs_dim, agents.action_dim, "categorical")
         mark()
         upd = learner.update(flat, control_dev[0])
         mark()
@@ -140,10 +151,12 @@ def run_train(args, rank, world, local):
     for _ in range(args.warmup):
         step()
     ticks_before = state["ticks"]
+    launches_before = launches.read()
     phases["on"] = True
     with ClockSampler(local) as clocks:
         ms = _timed(step, args.steps, world)
     phases["on"] = False
+    wrapper_launches = launches.read() - launches_before
     torch.cuda.synchronize()
     breakdown = {"rollout": 0., "gae": 0., "update": 0.}
     for ev in phases["events"]:
@@ -173,21 +186,26 @@ def run_train(args, rank, world, local):
     e2e_ticks = args.envs * (state["ticks"] - t0) * world
     decisions_ticks = ticks_timed / max(1, args.steps)
     minibatches = args.epochs * args.minibatches
-    # own kernels per step: control+plan+tick+sense per tick, observe + policy act per decision, the
-    # bootstrap value, GAE, and per minibatch either (adv stats, fused fwd+bwd, partial reduce,
-    # sum-of-squares, Adam, weight pack) on the tensor-core path or (sum-of-squares, Adam)
-    per_mb = 6 if learner.tc is not None else 2
-    per_decision = 2 if learner.tc is not None else 1
-    launches = int(args.steps * (decisions_ticks * 4 + per_decision * args.decisions + 2 + per_mb * minibatches))
+    # own kernels per step: control+plan+tick+sense+observe per tick (C++ launches); on the fused
+    # MLP path the policy act per decision, the bootstrap value and per minibatch adv stats, fused
+    # fwd+bwd, partial reduce and weight pack; plus the kernels the Python wrappers count (GAE,
+    # GEMMs, LayerNorm, Adam, peer all-reduce)
+    per_tick = 5 if OBSERVE_EVERY_TICK else 4
+    sim_launches = decisions_ticks * per_tick + (0 if OBSERVE_EVERY_TICK else args.decisions)
+    tc_launches = (args.decisions + 1 + 4 * minibatches) if learner.tc is not None else 0
+    gpu_launches = int(args.steps * (sim_launches + tc_launches) + wrapper_launches)
     return {
         "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32",
+        "vs_baseline": None, "dtype": "bf16" if (learner.tc is not None or learner.cfg.bf16) else "fp32",
+        "dtypes": DTYPES,
         "data": "synthetic (random-init seeded REBUILT matches and policy; no external data)",
         "ppo_samples_per_s": samples_total / (ms / 1e3), "ppo_samples_per_step_per_gpu": samples,
-        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 400 FUEL, 64 substeps/tick, "
-                            "perception every tick, 0.3 m planner grid 56x27 as in the reference, replan every 20 ticks) "
-                            "+ PPO on the strategic_adstar ActorCritic 137->128->128->8 for 3 learned defenders",
+        "config": {"model": BENCH_DESC + (" + PPO on the strategic_adstar ActorCritic 137->128->128->8 for 3 "
+                                          "learned defenders" if args.network == "mlp" else
+                                          f" + PPO on {args.network} ({sum(p.numel() for p in learner.model.parameters())}"
+                                          " parameters, bf16 autocast, fp32 master) for 3 learned defenders"),
+                   "network": args.network,
                    "global_batch": args.envs * world, "envs_per_gpu": args.envs,
                    "seq_len": args.decisions, "decisions_per_step": args.decisions,
                    "env_ticks_per_step_per_world": decisions_ticks, "ppo_epochs": args.epochs,
@@ -198,87 +216,12 @@ def run_train(args, rank, world, local):
         "e2e": {"value": e2e_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
                 "ppo_samples_per_s": samples_total / (e2e_ms / 1e3),
                 "h2d_bytes_per_step": host_control.numel() * 4, "d2h_bytes_per_step": host_stats.numel() * 4},
-        "gpu_launches": launches,
+        "gpu_launches": gpu_launches,
         "breakdown_ms_per_step": breakdown,
-        "policy_kernels": "tcgen05" if learner.tc is not None else "torch",
+        "policy_kernels": ("tcgen05 fused MLP kernels" if learner.tc is not None else
+                           "tcgen05 GEMM + fused LayerNorm kernels with torch attention/elementwise"),
         "final_stats": {"mean_reward": float(stats_dev[0]), "approx_kl": float(stats_dev[1]),
                         "entropy": float(stats_dev[2]), "grad_norm": float(stats_dev[3])},
-    }
-
-
-def run_train_zoo(args, rank, world, local):
-    """PPO step with a perception-input zoo policy (e.g. the ~4M-parameter
-    entity encoder, d = 256, 4 heads, 2 blocks) in bf16 autocast."""
-    import torch
-    sys.path.insert(0, HERE)
-    from autodrive_b200.bench.zoo_ppo import ZooPPO
-    from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
-    from autodrive_b200.utils.clocks import ClockSampler
-    dev = torch.device("cuda", local)
-    env = TensorThreeVsThreeEnv(num_envs=args.envs, device=dev, seed=args.seed + rank * 1_000_003,
-                                control_modes=("deterministic",) * 3 + ("nn",) * 3, fuel_physics=True,
-                                horizon=8000, **BENCH_ENV)
-    ppo = ZooPPO(env, args.network, world, epochs=args.epochs, minibatches=args.minibatches,
-                 grad_backend=args.grad_backend)
-    state = {"ticks": 0, "upd": None, "events": None}
-    stats_dev = torch.zeros(3, device=dev)
-
-    def step():
-        ev = None
-        if state["events"] is not None:
-            ev = []
-            state["events"].append(ev)
-        ticks, upd = ppo.step(args.decisions, ev)
-        state["ticks"] += ticks
-        stats_dev[0] = upd["mean_reward"]
-        stats_dev[1] = upd["approx_kl_sum"] / max(1, upd["batches"])
-        stats_dev[2] = upd["entropy_sum"] / max(1, upd["batches"])
-
-    for _ in range(args.warmup):
-        step()
-    t0 = state["ticks"]
-    state["events"] = []
-    with ClockSampler(local) as clocks:
-        ms = _timed(step, args.steps, world)
-    torch.cuda.synchronize()
-    breakdown = {"rollout": sum(e[0].elapsed_time(e[1]) for e in state["events"]) / args.steps,
-                 "update": sum(e[1].elapsed_time(e[2]) for e in state["events"]) / args.steps}
-    state["events"] = None
-    ticks_timed = state["ticks"] - t0
-    value = args.envs * ticks_timed * world / (ms / 1e3)
-    samples = args.envs * 3 * args.decisions
-    host_stats = torch.zeros(3).pin_memory()
-    host_seed = torch.tensor([float(args.seed)]).pin_memory()
-    seed_dev = torch.zeros(1, device=dev)
-
-    def e2e_step():
-        seed_dev.copy_(host_seed, non_blocking=True)
-        step()
-        host_stats.copy_(stats_dev, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        _ = float(host_stats[0])
-
-    t1 = state["ticks"]
-    e2e_ms = _timed(e2e_step, args.steps, world)
-    e2e_ticks = args.envs * (state["ticks"] - t1) * world
-    return {
-        "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (random-init seeded REBUILT matches and policy; no external data)",
-        "ppo_samples_per_s": samples * args.steps * world / (ms / 1e3), "ppo_samples_per_step_per_gpu": samples,
-        "config": {"model": f"TensorThreeVsThreeEnv 3v3 full match (fuel physics on, 400 FUEL, perception every "
-                            f"tick) + PPO on PerceptionActorCritic {args.network} ({ppo.params} parameters, "
-                            f"bf16 autocast, fp32 master) for 3 learned defenders",
-                   "global_batch": args.envs * world, "envs_per_gpu": args.envs, "seq_len": args.decisions,
-                   "ppo_epochs": args.epochs, "ppo_minibatches": args.minibatches,
-                   "grad_backend": ppo.sync.backend, "parallelism": f"env-batch x dp{world}",
-                   "l2": "working set > 126 MB L2 (no flush needed)"},
-        "clocks": clocks.summary(),
-        "e2e": {"value": e2e_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
-                "h2d_bytes_per_step": host_seed.numel() * 4, "d2h_bytes_per_step": host_stats.numel() * 4},
-        "gpu_launches": None,
-        "breakdown_ms_per_step": {k: round(v, 3) for k, v in breakdown.items()},
     }
 
 
@@ -292,16 +235,17 @@ def run_sim(args, rank, world, local):
                                 fuel_physics=True, horizon=8000, **BENCH_ENV)
     ticks = args.ticks_per_step
     actions = torch.full((args.envs, 6), 7, dtype=torch.int32, device=dev)
+    held = dict(observe_every_tick=OBSERVE_EVERY_TICK)
     for _ in range(args.warmup):
-        env.step_held(actions, ticks)
+        env.step_held(actions, ticks, **held)
     with ClockSampler(local) as clocks:
-        ms = _timed(lambda: env.step_held(actions, ticks), args.steps, world)
+        ms = _timed(lambda: env.step_held(actions, ticks, **held), args.steps, world)
     env_ticks = args.envs * ticks * args.steps * world
     host_actions = torch.full((args.envs, 6), 7, dtype=torch.int32).pin_memory()
     host_rewards = torch.empty((args.envs, 6), dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        _, rew, _ = env.step_held(host_actions.to(dev, non_blocking=True), ticks)
+        _, rew, _ = env.step_held(host_actions.to(dev, non_blocking=True), ticks, **held)
         host_rewards.copy_(rew, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         _ = float(host_rewards.sum())
@@ -313,19 +257,30 @@ def run_sim(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (random-init seeded REBUILT matches, deterministic scripted controllers)",
-        "config": {"model": "TensorThreeVsThreeEnv 3v3 full match, fuel physics on (400 FUEL, 64 substeps/tick), "
-                            "perception every tick, 0.3 m planner grid 56x27 as in the reference, replan every 20 ticks, "
-                            "simulator only",
+        "config": {"model": BENCH_DESC + ", simulator only",
                    "global_batch": args.envs * world, "envs_per_gpu": args.envs, "seq_len": ticks,
                    "parallelism": f"env-batch x dp{world}", "l2": "working set > 126 MB L2 (no flush needed)"},
         "clocks": clocks.summary(),
         "e2e": {"value": env_ticks / (e2e_ms / 1e3), "unit": "env-ticks/s",
                 "h2d_bytes_per_step": host_actions.numel() * 4, "d2h_bytes_per_step": host_rewards.numel() * 4},
-        "gpu_launches": (ticks * 4 + 1) * args.steps,
+        "gpu_launches": (ticks * (5 if OBSERVE_EVERY_TICK else 4) + (0 if OBSERVE_EVERY_TICK else 1)) * args.steps,
     }
 
 
 def run_reference(args, rank, world, local):
+    """The unmodified reference (baseline/_ref) through its public API.
+
+    Calibration: the reference's TensorThreeVsThreeEnv on this GPU at a few
+    worlds with the benchmark world's settings (400 FUEL, perception every
+    tick, observations every tick, fuel physics on), one warm-up tick and two
+    timed ticks. Its CUDA path builds FUEL contact pairs with per-world
+    Python loops on the host (frc_defense/fuel_physics.py:337-382), so the
+    full configuration is projected first; when it fits the budget the
+    reference's own loop runs and is timed (`--mode sim`: env.step ticks as in
+    scripts/benchmark_3v3_full_match.py:15-58; `--mode train`: one
+    train_3v3_generation call of `--decisions` rollout steps per step,
+    frc_defense/tensor_training.py:137-157).
+    """
     ref = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "frc_defense")):
         return {"impl": "reference", "unavailable": "baseline/_ref is not installed"}
@@ -333,32 +288,71 @@ def run_reference(args, rank, world, local):
     import torch
     from frc_defense.tensor_3v3 import TensorThreeVsThreeEnv as RefEnv
     dev = torch.device("cuda", local)
-    # The reference's CUDA path builds FUEL contact pairs with per-world Python
-    # loops on the host (frc_defense/fuel_physics.py:337-382). Calibrate one
-    # tick at a small batch first and refuse configurations that cannot finish.
+    torch.cuda.set_device(dev)
     calib = min(args.envs, 4)
     modes = ("deterministic",) * 3 + (("nn",) * 3 if args.mode == "train" else ("deterministic",) * 3)
-    env = RefEnv(num_envs=calib, device=dev, seed=args.seed + rank, control_modes=modes,
-                 robot_roles=("offense",) * 3 + ("defense",) * 3, horizon=8000, randomize=True,
-                 fuel_count=BENCH_ENV["fuel_count"], perception_interval=BENCH_ENV["perception_interval"],
-                 fused_sensor_rng=True, fuel_physics=True)
+    env_kw = dict(robot_roles=("offense",) * 3 + ("defense",) * 3, horizon=8000, randomize=True,
+                  fuel_count=BENCH_ENV["fuel_count"], perception_interval=BENCH_ENV["perception_interval"],
+                  fused_sensor_rng=True, fuel_physics=True)
+    env = RefEnv(num_envs=calib, device=dev, seed=args.seed + rank, control_modes=modes, **env_kw)
+    env.reset(seed=args.seed + rank)
     actions = torch.full((calib, 6), 7, dtype=torch.long, device=dev)
-    env.step(actions, capture_observation=False, capture_info=False)
+    env.step(actions, capture_observation=OBSERVE_EVERY_TICK, capture_info=False)
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    env.step(actions, capture_observation=False, capture_info=False)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(2):
+        env.step(actions, capture_observation=OBSERVE_EVERY_TICK, capture_info=False)
+    stop.record()
     torch.cuda.synchronize()
-    per_tick = time.perf_counter() - t0
+    per_tick = _max_over_ranks(start.elapsed_time(stop) / 2e3, world)
+    del env
     ticks_per_step = args.decisions * 12.5 if args.mode == "train" else args.ticks_per_step
     projected = per_tick * args.envs / calib * ticks_per_step * (args.steps + args.warmup)
+    calibration = {"envs": calib, "ticks": 2, "seconds_per_tick": per_tick,
+                   "env_ticks_per_s": calib / per_tick, "device_timed": True,
+                   "settings": "400 FUEL, perception and observations every tick, fuel physics on, reference "
+                               "planner grid 0.3 m (no resolution keyword)"}
     if projected > args.reference_budget_s:
-        return {"impl": "reference",
-                "unavailable": (f"reference 3v3 with fuel physics measured {per_tick:.2f} s per tick at {calib} "
+        return {"impl": "reference", "n_gpus": world,
+                "unavailable": (f"reference 3v3 (fuel physics on) measured {per_tick:.2f} s per tick at {calib} "
                                 f"worlds ({calib / per_tick:.2f} env-ticks/s) on this GPU; {args.envs} worlds x "
                                 f"{ticks_per_step * (args.steps + args.warmup):.0f} ticks projects to "
-                                f"{projected / 3600:.1f} h"),
-                "calibration_env_ticks_per_s": calib / per_tick, "n_gpus": world}
-    raise SystemExit("reference configuration fits the budget; extend run_reference before using it")
+                                f"{projected / 3600:.1f} h, over the {args.reference_budget_s:.0f} s budget"),
+                "calibration": calibration, "calibration_env_ticks_per_s": calib / per_tick}
+    if args.mode == "sim":
+        env = RefEnv(num_envs=args.envs, device=dev, seed=args.seed + rank, control_modes=modes, **env_kw)
+        env.reset(seed=args.seed + rank)
+        actions = torch.full((args.envs, 6), 7, dtype=torch.long, device=dev)
+
+        def step():
+            for _ in range(args.ticks_per_step):
+                env.step(actions, capture_observation=OBSERVE_EVERY_TICK, capture_info=False)
+        work = args.envs * args.ticks_per_step
+    else:
+        import tempfile
+        from frc_defense.tensor_training import train_3v3_generation
+        out_dir = tempfile.mkdtemp(prefix="ref_bench_")
+        counter = [0]
+        samples = args.envs * 3 * args.decisions
+
+        def step():
+            counter[0] += 1
+            train_3v3_generation("defense", counter[0], out_dir, seed=args.seed, num_envs=args.envs * world,
+                                 device=str(dev), rollout_steps=args.decisions, epochs=args.epochs,
+                                 minibatch_size=max(world, samples * world // args.minibatches))
+        work = args.envs * args.decisions * 12.5
+    for _ in range(args.warmup):
+        step()
+    ms = _timed(step, args.steps, world)
+    value = work * args.steps * world / (ms / 1e3)
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "env-ticks/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (reference package, random init)", "calibration": calibration,
+            "config": {"model": "reference TensorThreeVsThreeEnv (400 FUEL, perception every tick, fuel physics on)",
+                       "global_batch": args.envs * world, "envs_per_gpu": args.envs, "mode": args.mode,
+                       "parallelism": f"env-batch x dp{world}"}}
 
 
 def main():
@@ -388,8 +382,7 @@ def main():
     if args.impl == "reference":
         result = run_reference(args, rank, world, local)
     else:
-        train = run_train if args.network == "mlp" else run_train_zoo
-        result = (train if args.mode == "train" else run_sim)(args, rank, world, local)
+        result = (run_train if args.mode == "train" else run_sim)(args, rank, world, local)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:

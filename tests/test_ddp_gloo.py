@@ -1,5 +1,6 @@
 """Data-parallel PPO semantics on two gloo CPU ranks (world_size=2)."""
 import json
+import math
 import os
 import socket
 import subprocess
@@ -22,15 +23,18 @@ sys.path.insert(0, {root!r})
 from autodrive_b200.parallel import dist as pdist
 from autodrive_b200.train.ppo import train_once
 state = pdist.distributed_state("cpu", timeout_s=120)
-r = train_once("defense", 4 * 8 * 2, {out!r}, seed=0, num_envs=4, device="cpu", opponent="offense",
-               rollout_steps=8, epochs=1, minibatch_size=16, horizon=300, fuel_physics=False,
-               curriculum=False, dist_state=state)
-flat = torch.cat([p.detach().reshape(-1) for p in torch.load(os.path.join({out!r}, "policy.pt"),
-                 weights_only=True)["model_state_dict"].values()]) if state.rank == 0 else None
-# every replica must hold identical parameters after the synchronised updates
-import torch.distributed as dist
-from autodrive_b200.models import build_policy
-print(json.dumps({{"rank": state.rank, "world": r["world_size"], "transitions": r["transitions"]}}))
+# CPU plumbing configuration: two-robot defense env, 4 worlds per rank, static
+# FUEL (60 spheres at uniform random positions), a 200-tick rollout (16
+# strategic decisions held 12/13 ticks) against the deterministic scripted
+# offense, the 2 x 256 tanh MLP, PPO with 2 epochs x 4 minibatches, clip 0.2,
+# Adam lr 3e-4, seed 0
+r = train_once("defense", 4 * 16, {out!r}, seed=0, num_envs=4, device="cpu", opponent="offense",
+               rollout_steps=16, epochs=2, minibatch_size=16, horizon=200, fuel_physics=False,
+               clip_coef=.2, learning_rate=3e-4, network="mlp256", curriculum=False, dist_state=state,
+               env_kwargs={{"fuel_count": 60, "fuel_layout": "uniform"}})
+print(json.dumps({{"rank": state.rank, "world": r["world_size"], "transitions": r["transitions"],
+                  "ticks": r["physics_world_ticks_per_second"] > 0, "mean_reward": r["mean_reward"],
+                  "entropy": r["entropy"], "grad_norm": r["grad_norm"], "params": r["parameters_sha256"]}}))
 pdist.teardown(state)
 """
 
@@ -52,9 +56,14 @@ def test_two_rank_ppo(tmp_path):
     assert {r["rank"] for r in rows} == {0, 1}
     assert all(r["world"] == 2 for r in rows)
     # counters are all-reduced: both ranks report the global transition count
-    assert rows[0]["transitions"] == rows[1]["transitions"] == 2 * 2 * 4 * 8
+    assert rows[0]["transitions"] == rows[1]["transitions"] == 2 * 4 * 16
+    for r in rows:
+        assert all(math.isfinite(r[k]) for k in ("mean_reward", "entropy", "grad_norm")), r
+    # identical starting weights + averaged gradients: the replicas end equal
+    assert rows[0]["params"] == rows[1]["params"]
     status = json.load(open(os.path.join(out, "status.json")))
     assert status["status"] == "completed" and status["world_size"] == 2
+    assert status["network"] == "mlp256"
 
 
 def test_rank_that_never_joins_times_out(tmp_path):

@@ -112,3 +112,65 @@ def test_two_ranks_match_nccl_average(tmp_path, oneshot_bytes, mode):
         assert row["diff"] < 1e-5, row
         assert row["stats_ok"] and row["bcast_ok"], row
         assert abs(row["norm_a"] - row["norm_b"]) < 1e-4 * max(1., row["norm_a"]), row
+
+
+TIMEOUT_WORKER = r"""
+import json, os, sys, time, torch
+sys.path.insert(0, {root!r})
+from autodrive_b200.parallel import dist as pdist
+from autodrive_b200.parallel.p2p import FusedAllReduceAdam, PeerCommError
+from autodrive_b200.train.optim import FusedAdam
+state = pdist.distributed_state("cuda", timeout_s=120)
+rank = state.rank
+torch.manual_seed(0)
+model = torch.nn.Sequential(torch.nn.Linear(37, 64), torch.nn.Tanh(), torch.nn.Linear(64, 9)).cuda()
+opt = FusedAdam(model, lr=1e-2, max_grad_norm=.5)
+peer = FusedAllReduceAdam(opt, max_wait_iters=1 << 12)
+result = {{"rank": rank}}
+if rank == 0:
+    # rank 1 stays alive between steps but never joins this step: every
+    # bounded wait of rank 0's kernels must run out and report its phase
+    opt.zero_grad()
+    model(torch.randn(64, 37, device="cuda")).square().sum().backward()
+    t0 = time.perf_counter()
+    peer.step()
+    try:
+        peer.check(block=True)
+        result["step_error"] = None
+    except PeerCommError as exc:
+        result["step_error"] = str(exc)
+    result["step_seconds"] = time.perf_counter() - t0
+    sums = torch.ones(2, dtype=torch.float64, device="cuda")
+    peer.stats_allreduce(sums)
+    try:
+        peer.check(block=True)
+        result["stats_error"] = None
+    except PeerCommError as exc:
+        result["stats_error"] = str(exc)
+    result["status_after"] = int(peer.comm.status.item())
+    torch.cuda.synchronize()
+pdist.barrier()
+print(json.dumps(result))
+pdist.teardown(state)
+"""
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_wait_expiry_raises(tmp_path):
+    """A rank that skips a step makes the other rank's bounded device waits
+    run out: the kernel returns, the status word holds the phase and the host
+    raises PeerCommError naming it (gradients-ready, then stats exchange)."""
+    script = tmp_path / "timeout_worker.py"
+    script.write_text(TIMEOUT_WORKER.format(root=ROOT))
+    env = {**os.environ, "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_free_port()), "WORLD_SIZE": "2",
+           "NCCL_NVLS_ENABLE": "0"}
+    procs = [subprocess.Popen([sys.executable, str(script)], stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                              text=True, env={**env, "RANK": str(r), "LOCAL_RANK": str(r)}) for r in range(2)]
+    outs = [p.communicate(timeout=300) for p in procs]
+    for p, (so, se) in zip(procs, outs):
+        assert p.returncode == 0, se[-3000:]
+    row = json.loads(outs[0][0].strip().splitlines()[-1])
+    assert row["step_error"] and "gradients-ready" in row["step_error"], row
+    assert row["stats_error"] and "stats exchange" in row["stats_error"], row
+    assert row["status_after"] == 0, row
+    assert row["step_seconds"] < 30, row

@@ -126,3 +126,24 @@ def test_tc_linear_bf16_autocast_outputs_and_grads():
     for got, want in ((x.grad.float(), gx_ref), (tl.weight.grad, gw_ref), (tl.bias.grad, w.sum(0))):
         rel = (got - want).norm().item() / max(want.norm().item(), 1e-12)
         assert rel < 2e-2, rel
+
+
+@pytest.mark.gpu
+def test_gemm_wait_expiry_is_reported_and_context_survives():
+    """With a zero wait limit the kernel's bounded waits run out: the CTAs
+    drain their issued loads and MMAs, the status word records the phase, the
+    host raises TensorCoreTimeout (and clears the word), and the next GEMM
+    with the normal limit is correct."""
+    from autodrive_b200.ops.tc_linear import TensorCoreTimeout, check_gemm_status
+    g = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.randn(4096, 1024, device="cuda", generator=g).bfloat16()
+    b = torch.randn(1024, 1024, device="cuda", generator=g).bfloat16()
+    check_gemm_status()
+    gemm(a, b, wait_ns=0)
+    with pytest.raises(TensorCoreTimeout, match="wait ran out"):
+        check_gemm_status()
+    check_gemm_status()   # cleared
+    out = gemm(a, b)
+    check_gemm_status()
+    ref = a.float() @ b.float().T
+    assert (out - ref).abs().max().item() < 1e-3 * ref.abs().max().item()

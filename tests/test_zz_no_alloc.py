@@ -58,6 +58,33 @@ def test_noalloc_matches_existing_entry_point_twice():
             assert torch.allclose(a, b, rtol=1e-5, atol=1e-6)
 
 
+def test_noalloc_matches_torch_adam_and_clip_in_fp32():
+    """Two consecutive calls against the plain PyTorch fp32 update:
+    clip_grad_norm_(0.5) then torch.optim.Adam (lr 3e-4, betas .9/.999,
+    eps 1e-5)."""
+    _, fn, msg = _lib()
+    torch.manual_seed(1)
+    n = 65_537
+    ref = torch.nn.Parameter(torch.randn(n, device="cuda"))
+    opt = torch.optim.Adam([ref], lr=3e-4, betas=(.9, .999), eps=1e-5, foreach=False, fused=False)
+    p = ref.detach().clone()
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    norm = torch.zeros(1, device="cuda")
+    for step in (1, 2):
+        g = torch.randn(n, device="cuda") * (2. if step == 1 else .001)  # clipped, then unclipped
+        ref.grad = g.clone()
+        total = torch.nn.utils.clip_grad_norm_([ref], .5)
+        opt.step()
+        status = _call(fn, p, g, m, v, norm, step)
+        assert status == 0, msg(status)
+        torch.cuda.synchronize()
+        assert torch.allclose(norm, total.reshape(1), rtol=1e-5, atol=1e-6)
+        assert torch.allclose(p, ref.detach(), rtol=1e-5, atol=1e-6)
+        state = opt.state[ref]
+        assert torch.allclose(m, state["exp_avg"], rtol=1e-5, atol=1e-7)
+        assert torch.allclose(v, state["exp_avg_sq"], rtol=1e-5, atol=1e-9)
+
+
 def test_noalloc_rejects_block_count_beyond_scratch():
     _, fn, msg = _lib()
     n = 1024
