@@ -23,10 +23,17 @@ namespace ad {
 struct PlanScratch {
   uint8_t* blocked;   // [nx*ny]
   float* value;       // [nx*ny]
-  float* path;        // [kPathPoints*2]
-  float* tmp;         // [kPathPoints*2 + 4]
+  float* path;        // [plan_lattice_cap * 2]: lattice route of the greedy descent
+  float* tmp;         // [4 + plan_lattice_cap * 2]: resolved goal, then the simplified corners
   int* misc;          // [8]
 };
+
+// Lattice points the descent may walk: four times the grid's half perimeter
+// (a shortest 8-connected route is far shorter), at least kPathPoints.
+AD_HD int plan_lattice_cap(const SimParams& sp) {
+  const int c = 4 * (sp.plan_nx + sp.plan_ny);
+  return c > kPathPoints ? c : kPathPoints;
+}
 
 AD_HD int cell_index(const SimParams& sp, int ix, int iy) { return ix * sp.plan_ny + iy; }
 AD_HD float cell_x(const SimParams& sp, int ix) { return ((float)ix + .5f) * sp.plan_res; }
@@ -299,7 +306,8 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   int px = ps.misc[0], py = ps.misc[1];
   const int gx = ps.misc[2], gy = ps.misc[3];
   int len = 1;
-  for (int k = 1; k < kPathPoints; ++k) {
+  const int cap = plan_lattice_cap(sp);
+  for (int k = 1; k < cap; ++k) {
     if (px == gx && py == gy) break;
     float best = 1.e6f;
     int bk = -1;
@@ -328,7 +336,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   }
   // line-of-sight simplification (PathPlanner): a lattice point is kept only
   // when the last kept point cannot see the point after it
-  float* simp = ps.tmp + 4;  // [kPathPoints * 2]
+  float* simp = ps.tmp + 4;  // [plan_lattice_cap * 2]
   int m = 1;
   simp[0] = ps.path[0];
   simp[1] = ps.path[1];

@@ -370,10 +370,11 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
   const int nc = sp.plan_nx * sp.plan_ny;
   PlanScratch ps;
   float* f = reinterpret_cast<float*>(smem);
+  const int cap = plan_lattice_cap(sp);
   ps.value = f;
   ps.path = f + nc;
-  ps.tmp = ps.path + kPathPoints * 2;
-  ps.misc = reinterpret_cast<int*>(ps.tmp + kPathPoints * 2 + 4);
+  ps.tmp = ps.path + cap * 2;
+  ps.misc = reinterpret_cast<int*>(ps.tmp + cap * 2 + 4);
   ps.blocked = reinterpret_cast<uint8_t*>(ps.misc + 8);
   __shared__ PlanRequest q;
   if (threadIdx.x == 0) q = make_plan_request(w, sp, e, r);
@@ -435,7 +436,7 @@ std::vector<unsigned long long> sense_profile_read() {
 
 size_t plan_smem_bytes(const SimParams& sp) {
   const int nc = sp.plan_nx * sp.plan_ny;
-  return (size_t)(nc + kPathPoints * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc + 16;
+  return (size_t)(nc + plan_lattice_cap(sp) * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc + 16;
 }
 
 void validate_params(const SimParams& sp) {
@@ -549,10 +550,11 @@ void host_control(World w, const SimParams& sp, const int32_t* actions) {
 void host_plan(World w, const SimParams& sp, int force) {
   const int nc = sp.plan_nx * sp.plan_ny;
   host_parallel(sp.n * sp.R, [&](int, int b, int end) {
-    std::vector<float> fbuf(nc + kPathPoints * 4 + 4);
+    const int cap = plan_lattice_cap(sp);
+    std::vector<float> fbuf(nc + cap * 4 + 4);
     std::vector<uint8_t> blocked(nc);
     int misc[8];
-    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + kPathPoints * 2, misc};
+    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc};
     for (int row = b; row < end; ++row) {
       const int e = row / sp.R, r = row % sp.R;
       if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;

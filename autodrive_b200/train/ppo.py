@@ -169,7 +169,7 @@ class PPOLearner:
         if self.tc is not None:
             return self._update_tc(flat, entropy_coef)
         cfg = self.cfg
-        n = flat["obs"].shape[0]
+        n = flat["actions"].shape[0]
         mb = min(cfg.minibatch_size, n)
         kl = torch.zeros((), device=self.device)
         clip_frac = torch.zeros((), device=self.device)
