@@ -20,7 +20,9 @@ GET endpoints (JSON unless noted):
   /api/focused-playback?...                     same, short focused window
   /api/zone-playback-progress?simulation_id=I
   /api/zone-playback-result?simulation_id=I
+  /api/zone-playback-stream?simulation_id=I&offset=B   live frames of a recording from byte B
   /api/zone-playback-active
+  /api/meco-status          MECO runs: latest metrics per track, ledger chain check, weights digest
   /api/scenario-replays     saved recordings
 DELETE /api/scenario-replay?simulation_id=I   remove a finished saved recording
 
@@ -77,13 +79,22 @@ class Jobs:
         with self.lock:
             self.jobs[sid] = job
 
+        self.store.mkdir(parents=True, exist_ok=True)
+        stream = self.store / f"{sid}.stream.jsonl"
+
+        def emit(item: dict) -> None:
+            # one JSON object per line, appended as frames are produced
+            with stream.open("a") as fh:
+                fh.write(json.dumps(item, separators=(",", ":")) + "\n")
+
         def run():
             try:
                 rec = record_playback(seconds=seconds, device=self.device, seed=seed,
                                       checkpoint=str(checkpoint) if checkpoint else None,
                                       progress=lambda f: job.__setitem__("progress", round(f, 3)),
-                                      cancel=lambda: job["cancel"])
-                self.store.mkdir(parents=True, exist_ok=True)
+                                      cancel=lambda: job["cancel"],
+                                      on_metadata=lambda m: emit({"type": "metadata", **m}),
+                                      on_frame=lambda f: emit({"type": "frame", "frame": f}))
                 write_json_atomic(self.store / f"{sid}.json", rec)
                 job["state"] = "complete"
             except Exception as exc:  # noqa: BLE001 - reported through the API
@@ -96,8 +107,74 @@ class Jobs:
             return [{k: v for k, v in j.items() if k != "cancel"} for j in self.jobs.values() if j["state"] == "running"]
 
 
-def create_handler(run_dir, curriculum_root=None, device: str = "cpu"):
+def read_stream(jobs: "Jobs", q: dict) -> dict:
+    """Frames of a running (or finished) recording from byte `offset` of its
+    JSON-lines stream; `next_offset` resumes after the last complete line."""
+    sid = q.get("simulation_id", [""])[0]
+    if not _SIM.fullmatch(sid):
+        raise ValueError("invalid simulation_id")
+    offset = int(q.get("offset", ["0"])[0])
+    if offset < 0:
+        raise ValueError("offset must be a non-negative integer")
+    job = jobs.jobs.get(sid)
+    path = jobs.store / f"{sid}.stream.jsonl"
+    metadata, frames, next_offset = None, [], offset
+    if path.is_file():
+        size = path.stat().st_size
+        offset = 0 if offset > size else offset
+        with path.open("rb") as fh:
+            fh.seek(offset)
+            chunk = fh.read(1_000_000)
+        end = chunk.rfind(b"\n")
+        if end >= 0:
+            next_offset = offset + end + 1
+            for line in chunk[:end + 1].splitlines():
+                if not line:
+                    continue
+                item = json.loads(line)
+                if item.get("type") == "metadata":
+                    metadata = {k: v for k, v in item.items() if k != "type"}
+                elif item.get("type") == "frame" and isinstance(item.get("frame"), dict):
+                    frames.append(item["frame"])
+    state = job["state"] if job else ("complete" if (jobs.store / f"{sid}.json").is_file() else "waiting")
+    return {"simulation_id": sid, "metadata": metadata, "frames": frames, "next_offset": next_offset,
+            "status": state}
+
+
+def meco_status_payload(root: Path) -> dict:
+    """MECO research runs under `root`: per run directory with a metric
+    ledger, the latest update metrics per scorer track, the checkpoint digest
+    and whether the ledger's hash chain verifies; runs of the same scenario
+    family form one comparison group (frc_defense/meco_dashboard.py)."""
+    from ..meco.train import MetricLedger
+    policies, errors = [], []
+    for ledger_path in sorted(Path(root).glob("*/metric-ledger.jsonl")):
+        run = ledger_path.parent
+        try:
+            ledger = MetricLedger(ledger_path)
+            records = ledger.records()
+            chain_ok = ledger.verify()
+        except (OSError, ValueError, KeyError) as exc:
+            errors.append({"run": run.name, "error": str(exc)})
+            continue
+        updates = [r for r in records if r.get("kind") == "meco_update"]
+        checkpoint = next((r for r in reversed(records) if r.get("kind") == "checkpoint"), None)
+        last = updates[-1]["payload"] if updates else {}
+        policies.append({"run": run.name, "track": last.get("track"), "updates": len(updates),
+                         "latest": {k: v for k, v in last.items() if k not in ("config",)},
+                         "weights_sha256": (checkpoint or {}).get("payload", {}).get("weights_sha256"),
+                         "ledger_chain_verified": chain_ok, "records": len(records)})
+    groups: dict = {}
+    for pol in policies:
+        groups.setdefault(pol["latest"].get("scenario") or "default", []).append(pol["run"])
+    return {"schema_version": 1, "policies": policies,
+            "comparison_groups": [{"scenario": k, "runs": v} for k, v in sorted(groups.items())],
+            "errors": errors}
+
+
+def create_handler(run_dir, curriculum_root=None, device: str = "cpu", meco_root=None):
     run_dir = Path(run_dir)
+    meco_root = Path(meco_root) if meco_root else run_dir / "meco"
     curriculum_root = Path(curriculum_root) if curriculum_root else run_dir
     jobs = Jobs(run_dir / ".scenario-progress", device)
     identity = source_identity()
@@ -247,6 +324,17 @@ def create_handler(run_dir, curriculum_root=None, device: str = "cpu"):
                         return self._json({k: v for k, v in (job or {"id": sid, "state": "complete",
                                                                       "progress": 1.}).items() if k != "cancel"})
                     return self._file_json(jobs.store / f"{sid}.json", {"state": (job or {}).get("state", "missing")})
+                if p == "/api/zone-playback-stream":
+                    try:
+                        return self._json(read_stream(jobs, q))
+                    except ValueError as exc:
+                        return self.send_error(400, str(exc))
+                if p == "/api/meco-status":
+                    try:
+                        return self._json(meco_status_payload(meco_root))
+                    except (OSError, ValueError) as exc:
+                        return self._json({"schema_version": 1, "policies": [], "comparison_groups": [],
+                                           "errors": [{"error": f"MECO status unavailable: {exc}"}]}, 503)
                 if p == "/api/zone-playback-active":
                     return self._json(jobs.active())
                 if p == "/api/scenario-replays":
@@ -276,8 +364,9 @@ def create_handler(run_dir, curriculum_root=None, device: str = "cpu"):
     return Handler
 
 
-def serve(run_dir, host="127.0.0.1", port=8765, curriculum_root=None, device="cpu") -> ThreadingHTTPServer:
-    httpd = ThreadingHTTPServer((host, port), create_handler(run_dir, curriculum_root, device))
+def serve(run_dir, host="127.0.0.1", port=8765, curriculum_root=None, device="cpu",
+          meco_root=None) -> ThreadingHTTPServer:
+    httpd = ThreadingHTTPServer((host, port), create_handler(run_dir, curriculum_root, device, meco_root))
     return httpd
 
 
@@ -288,8 +377,9 @@ def main(argv=None) -> None:
     p.add_argument("--host", default="127.0.0.1")
     p.add_argument("--port", type=int, default=8765)
     p.add_argument("--device", default="cpu", help="device for playback recording jobs")
+    p.add_argument("--meco-root", default=None, help="MECO run directories (default: <run-dir>/meco)")
     a = p.parse_args(argv)
-    httpd = serve(a.run_dir, a.host, a.port, a.curriculum_root, a.device)
+    httpd = serve(a.run_dir, a.host, a.port, a.curriculum_root, a.device, a.meco_root)
     print(f"dashboard on http://{a.host}:{a.port} (run dir {a.run_dir})")
     try:
         httpd.serve_forever()

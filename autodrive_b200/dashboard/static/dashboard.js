@@ -1,5 +1,8 @@
 // Dashboard viewer: polls the JSON API and renders playback frames on a 2-D
-// canvas (field boxes, robots as oriented 0.9 m squares, FUEL, planned routes).
+// canvas (field boxes, robots as oriented 0.9 m squares with intake marker and
+// held-FUEL count, free FUEL, planned routes, navigation targets, each robot's
+// perceived FUEL tracks), streams a recording live while it is produced, and
+// lists training, curriculum and MECO status.
 "use strict";
 const $ = (id) => document.getElementById(id);
 const canvas = $("field");
@@ -47,8 +50,25 @@ function drawFrame(f) {
     const [px, py] = toCanvas(x, y);
     ctx.beginPath(); ctx.arc(px, py, 0.075 * s, 0, 2 * Math.PI); ctx.fill();
   }
+  const showTracks = $("show-tracks") && $("show-tracks").checked;
   f.robots.forEach((pose, r) => {
     const team = playback.teams ? playback.teams[r] : (r < 3 ? 0 : 1);
+    if (showTracks && f.tracks && f.tracks[r]) {
+      ctx.strokeStyle = team ? "#5ea8ff66" : "#ff6b6b66";
+      ctx.lineWidth = 1;
+      for (const [x, y] of f.tracks[r]) {
+        const [px, py] = toCanvas(x, y);
+        ctx.beginPath(); ctx.arc(px, py, 0.11 * s, 0, 2 * Math.PI); ctx.stroke();
+      }
+    }
+    if (f.targets && f.targets[r]) {
+      const [tx, ty] = toCanvas(f.targets[r][0], f.targets[r][1]);
+      ctx.strokeStyle = team ? "#9cc8ff" : "#ffa3a3";
+      ctx.lineWidth = 2;
+      ctx.beginPath();
+      ctx.moveTo(tx - 5, ty - 5); ctx.lineTo(tx + 5, ty + 5); ctx.moveTo(tx + 5, ty - 5); ctx.lineTo(tx - 5, ty + 5);
+      ctx.stroke();
+    }
     const route = f.routes ? f.routes[r] : [];
     if (route && route.length > 1) {
       ctx.setLineDash([6, 6]);
@@ -67,6 +87,11 @@ function drawFrame(f) {
     ctx.fillStyle = "#fff";
     ctx.fillRect(0.3 * s, -0.08 * s, 0.15 * s, 0.16 * s);
     ctx.restore();
+    const held = f.possession ? f.possession[r] : 0;
+    ctx.fillStyle = "#fff";
+    ctx.font = `${Math.max(10, 0.35 * s)}px sans-serif`;
+    ctx.textAlign = "center";
+    ctx.fillText(held ? `${r}:${held}` : `${r}`, px, py + 0.12 * s);
   });
   $("clock").textContent = `${f.time.toFixed(1)} s  red ${f.scores[2]}  blue ${f.scores[3]}`;
 }
@@ -109,13 +134,32 @@ async function refreshStatus() {
 async function record() {
   const run = $("run-select").value;
   const job = await getJSON(`/api/zone-playback?seconds=20&seed=${Date.now() % 1000}${run ? "&run=" + run : ""}`);
+  // live stream: frames appear as the recording job produces them
+  playback = { frames: [], teams: [0, 0, 0, 1, 1, 1] };
+  let offset = 0;
   const poll = async () => {
-    const p = await getJSON(`/api/zone-playback-progress?simulation_id=${job.simulation_id}`);
-    $("job").textContent = `${p.state} ${Math.round(100 * (p.progress || 0))}%`;
-    if (p.state === "running") return setTimeout(poll, 500);
-    if (p.state === "complete") loadPlayback(`/api/zone-playback-result?simulation_id=${job.simulation_id}`);
+    const st = await getJSON(`/api/zone-playback-stream?simulation_id=${job.simulation_id}&offset=${offset}`);
+    if (st.metadata) playback = { ...st.metadata, frames: playback.frames };
+    offset = st.next_offset;
+    if (st.frames.length) {
+      const atEnd = frame >= playback.frames.length - 1;
+      playback.frames.push(...st.frames);
+      $("scrub").max = Math.max(0, playback.frames.length - 1);
+      if (atEnd) show(playback.frames.length - 1);
+    }
+    $("job").textContent = `${st.status} ${playback.frames.length} frames`;
+    if (st.status === "running" || st.status === "waiting") return setTimeout(poll, 400);
   };
   poll();
+}
+
+async function refreshMeco() {
+  try {
+    const m = await getJSON("/api/meco-status");
+    $("meco").innerHTML = (m.policies || []).map((p) =>
+      `<li>${p.run}: track ${p.track ?? "?"}, ${p.updates} updates, ledger ${p.ledger_chain_verified ? "verified" : "BROKEN"}` +
+      `${p.weights_sha256 ? ", weights " + p.weights_sha256.slice(0, 12) : ""}</li>`).join("") || "<li>no MECO runs</li>";
+  } catch (e) { $("meco").innerHTML = "<li>MECO status unavailable</li>"; }
 }
 
 function tick() {
@@ -135,7 +179,9 @@ async function init() {
   $("scrub").oninput = (e) => show(+e.target.value);
   show(0);
   refreshStatus();
+  refreshMeco();
   setInterval(refreshStatus, 5000);
+  setInterval(refreshMeco, 15000);
   tick();
 }
 init();

@@ -24,6 +24,11 @@ def server(tmp_path):
     cur = run / "cur"
     cur.mkdir()
     (cur / "curriculum-status.json").write_text(json.dumps({"state": "complete", "qualified": ["pickup_simple"]}))
+    from autodrive_b200.meco.train import MetricLedger
+    ledger = MetricLedger(run / "meco" / "track-a" / "metric-ledger.jsonl")
+    ledger.append("meco_update", {"track": "A1", "update": 1, "mean_return": .1})
+    ledger.append("meco_update", {"track": "A1", "update": 2, "mean_return": .2})
+    ledger.append("checkpoint", {"path": "meco.pt", "weights_sha256": "ab" * 32})
     httpd = serve(run, port=0)
     t = threading.Thread(target=httpd.serve_forever, daemon=True)
     t.start()
@@ -59,6 +64,9 @@ def test_endpoints(server):
     cur = json.loads(_get(server + "/api/curriculum-status")[2])
     assert cur and cur[0]["qualified"] == ["pickup_simple"]
     assert _get(server + "/api/nope")[0] == 404
+    meco = json.loads(_get(server + "/api/meco-status")[2])
+    assert meco["schema_version"] == 1 and meco["policies"][0]["run"] == "track-a"
+    assert meco["policies"][0]["ledger_chain_verified"] and meco["policies"][0]["updates"] == 2
 
 
 def test_recording_job_and_delete(server):
@@ -73,6 +81,14 @@ def test_recording_job_and_delete(server):
     assert p["state"] == "complete", p
     rec = json.loads(_get(server + f"/api/zone-playback-result?simulation_id={sid}")[2])
     assert len(rec["frames"]) == 10 and len(rec["frames"][0]["robots"]) == 6
+    assert len(rec["frames"][0]["tracks"]) == 6 and len(rec["frames"][0]["possession"]) == 6
+    # the live stream carries the same frames, resumable from a byte offset
+    first = json.loads(_get(server + f"/api/zone-playback-stream?simulation_id={sid}&offset=0")[2])
+    assert first["status"] == "complete" and first["metadata"]["teams"] == [0, 0, 0, 1, 1, 1]
+    assert [f["tick"] for f in first["frames"]] == [f["tick"] for f in rec["frames"]]
+    rest = json.loads(_get(server + f"/api/zone-playback-stream?simulation_id={sid}&offset={first['next_offset']}")[2])
+    assert rest["frames"] == [] and rest["next_offset"] == first["next_offset"]
+    assert _get(server + "/api/zone-playback-stream?simulation_id=../x")[0] == 400
     assert any(r["simulation_id"] == sid for r in json.loads(_get(server + "/api/scenario-replays")[2]))
     assert _get(server + f"/api/scenario-replay?simulation_id={sid}", method="DELETE")[0] == 200
     assert _get(server + "/api/scenario-replay?simulation_id=bad/../x", method="DELETE")[0] == 400
