@@ -94,6 +94,14 @@ class TensorThreeVsThreeEnv:
             raise ValueError("turret_scoring_bps must be finite and positive")
         if behavior_probe is not None:
             raise ValueError("behavior probes are not supported by this simulator")
+        if len(tuple(obstacles)):
+            raise ValueError("static circular obstacles are not modelled by the 3v3 kernels; the field's "
+                             "structures are the REBUILT layout's boxes")
+        # the sensor noise/dropout draws always come from the in-kernel
+        # counter-based generator (the reference's fused_sensor_rng=True path)
+        self.fused_sensor_rng = True
+        self.random_gamepiece_placement = bool(random_gamepiece_placement)
+        self._placement_generator = torch.Generator(device="cpu").manual_seed(int(seed or 0) ^ 0x5A17)
         self.device = torch.device(device)
         self.dt, self.horizon = float(dt), int(horizon)
         self.field_length = float(field_length)
@@ -362,6 +370,21 @@ class TensorThreeVsThreeEnv:
         P = self.fuel_count
         fpos = torch.zeros((self.n, 3, P), device=self.device)
         xy = pos.to(self.device)[None].expand(self.n, -1, -1).clone()
+        if self.random_gamepiece_placement:
+            # every staged piece on a random distinct cell of a whole-field
+            # lattice spaced one diameter + 1 cm (frc_defense/tensor_defense_gamepieces.py:175-193)
+            half = .075
+            spacing = 2 * half + .01
+            nx = int((self.field_length - 2 * half) // spacing) + 1
+            ny = int((self.field_width - 2 * half) // spacing) + 1
+            gx, gy = torch.meshgrid(half + torch.arange(nx) * spacing, half + torch.arange(ny) * spacing,
+                                    indexing="ij")
+            cells = torch.stack((gx.reshape(-1), gy.reshape(-1)), -1)
+            staged = active & (owner < 0)
+            count = int(staged.sum())
+            order = torch.rand((self.n, cells.shape[0]), generator=self._placement_generator).argsort(-1)[:, :count]
+            idx = staged.nonzero().squeeze(-1)
+            xy[:, idx] = cells[order].to(self.device)
         for r, b, e in preload:
             xy[:, b:e] = ws["r_pose"][:, r, None, :2]
         fpos[:, 0] = xy[..., 0]

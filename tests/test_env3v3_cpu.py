@@ -80,3 +80,18 @@ def test_fuel_physics_keeps_pieces_in_field():
     assert torch.isfinite(pos).all()
     assert bool((pos[..., 0][live] > -0.01).all() and (pos[..., 0][live] < 16.55).all())
     assert bool((pos[..., 2][live] > 0.).all())
+
+
+def test_random_gamepiece_placement_and_rejected_obstacles():
+    import pytest
+    from autodrive_b200.sim.env3v3 import TensorThreeVsThreeEnv
+    a = TensorThreeVsThreeEnv(num_envs=2, device="cpu", seed=4, fuel_physics=False, random_gamepiece_placement=True)
+    b = TensorThreeVsThreeEnv(num_envs=2, device="cpu", seed=4, fuel_physics=False)
+    pa, pb = a.piece_pos, b.piece_pos
+    act = a.piece_active
+    assert not torch.equal(pa[0][act[0]], pb[0][act[0]])
+    assert not torch.equal(pa[0][act[0]], pa[1][act[1]])          # each world draws its own layout
+    d = torch.cdist(pa[0][act[0]], pa[0][act[0]]) + torch.eye(int(act[0].sum())) * 10
+    assert float(d.min()) >= .159                                  # distinct lattice cells
+    with pytest.raises(ValueError, match="obstacles"):
+        TensorThreeVsThreeEnv(num_envs=1, device="cpu", fuel_physics=False, obstacles=((8., 4., .3),))
