@@ -267,6 +267,8 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   const int dxs[8] = {1, -1, 0, 0, 1, 1, -1, -1};
   const int dys[8] = {0, 0, 1, -1, 1, -1, 1, -1};
   volatile float* vv = ps.value;
+  int sweeps_run = 0;
+  bool converged = false;
   for (int sweep = 0; sweep < sp.plan_sweeps; ++sweep) {
     const int dir = sweep & 3;
     const bool along_x = dir < 2;
@@ -299,9 +301,15 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
 #else
     const int any = changed;
 #endif
-    if (!any) break;
+    sweeps_run = sweep + 1;
+    if (!any) {
+      converged = true;
+      break;
+    }
   }
   SERIAL_BEGIN
+  // sweeps used; negative when the budget ran out before a sweep changed nothing
+  w.p_sweeps[er] = converged ? sweeps_run : -sweeps_run;
   // greedy descent
   int px = ps.misc[0], py = ps.misc[1];
   const int gx = ps.misc[2], gy = ps.misc[3];

@@ -11,7 +11,7 @@
 // Persistent kernel: one CTA per SM (at most one per work item) walks the
 // 128x128 output tiles (x split-K slices) in a static round-robin, N tiles
 // fastest so the CTAs running at the same time share A row blocks in L2.
-// 192 threads:
+// 320 threads:
 //   warp 0  TMA producer: 2-D tiled loads (128-byte swizzle) of the A and B
 //           tiles of each 64-deep K step into a 4-stage shared-memory ring
 //           that runs continuously across tiles;
@@ -19,9 +19,10 @@
 //           one lane issues 4 tcgen05.mma per K step into the accumulator of
 //           the current tile, commits each stage back to the producer and
 //           the finished accumulator to the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator rows (the accumulator
-//           is handed back to the MMA warp as soon as it is read), + bias,
-//           activation, fp32 or bf16 stores with bounds checks.
+//   warps 2-9 epilogue, two per TMEM lane quadrant, each owning half of the
+//           column chunks: both of its tcgen05.ld loads in flight at once, the
+//           accumulator handed back to the MMA warp as soon as it is read,
+//           then + bias, activation, fp32 or bf16 stores with bounds checks.
 // With two accumulators the epilogue of tile i overlaps the loads and MMAs
 // of tile i+1. Out-of-range tile parts are zero-filled by the TMA unit.
 // Every mbarrier wait is bounded in wall-clock time (`wait_ns`, 2 s by
@@ -48,7 +49,8 @@ namespace py = pybind11;
 namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                    // two warps per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTileBytes = 128 * 128;        // one 128 x 64 bf16 operand tile
 constexpr uint32_t kStageBytes = 2 * kTileBytes;
 constexpr uint64_t kDrainNs = 200000000ull;       // 200 ms for in-flight copies / MMAs after a failure
@@ -165,7 +167,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(tfull0 + 8 * a, 1);
-      tc::mbar_init(tempty0 + 8 * a, 128);   // every epilogue thread arrives
+      tc::mbar_init(tempty0 + 8 * a, 32 * kEpiWarps);   // every epilogue thread arrives
     }
     tc::mbar_init(drain, 1);
     tc::mbar_init_fence();
@@ -266,8 +268,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   }
 
   if (warp >= 2) {
-    // ---- epilogue ----
-    const int q = warp & 3;               // TMEM lanes 32q..32q+31 belong to this warp
+    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its quadrant) and
+    // the column chunks of its half (two warps per quadrant); both chunks'
+    // loads are in flight together, and the accumulator is handed back to the
+    // MMA warp before the stores
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int kChunks = kBN / 32 / 2;  // chunks per warp
     int lt = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++lt) {
       const TileCoord t = tile_of(w, tiles_n, tiles_m);
@@ -280,15 +287,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       if (!got || *fail) break;
       tc::tc_fence_after();
       const int row = t.m0 + 32 * q + lane;
-#pragma unroll 1
-      for (int cc = 0; cc < kBN / 32; ++cc) {
-        float v[32];
-        tc::tmem_ld32(tmem + acc * kAccCols + ((uint32_t)(32 * q) << 16) + 32 * cc, v);
-        if (cc == kBN / 32 - 1) {         // accumulator read out: the MMA warp may reuse it
-          tc::tc_fence_before();
-          tc::mbar_arrive(tempty0 + 8 * acc);
-        }
-        if (row < g.M) store_chunk(g, v, row, t.n0 + 32 * cc, t.z);
+      float v[kChunks][32];
+      const uint32_t base = tmem + acc * kAccCols + ((uint32_t)(32 * q) << 16);
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) tc::tmem_ld32_issue(base + 32 * (2 * k + half), v[k]);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < kChunks; ++k) tc::tmem_regs_ready(v[k]);
+      tc::tc_fence_before();
+      tc::mbar_arrive(tempty0 + 8 * acc);   // accumulator read out: the MMA warp may reuse it
+      if (row < g.M) {
+#pragma unroll
+        for (int k = 0; k < kChunks; ++k) store_chunk(g, v[k], row, t.n0 + 32 * (2 * k + half), t.z);
       }
     }
   }

@@ -130,6 +130,7 @@ enum DType : int { DT_F32 = 0, DT_I32 = 1, DT_U8 = 2, DT_I8 = 3, DT_F64 = 4 };
   X(p_heading, float, DT_F32, 2, N, R, 1, 1)                            \
   X(p_progress, float, DT_F32, 2, N, R, 1, 1)                           \
   X(p_trench, uint8_t, DT_U8, 2, N, R, 1, 1)                            \
+  X(p_sweeps, int32_t, DT_I32, 2, N, R, 1, 1)                           \
   X(obs, float, DT_F32, 3, N, R, O, 1)                                  \
   X(e_episode, int32_t, DT_I32, 1, N, 1, 1, 1)                         \
   X(active, uint8_t, DT_U8, 1, N, 1, 1, 1)

@@ -175,8 +175,9 @@ class TensorThreeVsThreeEnv:
             teammate_coordination=int(self.teammate_coordination_enabled),
             normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=float(planner_resolution), plan_nx=plan_nx, plan_ny=plan_ny,
-            plan_sweeps=int(planner_sweeps if planner_sweeps is not None else
-                            max(72, math.ceil(72 * .3 / planner_resolution - 1e-6))),
+            # directional line sweeps; the iteration stops at the first sweep
+            # that changes no cell, so the budget only bounds pathological grids
+            plan_sweeps=int(planner_sweeps if planner_sweeps is not None else 4 * (plan_nx + plan_ny)),
             fuel_radius_rules=.0825, stereo_tracks=1,
             sweeping=int(self.sweeping_enabled), raster_lookahead=20,
             depots=[d.as_tensor() for d in sorted(fieldmod.depot_boxes(self.field_boxes),
@@ -584,4 +585,6 @@ class PlannerView:
     last_heading = property(lambda self: self.ws["p_heading"].reshape(-1))
     last_progress = property(lambda self: self.ws["p_progress"].reshape(-1))
     last_trench_alignment = property(lambda self: self.ws["p_trench"].reshape(-1).bool())
+    # value-iteration sweeps of each row's last plan (negative: budget ran out first)
+    last_sweeps = property(lambda self: self.ws["p_sweeps"].reshape(-1))
     last_speed_profile = property(lambda self: self.ws["p_profile"].reshape(-1, self.ws["p_profile"].shape[2]))

@@ -196,7 +196,8 @@ class TensorDefenseEnv:
             perception_fov=math.radians(fov) * .5, track_timeout=self.perception_track_timeout,
             replan_interval=replan, normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=.3, plan_nx=math.ceil(field_length / .3), plan_ny=math.ceil(field_width / .3),
-            plan_sweeps=72, fuel_radius_rules=.0825, perception_interval=1)
+            plan_sweeps=4 * (math.ceil(field_length / .3) + math.ceil(field_width / .3)), fuel_radius_rules=.0825,
+            perception_interval=1)
         self.ws = WorldState(params, self.device)
         self.sim = RobotView(self.ws, dt=self.dt, field_length=field_length, field_width=field_width,
                              team_ids=(0, 1), boxes=[b.as_tensor() for b in solids],

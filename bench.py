@@ -184,6 +184,7 @@ def run_train(args, rank, world, local):
     t0 = state["ticks"]
     e2e_ms = _timed(e2e_step, args.steps, world)
     e2e_ticks = args.envs * (state["ticks"] - t0) * world
+    profile = _profile_step(step, args.profile) if args.profile else None
     decisions_ticks = ticks_timed / max(1, args.steps)
     minibatches = args.epochs * args.minibatches
     # own kernels per step: control+plan+tick+sense+observe per tick (C++ launches); on the fused
@@ -222,7 +223,34 @@ def run_train(args, rank, world, local):
                            "tcgen05 GEMM + fused LayerNorm kernels with torch attention/elementwise"),
         "final_stats": {"mean_reward": float(stats_dev[0]), "approx_kl": float(stats_dev[1]),
                         "entropy": float(stats_dev[2]), "grad_norm": float(stats_dev[3])},
+        **({"profile": profile} if profile else {}),
     }
+
+
+def _profile_step(step, path: str) -> dict:
+    """One extra (untimed) step under torch.profiler: device time per kernel
+    name, written to `path` as JSON (top 40) and summarised in the result."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    rows = []
+    for e in prof.key_averages():
+        dev = getattr(e, "device_time_total", None)
+        if dev is None:
+            dev = getattr(e, "cuda_time_total", 0.)
+        if dev > 0:
+            rows.append({"name": e.key[:160], "device_ms": dev / 1e3, "calls": e.count})
+    rows.sort(key=lambda r: -r["device_ms"])
+    total = sum(r["device_ms"] for r in rows)
+    for r in rows:
+        r["share"] = r["device_ms"] / max(total, 1e-9)
+    with open(path, "w") as f:
+        json.dump({"device_ms_total": total, "kernels": rows[:40]}, f, indent=1)
+    return {"device_ms_total": round(total, 3), "top": [(r["name"][:60], round(r["share"], 4)) for r in rows[:8]],
+            "file": path}
 
 
 def run_sim(args, rank, world, local):
@@ -373,6 +401,8 @@ def main():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--reference-budget-s", type=float, default=900.)
+    p.add_argument("--profile", help="train mode: also run one step under torch.profiler and write the device "
+                                     "time per kernel to this JSON file")
     args = p.parse_args()
     if args.warmup < 3:
         p.error("at least 3 warm-up steps are required")
