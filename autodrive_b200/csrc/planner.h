@@ -26,6 +26,7 @@ struct PlanScratch {
   float* path;        // [plan_lattice_cap * 2]: lattice route of the greedy descent
   float* tmp;         // [4 + plan_lattice_cap * 2]: resolved goal, then the simplified corners
   int* misc;          // [8]
+  unsigned long long* best;  // [2] packed endpoint-projection minima
 };
 
 // Lattice points the descent may walk: four times the grid's half perimeter
@@ -218,27 +219,43 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     ps.blocked[c] = b ? 1 : 0;
   }
   BARRIER();
-  SERIAL_BEGIN
-  // project blocked endpoints to the nearest free cell
+  // project blocked endpoints to the nearest free cell: a block-wide minimum
+  // of packed (squared distance, cell index) keys, i.e. the nearest free cell
+  // with ties to the lower index (the serial scan's choice)
   float pts[4] = {q.sx, q.sy, q.gx, q.gy};
+  bool need[2];
   for (int k = 0; k < 2; ++k) {
-    int ix = clampi((int)floorf(pts[k * 2] / sp.plan_res), 0, nx - 1);
-    int iy = clampi((int)floorf(pts[k * 2 + 1] / sp.plan_res), 0, ny - 1);
-    if (!ps.blocked[cell_index(sp, ix, iy)]) continue;
-    float best = kInf;
-    int bc = -1;
-    for (int c = 0; c < nc; ++c) {
+    const int ix = clampi((int)floorf(pts[k * 2] / sp.plan_res), 0, nx - 1);
+    const int iy = clampi((int)floorf(pts[k * 2 + 1] / sp.plan_res), 0, ny - 1);
+    need[k] = ps.blocked[cell_index(sp, ix, iy)] != 0;
+  }
+  SERIAL_BEGIN
+  ps.best[0] = ps.best[1] = ~0ull;
+  SERIAL_END
+  BARRIER();
+  if (need[0] || need[1]) {
+    PAR_FOR(c, nc) {
       if (ps.blocked[c]) continue;
-      float d = sqr(cell_x(sp, c / ny) - pts[k * 2]) + sqr(cell_y(sp, c % ny) - pts[k * 2 + 1]);
-      if (d < best) {
-        best = d;
-        bc = c;
+      const float cx = cell_x(sp, c / ny), cy = cell_y(sp, c % ny);
+      for (int k = 0; k < 2; ++k) {
+        if (!need[k]) continue;
+        const float d = sqr(cx - pts[k * 2]) + sqr(cy - pts[k * 2 + 1]);
+        const unsigned long long key = ((unsigned long long)float_bits(d) << 32) | (unsigned)c;
+#if defined(__CUDA_ARCH__)
+        atomicMin(&ps.best[k], key);
+#else
+        if (key < ps.best[k]) ps.best[k] = key;
+#endif
       }
     }
-    if (bc >= 0) {
-      pts[k * 2] = cell_x(sp, bc / ny);
-      pts[k * 2 + 1] = cell_y(sp, bc % ny);
-    }
+  }
+  BARRIER();
+  SERIAL_BEGIN
+  for (int k = 0; k < 2; ++k) {
+    if (!need[k] || ps.best[k] == ~0ull) continue;
+    const int bc = (int)(ps.best[k] & 0xffffffffull);
+    pts[k * 2] = cell_x(sp, bc / ny);
+    pts[k * 2 + 1] = cell_y(sp, bc % ny);
   }
   ps.misc[0] = clampi((int)floorf(pts[0] / sp.plan_res), 0, nx - 1);
   ps.misc[1] = clampi((int)floorf(pts[1] / sp.plan_res), 0, ny - 1);
@@ -342,27 +359,65 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     ps.path[(len - 1) * 2] = ps.tmp[0];
     ps.path[(len - 1) * 2 + 1] = ps.tmp[1];
   }
+  ps.misc[6] = len;
+  SERIAL_END
+  BARRIER();
   // line-of-sight simplification (PathPlanner): a lattice point is kept only
-  // when the last kept point cannot see the point after it
+  // when the last kept point cannot see the point after it. Round by round:
+  // every thread tests the sight line from the current anchor to one later
+  // lattice point, the first blocked one (index j) makes point j-1 the next
+  // kept point and anchor; the serial rule's result, in as many rounds as
+  // there are corners
   float* simp = ps.tmp + 4;  // [plan_lattice_cap * 2]
-  int m = 1;
+  const int len = ps.misc[6];
+  SERIAL_BEGIN
   simp[0] = ps.path[0];
   simp[1] = ps.path[1];
+  ps.misc[5] = 0;   // anchor
+  ps.misc[7] = 1;   // kept points
+  SERIAL_END
+  BARRIER();
   if (len > 1) {
-    int anchor = 0;
-    for (int k = 1; k < len - 1; ++k) {
-      if (!grid_line_clear(sp, ps.blocked, ps.path[anchor * 2], ps.path[anchor * 2 + 1], ps.path[(k + 1) * 2],
-                           ps.path[(k + 1) * 2 + 1])) {
-        simp[m * 2] = ps.path[k * 2];
-        simp[m * 2 + 1] = ps.path[k * 2 + 1];
-        ++m;
-        anchor = k;
+    while (true) {
+      const int anchor = ps.misc[5];
+      SERIAL_BEGIN
+      ps.misc[4] = len;
+      SERIAL_END
+      BARRIER();
+      const float ax = ps.path[anchor * 2], ay = ps.path[anchor * 2 + 1];
+      PAR_FOR(j0, len - anchor - 2) {
+        const int j = anchor + 2 + j0;
+        if (!grid_line_clear(sp, ps.blocked, ax, ay, ps.path[j * 2], ps.path[j * 2 + 1])) {
+#if defined(__CUDA_ARCH__)
+          atomicMin(&ps.misc[4], j);
+#else
+          if (j < ps.misc[4]) ps.misc[4] = j;
+#endif
+        }
       }
+      BARRIER();
+      const int fail = ps.misc[4];
+      BARRIER();
+      if (fail >= len) break;
+      SERIAL_BEGIN
+      const int m = ps.misc[7];
+      simp[m * 2] = ps.path[(fail - 1) * 2];
+      simp[m * 2 + 1] = ps.path[(fail - 1) * 2 + 1];
+      ps.misc[7] = m + 1;
+      ps.misc[5] = fail - 1;
+      SERIAL_END
+      BARRIER();
     }
+    SERIAL_BEGIN
+    const int m = ps.misc[7];
     simp[m * 2] = ps.path[(len - 1) * 2];
     simp[m * 2 + 1] = ps.path[(len - 1) * 2 + 1];
-    ++m;
+    ps.misc[7] = m + 1;
+    SERIAL_END
+    BARRIER();
   }
+  SERIAL_BEGIN
+  const int m = ps.misc[7];
   // smoothed route: cubic Bezier corners with the longest handle (0.4, 0.28,
   // 0.18, 0.1, 0 x segment length) whose samples and kPathPoints-point
   // equal-arc resampling stay on free cells; else the simplified polyline,

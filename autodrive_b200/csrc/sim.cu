@@ -377,6 +377,8 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
   ps.misc = reinterpret_cast<int*>(ps.tmp + cap * 2 + 4);
   ps.blocked = reinterpret_cast<uint8_t*>(ps.misc + 8);
   __shared__ PlanRequest q;
+  __shared__ unsigned long long s_best[2];
+  ps.best = s_best;
   if (threadIdx.x == 0) q = make_plan_request(w, sp, e, r);
   __syncthreads();
   plan_route(w, sp, e, r, q, ps);
@@ -554,7 +556,8 @@ void host_plan(World w, const SimParams& sp, int force) {
     std::vector<float> fbuf(nc + cap * 4 + 4);
     std::vector<uint8_t> blocked(nc);
     int misc[8];
-    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc};
+    unsigned long long best[2];
+    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc, best};
     for (int row = b; row < end; ++row) {
       const int e = row / sp.R, r = row % sp.R;
       if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;

@@ -305,6 +305,37 @@ class _PackedAttention(torch.autograd.Function):
         return gqkv, None, None, None, None
 
 
+class _VarlenQueryAttention(torch.autograd.Function):
+    """One query per sample attending over that sample's packed keys and
+    values: q [b, d], kv [total, 2d] (keys then values, sample i at rows
+    cu_k[i]:cu_k[i+1]) on the memory-efficient attention kernel with
+    variable-length keys. Used for the last entity block, whose only consumed
+    output is the context token's."""
+
+    @staticmethod
+    def forward(ctx, q: Tensor, kv: Tensor, heads: int, cu_q: Tensor, cu_k: Tensor, max_k: int) -> Tensor:
+        b, d = q.shape
+        dh = d // heads
+        x = kv.view(1, kv.shape[0], 2, heads, dh)
+        out, lse, seed, offset, _, _ = torch.ops.aten._efficient_attention_forward(
+            q.view(1, b, heads, dh), x.select(2, 0), x.select(2, 1), None, cu_q, cu_k, 1, max_k, 0.0, 0, True)
+        ctx.heads, ctx.max_k = heads, max_k
+        ctx.save_for_backward(q, kv, out, lse, seed, offset, cu_q, cu_k)
+        return out.reshape(b, d)
+
+    @staticmethod
+    def backward(ctx, grad: Tensor):
+        q, kv, out, lse, seed, offset, cu_q, cu_k = ctx.saved_tensors
+        b, d = q.shape
+        h = ctx.heads
+        x = kv.view(1, kv.shape[0], 2, h, d // h)
+        gq, gk, gv, _ = torch.ops.aten._efficient_attention_backward(
+            grad.reshape(out.shape).contiguous().to(out.dtype), q.view(1, b, h, d // h), x.select(2, 0),
+            x.select(2, 1), None, out, cu_q, cu_k, 1, ctx.max_k, lse, 0.0, seed, offset, 0, False)
+        gkv = torch.stack((gk, gv), 2).reshape(kv.shape)
+        return gq.reshape(b, d), gkv, None, None, None, None
+
+
 class SelfAttention(nn.Module):
     """Multi-head self-attention with key padding; projections packed as
     ``in_proj_weight`` [3d, d] and ``out_proj`` like nn.MultiheadAttention."""
@@ -323,6 +354,17 @@ class SelfAttention(nn.Module):
         (sample i at rows cu[i]:cu[i+1]); CUDA, bf16 / fp16 projections."""
         qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
         return self.out_proj(_PackedAttention.apply(qkv, None, self.heads, cu, max_len))
+
+    def forward_packed_query(self, x: Tensor, cu: Tensor, max_len: int, rows: Tensor) -> Tensor:
+        """Attention output of the packed tokens `rows` only (one per sample,
+        e.g. each context token) over all valid tokens of their sample: the
+        key / value projection covers every token, the query projection only
+        those rows."""
+        d = self.dim
+        kv = _linear(x, self.in_proj_weight[d:], self.in_proj_bias[d:], self.tensor_cores)
+        q = _linear(x[rows], self.in_proj_weight[:d], self.in_proj_bias[:d], self.tensor_cores)
+        cu_q = torch.arange(rows.numel() + 1, device=x.device, dtype=torch.int32)
+        return self.out_proj(_VarlenQueryAttention.apply(q, kv, self.heads, cu_q, cu, max_len))
 
     def forward(self, x: Tensor, padding: Tensor) -> Tensor:
         b, t, d = x.shape
@@ -350,6 +392,13 @@ class EntityAttentionBlock(nn.Module):
     def forward_packed(self, tokens: Tensor, cu: Tensor, max_len: int) -> Tensor:
         tokens = tokens + self.attention.forward_packed(self.norm_attention(tokens), cu, max_len)
         return tokens + self.feedforward(self.norm_feedforward(tokens))
+
+    def forward_packed_rows(self, tokens: Tensor, cu: Tensor, max_len: int, rows: Tensor) -> Tensor:
+        """This block's outputs for the packed tokens `rows` only (one per
+        sample): the same values `forward_packed(...)[rows]` gives, without
+        the queries, projections and feed-forward of the other tokens."""
+        out = tokens[rows] + self.attention.forward_packed_query(self.norm_attention(tokens), cu, max_len, rows)
+        return out + self.feedforward(self.norm_feedforward(out))
 
     def forward(self, tokens: Tensor, padding: Tensor) -> Tensor:
         tokens = tokens + self.attention(self.norm_attention(tokens), padding)
@@ -404,9 +453,11 @@ class EntityAttentionPolicy(nn.Module):
         first = cu[:-1].long()
         ctx = self.scalar_encoder(inputs["scalars"])
         tokens = tokens.index_put((first,), ctx.to(tokens.dtype))
-        for blk in self.blocks:
+        for blk in self.blocks[:-1]:
             tokens = blk.forward_packed(tokens, cu, max_len)
-        h = self.fusion(tokens[first])
+        # only the context token's final state is read, so the last block
+        # computes its output for those rows alone
+        h = self.fusion(self.blocks[-1].forward_packed_rows(tokens, cu, max_len, first))
         return self.actor(h), self.critic(h).squeeze(-1)
 
     def forward(self, inputs: dict) -> tuple[Tensor, Tensor]:

@@ -66,8 +66,24 @@ _PRIM = GateDefinition()
 _CYCLE = GateDefinition(throughput_ratio=.8)
 _PRESS = GateDefinition(throughput_ratio=.8, min_useful_throughput=.01)
 _ROUTES = ("open", "trench", "bump")
+_BOTH_ROUTES = tuple(f"{phase}/{route}" for phase in ("active", "inactive") for route in _ROUTES)
+# HUB-switch categories: direction / load / time left before the switch / situation
+_TRANSITIONS = tuple(
+    f"{direction}/{load}/{timing}/{situation}"
+    for direction, situations in (("active_to_inactive", ("collecting", "carrying_home", "approaching_shot")),
+                                  ("inactive_to_active", ("before_release", "after_release", "staged_at_home")))
+    for load in ("empty", "partial", "full")
+    for timing in ("enough_time", "too_little_time")
+    for situation in situations) + ("empty_collection", "hold_useful_load")
+# blocker levels: none, a parked robot on the route, a patrolling defender, a
+# blocker in the trench / on the bump / at a seeded choice of route, two
+# reactive defenders, and a per-world mixture
+_BLOCKERS = ("level_0", "level_1_stationary", "level_2_patrol", "level_3_trench", "level_3_bump",
+             "level_3_seeded_choice", "level_4_reactive", "level_5_mixed")
 _PRESSURE = tuple(f"{ph}/{route}/{lvl}" for ph in ("active", "inactive") for route in _ROUTES
-                  for lvl in ("level_0", "level_1_stationary", "level_2_patrol", "level_4_reactive"))
+                  for lvl in _BLOCKERS
+                  if (lvl != "level_3_trench" or route == "trench") and (lvl != "level_3_bump" or route == "bump")
+                  and (lvl != "level_3_seeded_choice" or route != "open"))
 
 
 def _sc(name, stage, prereq, cats, budget, gate, success):
@@ -76,27 +92,30 @@ def _sc(name, stage, prereq, cats, budget, gate, success):
 
 SCENARIOS = {s.scenario_id: s for s in (
     _sc("pickup_simple", "1", (), ("single", "cluster"), 20., _PRIM, "acquire and retain the required distinct FUEL"),
-    _sc("pickup_scattered", "2", ("pickup_simple",), ("sparse", "dense"), 40., _PRIM,
+    _sc("pickup_scattered", "2", ("pickup_simple",), ("sparse", "dense", "initially_hidden"), 40., _PRIM,
         "retain the required fraction of the available FUEL"),
-    _sc("pickup_multi_zone", "3", ("pickup_scattered",), ("productive", "depleted"), 60., _PRIM,
-        "leave depleted zones and collect from productive ones"),
+    _sc("pickup_multi_zone", "3", ("pickup_scattered",), ("productive", "empty", "depleted"), 60., _PRIM,
+        "leave empty or depleted zones and collect from productive ones"),
     _sc("active_carry_to_zone", "4A", ("pickup_multi_zone",), ("active/trench", "active/bump"), 35., _PRIM,
         "reach the scoring area with the load while the HUB is active"),
-    _sc("active_shoot_preloaded", "4B", ("pickup_simple",), ("active/preloaded", "active/approach"), 25., _PRIM,
+    _sc("active_shoot_preloaded", "4B", ("pickup_simple",),
+        ("active/preloaded", "active/approach", "active/heading_error"), 25., _PRIM,
         "score the preloaded FUEL while the friendly HUB is active"),
-    _sc("inactive_ferry_preloaded", "4C", ("pickup_simple",), ("inactive/preloaded", "inactive/partial_load"), 30.,
+    _sc("inactive_ferry_preloaded", "4C", ("pickup_simple",),
+        ("inactive/preloaded", "inactive/approach", "inactive/alignment", "inactive/partial_load",
+         "inactive/full_load", "inactive/landing"), 30.,
         _PRIM, "deliver preloaded FUEL into the friendly staging zone"),
     _sc("active_collect_carry_score", "5A", ("pickup_multi_zone", "active_carry_to_zone", "active_shoot_preloaded"),
         tuple(f"active/{r}" for r in _ROUTES), 90., _CYCLE, "repeat collect-and-score cycles"),
     _sc("inactive_collect_ferry", "5B", ("pickup_multi_zone", "inactive_ferry_preloaded"),
         tuple(f"inactive/{r}" for r in _ROUTES), 90., _CYCLE, "repeat collect-and-ferry deliveries"),
     _sc("hub_transition_cycles", "6", ("active_collect_carry_score", "inactive_collect_ferry"),
-        ("active_to_inactive", "inactive_to_active"), 120., _CYCLE, "keep useful objectives across HUB switches"),
+        _TRANSITIONS, 120., _CYCLE, "keep useful objectives across HUB switches"),
     _sc("offense_vs_scripted_pressure", "7", ("hub_transition_cycles",), _PRESSURE, 120., _PRESS,
         "deliver useful FUEL under scripted defensive pressure"),
     _sc("team_delivery_cycles", "8", ("offense_vs_scripted_pressure",),
-        tuple(f"{r}/{t}" for r in _ROUTES for t in ("receiver", "multiple_teammates")), 150., _CYCLE,
-        "convert deliveries into team scoring"),
+        tuple(f"{c}/{t}" for c in _BOTH_ROUTES for t in ("receiver", "multiple_teammates", "opponents")), 150.,
+        _CYCLE, "convert deliveries into team scoring"),
     _sc("full_match_offense", "9", ("team_delivery_cycles", "offense_vs_scripted_pressure", "hub_transition_cycles"),
         _PRESSURE, 160., _PRESS, "contribute across the full match schedule"),
 )}
@@ -280,10 +299,12 @@ def task_mixture(state: CurriculumState, current_ids, next_ids=()) -> dict[str, 
 
 
 # ----------------------------------------------------------------------------- environment
-def _hub_phase_time(active: bool) -> float:
-    """Match-elapsed time (s) inside a teleop window where the red HUB is
-    active / inactive, with a few seconds before the next switch."""
-    return 30. if active else 55.
+def _hub_phase_time(active: bool, remaining: float = 24.) -> float:
+    """Match-elapsed time (s) at which the red HUB (slot 0's alliance) is
+    active / inactive with `remaining` seconds before it switches. With no
+    AUTO winner the red HUB is inactive in the first shift (30-55 s) and
+    active in the second (55-80 s)."""
+    return (80. if active else 55.) - remaining
 
 
 class CurriculumEnv:
@@ -299,12 +320,21 @@ class CurriculumEnv:
             raise ValueError(f"category {category!r} is not part of {scenario_id}")
         self.category = category
         modes = ["nn", "none", "none", "none", "none", "none"]
-        if scenario_id in ("offense_vs_scripted_pressure", "full_match_offense") and not category.endswith("level_0"):
-            modes[3] = "deterministic"
-            if "level_4" in category or scenario_id == "full_match_offense":
+        level = category.rsplit("/", 1)[-1]
+        if scenario_id in ("offense_vs_scripted_pressure", "full_match_offense"):
+            # parked robots (mode none) are static blockers; deterministic
+            # defense-role robots defend reactively
+            if level in ("level_2_patrol", "level_4_reactive", "level_5_mixed"):
+                modes[3] = "deterministic"
+            if level in ("level_4_reactive", "level_5_mixed") or (scenario_id == "full_match_offense"
+                                                                   and level != "level_0"):
                 modes[4] = "deterministic"
-        if scenario_id in ("team_delivery_cycles", "full_match_offense"):
+        if scenario_id == "full_match_offense" or category.endswith("/multiple_teammates"):
             modes[1] = modes[2] = "deterministic"
+        elif category.endswith("/receiver"):
+            modes[1] = "deterministic"
+        elif category.endswith("/opponents"):
+            modes[3] = modes[4] = "deterministic"
         self.env = TensorThreeVsThreeEnv(num_envs=num_envs, device=device, seed=seed, fuel_physics=fuel_physics,
                                          control_modes=tuple(modes), allow_nn_offense=True,
                                          horizon=int(self.scenario.time_budget_s / .02) + 1)
@@ -329,12 +359,39 @@ class CurriculumEnv:
         def rand(*shape):
             return torch.rand(shape, generator=g).to(self.device)
 
-        # robot 0 pose
+        parts = cat.split("/")
+        route = next((r for r in _ROUTES if r in parts), None)
+        # robot 0 pose: routes home through the open field, a trench or a bump
         x0 = depth + 1. + rand(n) * (L / 2 - depth - 2.)
         y0 = 1. + rand(n) * (W - 2.)
+        if route == "trench":
+            y0 = torch.where(rand(n) < .5, .6 + rand(n) * .5, W - 1.1 + rand(n) * .5)
+            x0 = depth + 1.8 + rand(n) * 2.
+        elif route == "bump":
+            y0 = torch.where(rand(n) < .5, 2.2 + rand(n) * .6, W - 2.8 + rand(n) * .6)
+            x0 = depth + 1.8 + rand(n) * 2.
+        elif route == "open":
+            y0 = W / 2 + (rand(n) * 2 - 1) * .6
         th0 = (rand(n) * 2 - 1) * math.pi
+        hub = env.hub_centers[0].to(self.device)
         if sid in ("active_shoot_preloaded",):
             x0 = depth + .4 + rand(n) * 1.5
+            if cat == "active/approach":
+                x0 = depth + 1.5 + rand(n) * 1.5
+            if cat == "active/heading_error":   # facing away from the HUB
+                th0 = torch.atan2(hub[1] - y0, hub[0] - x0) + math.pi + (rand(n) * 2 - 1) * .5
+        if sid == "inactive_ferry_preloaded":
+            x0 = {"inactive/approach": depth + 4. + rand(n) * 2., "inactive/landing": depth + .8 + rand(n) * .4
+                  }.get(cat, depth + 2. + rand(n) * 2.)
+            if cat == "inactive/alignment":     # facing away from home
+                th0 = rand(n) * .6 - .3
+        transition = sid == "hub_transition_cycles" and "/" in cat
+        if transition:
+            situation = parts[-1]
+            x0 = {"collecting": L / 2 - 1. + rand(n) * 1.5, "carrying_home": depth + 2. + rand(n) * 2.,
+                  "approaching_shot": depth + .6 + rand(n) * .8, "before_release": depth + 2.5 + rand(n) * 2.,
+                  "after_release": depth + 1.5 + rand(n) * 1.5, "staged_at_home": depth * .5 + rand(n) * 1.
+                  }[situation]
         pose = ws["r_pose"].clone()
         pose[:, 0, 0], pose[:, 0, 1], pose[:, 0, 2] = x0, y0, th0
         ws["r_pose"].copy_(torch.where(m[:, None, None], pose, ws["r_pose"]))
@@ -344,24 +401,45 @@ class CurriculumEnv:
         active = ws["f_active"].clone()
         owner = ws["f_owner"].clone()
         fx, fy = ws["f_pos"][:, 0].clone(), ws["f_pos"][:, 1].clone()
-        if sid.startswith("pickup") or sid in ("active_carry_to_zone",):
-            keep = {"single": 1, "cluster": 6, "sparse": 10, "dense": 30, "productive": 24, "depleted": 8}.get(cat, 12)
+        if sid.startswith("pickup") or sid in ("active_carry_to_zone",) or cat == "empty_collection":
+            keep = {"single": 1, "cluster": 6, "sparse": 10, "dense": 30, "initially_hidden": 8, "productive": 24,
+                    "empty": 16, "depleted": 8, "empty_collection": 12}.get(cat, 12)
             active.zero_()
             owner.fill_(-1)
             idx = torch.arange(keep)
-            if cat in ("single", "cluster", "dense"):  # around a point ahead of the robot
-                cx = (x0 + 1.5 * torch.cos(th0)).clamp(1., L - 1.)
-                cy = (y0 + 1.5 * torch.sin(th0)).clamp(1., W - 1.)
-                spread = .15 if cat != "dense" else .8
+            if cat in ("single", "cluster", "dense", "initially_hidden"):
+                # around a point ahead of the robot, or behind it (outside every camera's view)
+                ahead = -1.5 if cat == "initially_hidden" else 1.5
+                cx = (x0 + ahead * torch.cos(th0)).clamp(1., L - 1.)
+                cy = (y0 + ahead * torch.sin(th0)).clamp(1., W - 1.)
+                spread = {"dense": .8, "initially_hidden": .3}.get(cat, .15)
                 px = cx[:, None] + (rand(n, keep) * 2 - 1) * spread
                 py = cy[:, None] + (rand(n, keep) * 2 - 1) * spread
+            elif cat in ("empty", "empty_collection"):
+                # nothing within 3.5 m: the FUEL waits on the far side of the field
+                far_x = torch.where(x0 < L / 2, x0 + 4.5, x0 - 4.5).clamp(1., L - 1.)
+                px = far_x[:, None] + (rand(n, keep) * 2 - 1) * .8
+                py = (W - y0)[:, None] + (rand(n, keep) * 2 - 1) * .8
             else:
                 px = 1. + rand(n, keep) * (L - 2.)
                 py = .5 + rand(n, keep) * (W - 1.)
             fx[:, idx], fy[:, idx] = px.clamp(.1, L - .1), py.clamp(.1, W - .1)
             active[:, idx] = 1
+        load = 0
         if sid in ("active_shoot_preloaded", "inactive_ferry_preloaded", "active_carry_to_zone"):
-            load = 3 if cat.endswith("partial_load") else 5
+            load = 3 if cat.endswith("partial_load") else (8 if cat.endswith("full_load") else 5)
+        if transition:
+            load = {"empty": 0, "partial": 3, "full": 8}[parts[1]]
+            if parts[-1] == "staged_at_home":   # FUEL already staged in the home zone, robot empty
+                staged = torch.arange(P - 12, P - 4)
+                active[:, staged] = 1
+                owner[:, staged] = -1
+                fx[:, staged] = .3 + rand(n, 8) * (depth - .6)
+                fy[:, staged] = .5 + rand(n, 8) * (W - 1.)
+                load = 0
+        if cat == "hold_useful_load":
+            load = 5
+        if load:
             slots = torch.arange(P - load, P)
             active[:, slots] = 1
             owner[:, slots] = 0
@@ -373,13 +451,40 @@ class CurriculumEnv:
         ws["f_pos"].copy_(torch.where(m[:, None, None], fpos, ws["f_pos"]))
         ws["f_active"].copy_(torch.where(m[:, None], active, ws["f_active"]))
         ws["f_owner"].copy_(torch.where(m[:, None], owner, ws["f_owner"]))
+        # scripted blockers of the pressure scenarios: parked robots on the
+        # route home, in a trench, on a bump or at a seeded choice of those
+        level = parts[-1]
+        if level in ("level_1_stationary", "level_3_trench", "level_3_bump", "level_3_seeded_choice",
+                     "level_5_mixed"):
+            upper = y0 > W / 2
+            bx = torch.full((n,), 4.63, device=self.device)
+            by_trench = torch.where(upper, torch.full_like(y0, 7.24), torch.full_like(y0, .83))
+            by_bump = torch.where(upper, torch.full_like(y0, 5.56), torch.full_like(y0, 2.51))
+            if level == "level_3_trench":
+                by = by_trench
+            elif level == "level_3_bump":
+                by = by_bump
+            elif level == "level_3_seeded_choice":
+                by = torch.where(rand(n) < .5, by_trench, by_bump)
+            else:   # on the straight line home, halfway
+                bx, by = (x0 + depth) * .5, y0
+            slot = 5 if level == "level_5_mixed" else 3
+            bpose = ws["r_pose"].clone()
+            bpose[:, slot, 0], bpose[:, slot, 1], bpose[:, slot, 2] = bx, by, 0.
+            ws["r_pose"].copy_(torch.where(m[:, None, None], bpose, ws["r_pose"]))
+            for name in ("est_pose", "policy_pose"):
+                ws[name].copy_(torch.where(m[:, None, None], ws["r_pose"], ws[name]))
         # match clock / HUB phase
         hub_active = cat.startswith("active") or sid.startswith("active")
         if sid.startswith("inactive") or cat.startswith("inactive"):
             hub_active = False
         t = _hub_phase_time(hub_active)
         if sid == "hub_transition_cycles":
-            t = 48. if cat == "active_to_inactive" else 73.
+            if transition:    # now in the first phase, `timing` seconds before the switch
+                remaining = 12. if parts[2] == "enough_time" else 2.5
+                t = _hub_phase_time(parts[0] == "active_to_inactive", remaining)
+            else:
+                t = _hub_phase_time(cat == "empty_collection", 12.)
         if sid == "full_match_offense":
             t = 0.
         if not sid.startswith("pickup") or sid == "full_match_offense":

@@ -168,3 +168,36 @@ def test_entity_attention_packed_tokens_match_padded():
         assert (a - b_).abs().max().item() < 3e-2 * max(1., b_.abs().max().item())
     rel = (grads[0] - grads[1]).norm().item() / grads[1].norm().item()
     assert rel < 3e-2, rel
+
+
+@pytest.mark.gpu
+def test_varlen_query_attention_matches_fp32():
+    """One query per sample over variable-length packed keys / values
+    (forward and gradients) against fp32 softmax attention."""
+    from autodrive_b200.models.zoo import _VarlenQueryAttention
+    torch.manual_seed(9)
+    heads, dh = 4, 64
+    d = heads * dh
+    lens = torch.tensor([1, 7, 64, 130, 33, 250, 2, 90])
+    cu = torch.nn.functional.pad(lens.cumsum(0), (1, 0)).to(torch.int32).cuda()
+    total, b = int(lens.sum()), lens.numel()
+    q = (torch.randn(b, d, device="cuda") * .5).bfloat16().requires_grad_(True)
+    kv = (torch.randn(total, 2 * d, device="cuda") * .5).bfloat16().requires_grad_(True)
+    cu_q = torch.arange(b + 1, device="cuda", dtype=torch.int32)
+    out = _VarlenQueryAttention.apply(q, kv, heads, cu_q, cu, int(lens.max()))
+    qf, kvf = q.detach().float().requires_grad_(True), kv.detach().float().requires_grad_(True)
+    refs = []
+    for i in range(b):
+        s, e = int(cu[i]), int(cu[i + 1])
+        k = kvf[s:e, :d].view(-1, heads, dh).transpose(0, 1)
+        v = kvf[s:e, d:].view(-1, heads, dh).transpose(0, 1)
+        qq = qf[i].view(heads, 1, dh)
+        att = ((qq @ k.transpose(-1, -2)) / dh ** .5).softmax(-1)
+        refs.append((att @ v).reshape(d))
+    ref = torch.stack(refs)
+    assert (out.float() - ref).abs().max().item() < 3e-2
+    w = torch.randn_like(ref)
+    (out.float() * w).sum().backward()
+    (ref * w).sum().backward()
+    for a, r in ((q.grad, qf.grad), (kv.grad, kvf.grad)):
+        assert (a.float() - r).norm().item() / r.norm().item() < 3e-2
