@@ -101,8 +101,12 @@ def stages(args):
         phases = {n: round(c / crit, 4) for n, c in zip(names, cyc)}
     sim.sense_in_tick = True
     awake = (env.ws["f_active"].bool() & (env.ws["f_sleep"] == 0)).float().sum(-1).mean().item()
+    sweeps = env.ws["p_sweeps"].float()
+    planned = sweeps != 0
+    sweep_stats = {"mean": float(sweeps[planned].abs().mean()) if bool(planned.any()) else 0.,
+                   "max": float(sweeps.abs().max()), "not_converged": int((sweeps < 0).sum())}
     print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,
-                      "awake_fuel_per_world": awake, "phase_share": phases,
+                      "awake_fuel_per_world": awake, "planner_sweeps": sweep_stats, "phase_share": phases,
                       "sense_phase_share": sense_phases if args.phases else None,
                       "ms_per_tick": per_tick, "env_ticks_per_s": args.envs / (total / 1e3),
                       "threads": sim.threads}))
