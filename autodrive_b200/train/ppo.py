@@ -477,4 +477,7 @@ def checkpoint_payload(model, agents, architecture, network, action_kind, optimi
     # provenance: SHA-256 tree digest of the weights, computed where they live
     from ..utils.provenance import state_dict_digest
     payload["weights_sha256"] = state_dict_digest(payload["model_state_dict"])
+    from ..ops.ext import native_extension_identity
+    ident = native_extension_identity()
+    payload["native_extension"] = {k: ident.get(k) for k in ("sha256", "build_fingerprint", "sources_match_build")}
     return payload

@@ -23,12 +23,30 @@ ext = CUDAExtension(
     },
 )
 
+class BuildWithManifest(BuildExtension.with_options(use_ninja=True)):
+    """Build, then record the in-tree binary's digest and its sources'
+    digests in autodrive_b200/_C.manifest.json (checked at run time by
+    ``autodrive_b200.ops.ext.native_extension_identity``)."""
+
+    def run(self):
+        super().run()
+        import importlib.util
+        spec = importlib.util.spec_from_file_location(
+            "_ad_ext", os.path.join(HERE, "autodrive_b200", "ops", "ext.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        for e in self.extensions:
+            built = os.path.join(HERE, *e.name.split(".")[:-1], os.path.basename(self.get_ext_filename(e.name)))
+            if os.path.exists(built):
+                mod.write_build_manifest(built)
+
+
 setup(
     name="autodrive-b200",
     version="0.1.0",
     packages=find_packages(include=["autodrive_b200*", "frc_defense*"]),
     ext_modules=[ext],
-    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    cmdclass={"build_ext": BuildWithManifest},
     entry_points={"console_scripts": [
         "frc-defense=frc_defense.tensor_training:main",
         "frc-defense-tensor=frc_defense.tensor_training:main",

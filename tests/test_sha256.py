@@ -42,3 +42,15 @@ def test_gpu_matches_host():
     assert tensor_digest(t.cuda(), 1000) == tensor_digest(t, 1000) == _tree(bytes(t.tolist()), 1000)
     w = torch.randn(1000, 137)
     assert tensor_digest(w.cuda()) == tensor_digest(w)
+
+
+def test_native_extension_identity():
+    """The loaded extension is the in-tree file mapped into this process, and
+    (once built with its manifest) matches the manifest and current sources."""
+    from autodrive_b200.ops.ext import build_fingerprint, native_extension_identity, source_digests
+    ident = native_extension_identity()
+    assert ident["mapped"] in (True, None) and len(ident["sha256"]) == 64
+    assert ident["path"].endswith(".so")
+    assert "sim.cu" in source_digests() and len(build_fingerprint()) == 64
+    if ident["manifest_binary_match"] is not None:
+        assert ident["manifest_binary_match"]
