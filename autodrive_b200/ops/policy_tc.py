@@ -134,13 +134,27 @@ class TensorCorePolicy:
             self._partials = torch.empty((nblk, self.pstride), device=self.device)
         return self._partials
 
+    def minibatch_adv_stats(self, adv: torch.Tensor, batches) -> torch.Tensor:
+        """Local (sum, sum of squares, count) of the advantages of every
+        minibatch in `batches`, one row each (float64 [len(batches), 3])."""
+        out = torch.empty((len(batches), 3), dtype=torch.float64, device=adv.device)
+        for k, idx in enumerate(batches):
+            self.ext.policy_adv_stats(adv, idx, int(idx.numel()), out[k])
+        return out
+
     def train_minibatch(self, batch: dict, idx: torch.Tensor, ent_coef: torch.Tensor, clip: float,
-                        value_coef: float, l2_coef: float, loss_stats: torch.Tensor, all_reduce=None) -> None:
-        """Write the minibatch's PPO gradient into ``flat.grad`` (overwrites it)."""
+                        value_coef: float, l2_coef: float, loss_stats: torch.Tensor, all_reduce=None,
+                        adv_stats: torch.Tensor | None = None) -> None:
+        """Write the minibatch's PPO gradient into ``flat.grad`` (overwrites
+        it). `adv_stats` supplies the minibatch's already reduced advantage
+        statistics; otherwise they are computed (and all-reduced) here."""
         b = int(idx.numel())
-        self.ext.policy_adv_stats(batch["adv"], idx, b, self.adv_stats)
-        if all_reduce is not None:
-            all_reduce(self.adv_stats)
+        if adv_stats is not None:
+            self.adv_stats.copy_(adv_stats)
+        else:
+            self.ext.policy_adv_stats(batch["adv"], idx, b, self.adv_stats)
+            if all_reduce is not None:
+                all_reduce(self.adv_stats)
         part = self.partials(b)
         self.ext.policy_train(batch["obs"], idx, self.action_dim, self.images, self.flat.flat, self.offsets,
                               batch["actions"], batch.get("mask"), batch["logp"], batch["adv"], batch["returns"],

@@ -233,20 +233,30 @@ class PPOLearner:
             ent = torch.full((1,), float(entropy_coef), device=self.device)
         stats = self._loss_stats
         stats.zero_()
-        reduce = None
+        # every minibatch of the update is drawn up front, so the advantage
+        # statistics of all of them cross the ranks in one exchange instead of
+        # one synchronising all-reduce per minibatch
+        plan = [idx for _ in range(cfg.epochs) for idx in torch.randperm(n, device=self.device).split(mb)]
+        adv_stats = tc.minibatch_adv_stats(batch["adv"], plan)
         if self.world > 1:
             fused = getattr(self.sync, "fused", None)
-            reduce = fused.stats_allreduce if fused is not None else pdist.all_reduce_
+            flat_stats = adv_stats.view(-1)
+            if fused is not None:
+                for k in range(0, flat_stats.numel(), 15):   # the peer stats kernel carries <= 16 values
+                    chunk = flat_stats[k:k + 15].clone()
+                    fused.stats_allreduce(chunk)
+                    flat_stats[k:k + 15].copy_(chunk)
+            else:
+                pdist.all_reduce_(flat_stats)
         samples, batches = 0, 0
-        for _ in range(cfg.epochs):
-            perm = torch.randperm(n, device=self.device)
-            for idx in perm.split(mb):
-                tc.train_minibatch(batch, idx, ent, cfg.clip_coef, cfg.value_coef, cfg.l2_coef, stats, reduce)
-                self.sync.step()
-                self.weights_version += 1
-                tc.pack(self.weights_version)
-                samples += int(idx.numel())
-                batches += 1
+        for k, idx in enumerate(plan):
+            tc.train_minibatch(batch, idx, ent, cfg.clip_coef, cfg.value_coef, cfg.l2_coef, stats,
+                               adv_stats=adv_stats[k])
+            self.sync.step()
+            self.weights_version += 1
+            tc.pack(self.weights_version)
+            samples += int(idx.numel())
+            batches += 1
         tc._post_status()
         return {"approx_kl_sum": stats[0], "clip_fraction_sum": stats[1], "entropy_sum": stats[2],
                 "policy_loss_sum": stats[3], "value_loss_sum": stats[4], "samples": samples, "batches": batches}
