@@ -79,7 +79,7 @@ SimParams params_from_dict(const py::dict& d) {
   I(grid_cell) I(grid_nx) I(grid_ny) I(colored_solver) I(fuel_radius_rules) I(two_robot_schedule) I(counter_defense)
   I(perception_interval) I(opponent_kind) I(perception_range) I(perception_fov) I(perception_dropout) I(position_noise)
   I(velocity_noise) I(track_timeout) I(ball_diameter) I(stereo_baseline) I(stereo_tracks) I(sweeping) I(raster_lookahead) I(replan_interval)
-  I(teammate_coordination) I(normalize_obs) I(horizon) I(max_speed_nominal) I(max_omega_nominal)
+  I(teammate_coordination) I(normalize_obs) I(horizon) I(checks) I(max_speed_nominal) I(max_omega_nominal)
   I(plan_res) I(plan_nx) I(plan_ny) I(plan_sweeps) I(bump_cost) I(seed0) I(seed1)
 #undef I
   p.Q = p.R * (p.R - 1) / 2;

@@ -173,12 +173,82 @@ AD_HD void store_fuel(const TickShared& s, World& w, const SimParams& sp, int e)
   }
 }
 
+// State validation (option `checks`): before a tick uses the world state,
+// invalid entries are recorded as bits of the environment's status word
+// e_status and made harmless, so a corrupted state is reported instead of
+// being indexed with or propagated:
+//   1  a FUEL owner outside [-1, robots)     -> owner cleared (free piece)
+//   2  a non-finite FUEL position / velocity / spin -> piece deactivated
+//   4  an active FUEL piece more than 1 m outside the field or above 20 m -> deactivated
+//   8  a non-finite robot pose / velocity / command -> velocity and command
+//      zeroed, a non-finite pose replaced by the field centre
+constexpr int kStatusOwner = 1, kStatusFuelNonFinite = 2, kStatusFuelEscaped = 4, kStatusRobotNonFinite = 8;
+
+AD_HD bool bad_float(float v) { return (float_bits(v) & 0x7f800000u) == 0x7f800000u; }
+
+AD_HD void validate_state(World& w, const SimParams& sp, int e) {
+  int bits = 0;
+  const size_t b3 = (size_t)e * 3 * sp.P, b1 = (size_t)e * sp.P;
+  PAR_FOR(i, sp.P) {
+    const int o = w.f_owner[b1 + i];
+    if (o < -1 || o >= sp.R) {
+      w.f_owner[b1 + i] = -1;
+      bits |= kStatusOwner;
+    }
+    if (!w.f_active[b1 + i]) continue;
+    bool finite = true;
+    for (int k = 0; k < 3; ++k) {
+      const size_t j = b3 + (size_t)k * sp.P + i;
+      finite = finite && !bad_float(w.f_pos[j]) && !bad_float(w.f_vel[j]) && !bad_float(w.f_ang[j]);
+    }
+    if (!finite) {
+      w.f_active[b1 + i] = 0;
+      w.f_owner[b1 + i] = -1;
+      bits |= kStatusFuelNonFinite;
+      continue;
+    }
+    const float x = w.f_pos[b3 + i], y = w.f_pos[b3 + sp.P + i], z = w.f_pos[b3 + 2 * sp.P + i];
+    if (x < -1.f || x > sp.field_length + 1.f || y < -1.f || y > sp.field_width + 1.f || z < -1.f || z > 20.f) {
+      w.f_active[b1 + i] = 0;
+      w.f_owner[b1 + i] = -1;
+      bits |= kStatusFuelEscaped;
+    }
+  }
+  PAR_FOR(r, sp.R) {
+    const size_t b = ((size_t)e * sp.R + r) * 3;
+    bool bad_pose = false, bad_motion = false;
+    for (int k = 0; k < 3; ++k) {
+      bad_pose = bad_pose || bad_float(w.r_pose[b + k]);
+      bad_motion = bad_motion || bad_float(w.r_vel[b + k]) || bad_float(w.c_command[b + k]);
+    }
+    if (bad_pose || bad_motion) {
+      for (int k = 0; k < 3; ++k) {
+        w.r_vel[b + k] = 0.f;
+        w.c_command[b + k] = 0.f;
+      }
+      if (bad_pose) {
+        w.r_pose[b] = .5f * sp.field_length;
+        w.r_pose[b + 1] = .5f * sp.field_width;
+        w.r_pose[b + 2] = 0.f;
+      }
+      bits |= kStatusRobotNonFinite;
+    }
+  }
+#if defined(__CUDA_ARCH__)
+  if (bits) atomicOr(&w.e_status[e], bits);
+  __syncthreads();
+#else
+  w.e_status[e] |= bits;
+#endif
+}
+
 // Full controller tick for environment e (after control / plan stages).
 AD_HD void tick_env(World& w, const SimParams& sp, TickShared& s, int e, uint32_t tick, int32_t* poss,
                     int run_game) {
   G g{w, sp, e};
   const Rng rng{sp.seed0, sp.seed1};
   (void)tick;
+  if (sp.checks) validate_state(w, sp, e);
   if (run_game) {
     count_possession(w, sp, e, poss);
     SERIAL_BEGIN

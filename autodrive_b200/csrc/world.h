@@ -133,6 +133,7 @@ enum DType : int { DT_F32 = 0, DT_I32 = 1, DT_U8 = 2, DT_I8 = 3, DT_F64 = 4 };
   X(p_sweeps, int32_t, DT_I32, 2, N, R, 1, 1)                           \
   X(obs, float, DT_F32, 3, N, R, O, 1)                                  \
   X(e_episode, int32_t, DT_I32, 1, N, 1, 1, 1)                         \
+  X(e_status, int32_t, DT_I32, 1, N, 1, 1, 1)                          \
   X(active, uint8_t, DT_U8, 1, N, 1, 1, 1)
 
 struct World {
@@ -200,6 +201,7 @@ struct SimParams {
   int teammate_coordination = 0;
   int normalize_obs = 1;
   int horizon = 8000;
+  int checks = 0;               // 1: validate and sanitise the world state every tick (status word e_status)
   float max_speed_nominal = 9.6f, max_omega_nominal = 16.f;
   // planner grid
   float plan_res = .3f;

@@ -21,7 +21,8 @@ import torch
 from .. import field as fieldmod
 from ..utils import trace
 from .robots import RobotView, hub_line_spawn_poses
-from .world import FuelPhysicsConfig, SwerveParameters, WorldState, build_params, fuel_config
+from .world import (FuelPhysicsConfig, SwerveParameters, WorldState, build_params, check_state,
+                    fuel_config, state_checks_default)
 
 NUM_ROBOTS = 6
 OBS_DIM = 137
@@ -74,7 +75,7 @@ class TensorThreeVsThreeEnv:
                  behavior_probe_hub_active=True, random_gamepiece_placement=False,
                  field_length=16.54, field_width=8.07, obstacles=(), fuel_physics=True,
                  field_layout="2026_rebuilt", defer_initial_perception=False,
-                 planner_resolution=.3, planner_sweeps=None, swerve=None):
+                 planner_resolution=.3, planner_sweeps=None, swerve=None, state_checks=None):
         self.n = int(num_envs)
         if self.n < 1:
             raise ValueError("num_envs must be positive")
@@ -175,6 +176,7 @@ class TensorThreeVsThreeEnv:
             teammate_coordination=int(self.teammate_coordination_enabled),
             normalize_obs=int(self.normalize_observations), horizon=self.horizon,
             plan_res=float(planner_resolution), plan_nx=plan_nx, plan_ny=plan_ny,
+            checks=int(state_checks_default() if state_checks is None else bool(state_checks)),
             # directional line sweeps; the iteration stops at the first sweep
             # that changes no cell, so the budget only bounds pathological grids
             plan_sweeps=int(planner_sweeps if planner_sweeps is not None else 4 * (plan_nx + plan_ny)),
@@ -566,6 +568,12 @@ class TensorThreeVsThreeEnv:
             self.ws.sim.observe()
             self.ws["active"].copy_(saved)
         return self.ws["obs"]
+
+    def check_state(self, raise_error: bool = True) -> dict:
+        """Status words of the per-tick state validation (constructor option
+        `state_checks`, or AUTODRIVE_STATE_CHECKS=1): decoded, cleared, and
+        raised as SimulationStateError when an environment reported one."""
+        return check_state(self.ws, raise_error=raise_error)
 
     def action_mask(self) -> torch.Tensor:
         """Legal strategic actions per robot (last 8 observation features)."""

@@ -57,7 +57,7 @@ import torch
 from .. import field as fieldmod
 from .env3v3 import FuelView, PlannerView, _INF
 from .robots import RobotView
-from .world import SwerveParameters, WorldState, build_params, fuel_config
+from .world import SwerveParameters, WorldState, build_params, check_state, fuel_config, state_checks_default
 
 OPPONENT_KINDS = {"offense": 0, "adstar": 0, "guard": 0, "pursuit": 0, "mirror": 1, "cutoff": 2,
                   "velocity_intercept": 3, "random": 4}
@@ -167,6 +167,7 @@ class TensorDefenseEnv:
             raise ValueError("observation_noise must be >= 0 and observation_dropout in [0, 1)")
         self.adstar_spawn_hint = bool(kwargs.pop("adstar_spawn_hint", True))
         self.base_goal_radius = float(kwargs.pop("goal_radius", .5))
+        state_checks = kwargs.pop("state_checks", None)
         # reference options that only select among equivalent implementations
         # of the same computation (candidate reuse, squared distances, skipping
         # a metric-only objective) change nothing here
@@ -189,7 +190,8 @@ class TensorDefenseEnv:
             field_width=field_width, boxes=[b.as_tensor() for b in solids],
             bumps=[b.as_tensor() for b in bumps], hubs=hubs, team=(0, 1), mode=(learner_mode, 2),
             role=(0, 1) if task == "counter_defense" else (1, 0), kind=(0, 0),
-            counter_defense=1 if task == "counter_defense" else 0, capacity=(self.fuel_capacity, self.fuel_capacity),
+            counter_defense=1 if task == "counter_defense" else 0,
+            checks=int(state_checks_default() if state_checks is None else bool(state_checks)), capacity=(self.fuel_capacity, self.fuel_capacity),
             score_interval=(self.score_interval, self.score_interval), fuel=self.fuel_config,
             swerve=swerve, base_speed=base["speed"], base_omega=base["omega"], seed=int(seed or 0),
             two_robot_schedule=1, opponent_kind=opponent_code, perception_range=self.perception_range,
@@ -480,6 +482,10 @@ class TensorDefenseEnv:
         if not full:
             self.ws["active"].fill_(1)
         return self._last_observation, reward, terminated, truncated, info
+
+    def check_state(self, raise_error: bool = True) -> dict:
+        """Decoded status words of the per-tick state validation (option `state_checks`)."""
+        return check_state(self.ws, raise_error=raise_error)
 
     def strategic_action_mask(self) -> torch.Tensor:
         return self._last_observation[:, -8:] > .5 if self.action_mode == "strategic" else None

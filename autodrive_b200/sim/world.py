@@ -201,6 +201,38 @@ def build_params(*, n: int, robots: int, pieces: int, dt: float, field_length: f
     return p
 
 
+STATUS_BITS = {1: "FUEL owner outside [-1, robots) cleared", 2: "non-finite FUEL state (piece deactivated)",
+               4: "FUEL outside the field (piece deactivated)",
+               8: "non-finite robot pose / velocity / command (zeroed)"}
+
+
+class SimulationStateError(RuntimeError):
+    """The state validation of the simulator kernels found invalid entries."""
+
+
+def state_checks_default() -> bool:
+    import os
+    return os.environ.get("AUTODRIVE_STATE_CHECKS", "0") == "1"
+
+
+def check_state(ws: "WorldState", clear: bool = True, raise_error: bool = True) -> dict:
+    """Read the per-environment status words of the state validation (the
+    `state_checks` environment option), decode them and clear them; raises
+    SimulationStateError when any environment reported a problem."""
+    words = ws["e_status"].reshape(-1)
+    hit = (words != 0).nonzero().reshape(-1).tolist()
+    report = {"environments": hit, "problems": {}}
+    for e in hit:
+        w = int(words[e])
+        report["problems"][e] = [msg for bit, msg in STATUS_BITS.items() if w & bit]
+    if clear:
+        words.zero_()
+    if hit and raise_error:
+        raise SimulationStateError(f"invalid simulator state in {len(hit)} environment(s): "
+                                   f"{dict(list(report['problems'].items())[:4])}")
+    return report
+
+
 class WorldState:
     """All state tensors of a batch of environments plus the native handle."""
 
