@@ -328,10 +328,19 @@ def train_meco(config: MecoConfig, ledger: MetricLedger | None = None) -> tuple[
 
 
 # --------------------------------------------------------------------------- evaluation
+ABLATIONS = ("full", "no_penalty", "no_memory", "uniform_utility")
+
+
 def evaluate_meco(policy: MecoPolicy | None, scenario: str, *, episodes: int, split: str = "validation",
-                  master_seed: int = 0, device="cpu", max_age_s: float = .25) -> dict:
+                  master_seed: int = 0, device="cpu", max_age_s: float = .25, ablation: str = "full") -> dict:
     """Matched-seed evaluation of the track (through the fail-closed arbiter)
-    and of the scripted teacher on the same seeds."""
+    and of the scripted teacher on the same seeds. `ablation` removes one
+    part of the scorer at decision time: ``no_penalty`` (risk penalties
+    zeroed), ``no_memory`` (recurrent state reset every decision),
+    ``uniform_utility`` (every valid candidate scored alike, so the arbiter's
+    tie order decides). Per-episode outcomes are kept for paired tests."""
+    if ablation not in ABLATIONS:
+        raise ValueError(f"ablation must be one of {ABLATIONS}")
     sc = get_scenario(scenario)
     seeds = seed_partition(scenario, split, len(sc.required_categories))
     teacher = D2PredictivePolicy()
@@ -350,7 +359,11 @@ def evaluate_meco(policy: MecoPolicy | None, scenario: str, *, episodes: int, sp
                 fallback = teacher.choose(cenv)
                 if arm == "meco":
                     with torch.no_grad():
-                        util, pen, valid, _, hidden = policy(cenv.env, hidden)
+                        util, pen, valid, _, hidden = policy(cenv.env, None if ablation == "no_memory" else hidden)
+                    if ablation == "no_penalty":
+                        pen = torch.zeros_like(pen)
+                    elif ablation == "uniform_utility":
+                        util = torch.zeros_like(util)
                     ids = tuple(f"action-{k}" for k in range(ACTIONS))
                     now = float(cenv.elapsed) * cenv.env.dt
                     choice = []
@@ -367,6 +380,7 @@ def evaluate_meco(policy: MecoPolicy | None, scenario: str, *, episodes: int, sp
                 _, _, done = cenv.step(act)
             ok = episode_success(scenario, cat, cenv.metrics.counts(), cenv)
             row[arm] = int(ok.sum())
+            row[f"{arm}_episodes"] = [bool(v) for v in ok.tolist()]
             totals[arm][0] += int(ok.sum())
             totals[arm][1] += cenv.n
         out["categories"].append(row)
@@ -374,6 +388,7 @@ def evaluate_meco(policy: MecoPolicy | None, scenario: str, *, episodes: int, sp
         if n:
             out[arm] = {"success_rate": s / n, "wilson_95": wilson_interval(s, n), "episodes": n}
     out["arbiter"] = fallbacks
+    out["ablation"] = ablation
     return out
 
 
