@@ -8,10 +8,11 @@ randomized drivetrains, fuel physics on, replanning every 20 ticks,
 perception every 2nd tick, action 7 for every robot), and records every
 world's alliance scores and per-robot FUEL acquisitions at fixed checkpoints.
 
-    python -m autodrive_b200.bench.match_outcomes --impl ours --seeds 827104 827105 191873 \
+    python -m autodrive_b200.bench.match_outcomes run --impl ours --seeds 827104 827105 191873 \
         --envs 12 --ticks 8000 --output outcomes.json
-    python -m autodrive_b200.bench.match_outcomes --impl reference --device cpu --seeds 827104 \
+    python -m autodrive_b200.bench.match_outcomes run --impl reference --device cpu --seeds 827104 \
         --envs 4 --ticks 8000 --output ref.json
+    python -m autodrive_b200.bench.match_outcomes summarize outcomes.json ref.json
 
 `--impl reference` imports the unmodified reference package installed in
 ``baseline/_ref`` and drives it through its public ``TensorThreeVsThreeEnv``
