@@ -86,9 +86,12 @@ __device__ bool cross_rank_barrier(const Ptrs& P, int world, int rank, int slot,
 // out[4k..4k+3] = (1/W) sum over ranks of grad_q[base + 4k..], k in [0, nvec);
 // returns this thread's sum of squares of the written values. Every thread
 // issues kUnroll independent 16-byte loads per rank before using any, so
-// enough remote bytes are in flight to cover the NVLink round trip.
+// enough remote bytes are in flight to cover the NVLink round trip. Ranks are
+// visited starting at `first` (the two-shot owner starts at its next peer so
+// the W owners do not all read rank 0 first); the one-shot path passes 0 so
+// every rank sums in the same order and the replicas stay bitwise equal.
 __device__ __forceinline__ float reduce_range(const Ptrs& P, int world, float* __restrict__ out, int64_t base,
-                                              int64_t nvec, float inv_w) {
+                                              int64_t nvec, float inv_w, int first) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   float acc = 0.f;
   for (int64_t k0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k0 < nvec; k0 += kUnroll * stride) {
@@ -96,8 +99,9 @@ __device__ __forceinline__ float reduce_range(const Ptrs& P, int world, float* _
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q) {
-      if (q >= world) break;
+    for (int j = 0; j < kMaxRanks; ++j) {
+      if (j >= world) break;
+      const int q = first + j < world ? first + j : first + j - world;
       float4 x[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) fused_allreduce_adam_kernel(
   // phase 1: reduce-scatter the owned shard, sum of squares
   float acc = 0.f;
   const float inv_w = 1.f / (float)world;
-  if (healthy) acc = reduce_range(P, world, P.grad[rank] + lo, lo, shard / 4, inv_w);
+  if (healthy) acc = reduce_range(P, world, P.grad[rank] + lo, lo, shard / 4, inv_w, rank + 1 < world ? rank + 1 : 0);
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
@@ -193,7 +197,10 @@ __global__ void __launch_bounds__(kThreads) fused_allreduce_adam_kernel(
       }
       *reinterpret_cast<float4*>(m + i) = mm;
       *reinterpret_cast<float4*>(v + i) = vv;
-      for (int q = 0; q < world; ++q) *reinterpret_cast<float4*>(P.param[q] + i) = p;
+      for (int j = 1; j <= world; ++j) {   // peers from the next rank on, own buffer last
+        const int q = rank + j < world ? rank + j : rank + j - world;
+        *reinterpret_cast<float4*>(P.param[q] + i) = p;
+      }
     }
   }
   __threadfence_system();
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(kThreads) oneshot_allreduce_adam_kernel(
   const float inv_w = 1.f / (float)world;
   const int64_t nvec = n_padded / 4;
   float acc = 0.f;
-  if (healthy) acc = reduce_range(P, world, scratch, 0, nvec, inv_w);
+  if (healthy) acc = reduce_range(P, world, scratch, 0, nvec, inv_w, 0);
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
   __syncthreads();
