@@ -192,6 +192,7 @@ void register_policy_ops(py::module& m);
 void register_comm_ops(py::module& m);
 void register_policy_tc_ops(py::module& m);
 void register_tc_gemm_ops(py::module& m);
+void register_attention_ops(py::module& m);
 void register_layernorm_ops(py::module& m);
 void register_adstar_cpu(py::module& m);
 void register_sha256_ops(py::module& m);
@@ -248,6 +249,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_comm_ops(m);
   register_policy_tc_ops(m);
   register_tc_gemm_ops(m);
+  register_attention_ops(m);
   register_layernorm_ops(m);
   register_adstar_cpu(m);
   register_sha256_ops(m);

@@ -30,7 +30,9 @@ Module attribute names follow the reference networks (``trunk``, ``actor``,
 ``critic``, ``field_encoder``, ``scalar_encoder``, ``fusion``, ``blocks``;
 attention keeps ``in_proj_weight`` / ``out_proj``), so their state dicts line
 up. On CUDA every ``nn.Linear`` and the attention projections run on the
-tcgen05 GEMM (``ops.tc_linear``) when ``tensor_cores=True``.
+tcgen05 GEMM (``ops.tc_linear``) when ``tensor_cores=True``, and so does the
+variable-length self-attention of the packed entity tokens
+(``ops.attention``, head dim 64).
 """
 from __future__ import annotations
 
@@ -40,6 +42,7 @@ from torch.nn import functional as F
 
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
+from ..ops.attention import supported as _tc_attention_supported, varlen_attention
 from ..ops.layernorm import FusedLayerNorm
 from ..ops.tc_linear import _TcLinearFn, tensorize
 
@@ -353,6 +356,8 @@ class SelfAttention(nn.Module):
         """Attention within each sample of packed valid tokens x [total, d]
         (sample i at rows cu[i]:cu[i+1]); CUDA, bf16 / fp16 projections."""
         qkv = _linear(x, self.in_proj_weight, self.in_proj_bias, self.tensor_cores)
+        if self.tensor_cores and _tc_attention_supported(qkv, self.heads):
+            return self.out_proj(varlen_attention(qkv, cu, max_len, self.heads))
         return self.out_proj(_PackedAttention.apply(qkv, None, self.heads, cu, max_len))
 
     def forward_packed_query(self, x: Tensor, cu: Tensor, max_len: int, rows: Tensor) -> Tensor:

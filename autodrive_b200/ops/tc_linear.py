@@ -57,7 +57,8 @@ class TensorCoreTimeout(RuntimeError):
 
 
 _PHASES = ((1, "producer: stage free"), (2, "MMA: stage loaded"), (4, "epilogue: accumulator full"),
-           (8, "MMA: accumulator free"), (16, "drain of in-flight loads"), (32, "drain of in-flight MMAs"))
+           (8, "MMA: accumulator free"), (16, "drain of in-flight loads"), (32, "drain of in-flight MMAs"),
+           (64, "attention forward MMA"), (128, "attention backward MMA"), (256, "attention drain of in-flight MMAs"))
 
 
 def _describe(word: int) -> str:

@@ -11,7 +11,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 ext = CUDAExtension(
     name="autodrive_b200._C",
     sources=[os.path.join(CSRC, f) for f in (
-        "bindings.cpp", "adstar_cpu.cpp", "sim.cu", "policy_ops.cu", "policy_tc.cu", "tc_gemm.cu", "comm_ops.cu", "noalloc_adam.cu", "sha256.cu", "plan_a.cu", "layernorm.cu")],
+        "bindings.cpp", "adstar_cpu.cpp", "sim.cu", "policy_ops.cu", "policy_tc.cu", "tc_gemm.cu", "comm_ops.cu", "noalloc_adam.cu", "sha256.cu", "plan_a.cu", "layernorm.cu", "attention.cu")],
     include_dirs=[os.path.join(HERE, CSRC)],
     extra_compile_args={
         "cxx": ["-O3", "-std=c++17"],
