@@ -46,6 +46,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "tc_sm100.h"
@@ -69,23 +70,30 @@ constexpr uint32_t kFwdQ = 0, kFwdK = kImg64, kFwdV = 3 * kImg64, kFwdP = 4 * kI
 constexpr uint32_t kFwdSmem = kFwdMisc + 128 + 1024;
 // backward: Q ring (2) | dO ring (2) | K ring (2) | V ring (2) | P | dS | barriers
 constexpr uint32_t kBwdQ = 0, kBwdDO = 2 * kImg64, kBwdK = 4 * kImg64, kBwdV = 6 * kImg64, kBwdP = 8 * kImg64,
-                   kBwdDS = kBwdP + kImg128, kBwdMisc = kBwdDS + kImg128;
+                   kBwdDS = kBwdP + kImg128, kBwdStats = kBwdDS + kImg128;
+constexpr int kStatRows = 1024;                 // rows whose log-sum-exp and D stay in shared memory
+constexpr uint32_t kBwdMisc = kBwdStats + 2 * kStatRows * 4;
 constexpr uint32_t kBwdSmem = kBwdMisc + 128 + 1024;
 
 struct AttnArgs {
-  const __nv_bfloat16* qkv;   // [total, ld]
-  int64_t ld;                 // 3 * heads * 64
-  const int* cu;              // [samples + 1]
+  const int* cu_q;            // [samples + 1]: query rows of each sample
+  const int* cu_k;            // [samples + 1]: key / value rows of each sample
+  int q_col, k_col, v_col;    // column of head 0's queries / keys / values in their sources
   int heads;
-  int64_t total;
+  int64_t total_q;            // query rows (rows of out, dout, lse)
   float scale_log2;           // softmax scale * log2(e)
   float scale;                // softmax scale
-  __nv_bfloat16* out;         // [total, heads * 64]
-  float* lse;                 // [heads, total]: base-2 log-sum-exp of the scaled scores
-  const __nv_bfloat16* dout;  // [total, heads * 64]
-  __nv_bfloat16* dqkv;        // [total, ld]
-  float* dq_acc;              // [total, heads * 64] fp32 (samples longer than one block)
-  float* dvec;                // [heads, total] fp32: rowsum(dO * O)
+  __nv_bfloat16* out;         // [total_q, heads * 64]
+  float* lse;                 // [heads, total_q]: base-2 log-sum-exp of the scaled scores
+  const __nv_bfloat16* dout;  // [total_q, heads * 64]
+  __nv_bfloat16* dq;          // query gradient rows (stride ldq), head 0 at column dq_col
+  int64_t ldq;
+  int dq_col;
+  __nv_bfloat16* dkv;         // key / value gradient rows (stride ldkv)
+  int64_t ldkv;
+  int dk_col, dv_col;
+  float* dq_acc;              // [total_q, heads * 64] fp32 (samples with several key blocks)
+  float* dvec;                // [heads, total_q] fp32: rowsum(dO * O)
   int* status;
   uint64_t wait_ns;
 };
@@ -130,26 +138,37 @@ __device__ __forceinline__ bool wait_or_fail(uint32_t bar, uint32_t parity, cons
   }
 }
 
-// After a failure: let the MMAs and TMA loads this thread issued finish
-// (bounded) before the CTA frees TMEM and exits.
-__device__ __forceinline__ void drain_after_failure(uint32_t drain_bar, const uint32_t* bars, const uint32_t* issued,
-                                                    const uint32_t* consumed, int nbars, const AttnArgs& a) {
+// After a failure: let the MMAs and TMA loads of this thread finish
+// (bounded) before the CTA frees TMEM and exits. The load barriers are
+// consecutive mbarriers from `bar0`; bit i of `pending` marks a load on
+// barrier i not yet waited for, bit i of `parity` that barrier's phase parity.
+__device__ __forceinline__ void drain_after_failure(uint32_t drain_bar, uint32_t bar0, uint32_t pending,
+                                                    uint32_t parity, int nbars, const AttnArgs& a) {
   tc::mma_commit(drain_bar);
   if (!tc::mbar_wait(drain_bar, 0, kDrainNs)) atomicOr(a.status, kBitDrain);
   for (int i = 0; i < nbars; ++i)
-    for (uint32_t k = consumed[i]; k < issued[i]; ++k)
-      if (!tc::mbar_wait(bars[i], k & 1u, kDrainNs)) atomicOr(a.status, kBitDrain);
+    if ((pending >> i) & 1u)
+      if (!tc::mbar_wait(bar0 + 8u * i, (parity >> i) & 1u, kDrainNs)) atomicOr(a.status, kBitDrain);
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
-attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, int nqb) {
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv, const AttnArgs a,
+                int nqb) {
   const int qb = blockIdx.x % nqb;
   const int h = (blockIdx.x / nqb) % a.heads;
   const int seq = blockIdx.x / (nqb * a.heads);
-  const int s0 = a.cu[seq];
-  const int L = a.cu[seq + 1] - s0;
+  const int sq0 = a.cu_q[seq], Lq = a.cu_q[seq + 1] - sq0;
+  const int sk0 = a.cu_k[seq], Lk = a.cu_k[seq + 1] - sk0;
   const int q0 = qb * kBlk;
-  if (q0 >= L) return;   // whole CTA, before any barrier or TMEM allocation
+  if (q0 >= Lq) return;   // whole CTA, before any barrier or TMEM allocation
+  if (Lk <= 0) {          // no keys: zero output rows
+    for (int i = threadIdx.x; i < min(kBlk, Lq - q0) * 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(a.out + (int64_t)(sq0 + q0 + (i >> 3)) * (a.heads * kDh) + h * kDh)[i & 7] =
+          make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < min(kBlk, Lq - q0); i += blockDim.x)
+      a.lse[(int64_t)h * a.total_q + sq0 + q0 + i] = -INFINITY;
+    return;
+  }
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -165,7 +184,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 64);
   int* s_fail = reinterpret_cast<int*>(misc + 72);
   const int t = threadIdx.x, warp = t >> 5;
-  const int nkb = (L + kBlk - 1) / kBlk;
+  const int nkb = (Lk + kBlk - 1) / kBlk;
 
   if (t == kCompute) {
     tc::mbar_init(bar_k0, 1);
@@ -189,25 +208,26 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
 
   if (t == kCompute) {
     // ---- control: TMA loads and MMA issue ----
-    const int xq = h * kDh, xk = (a.heads + h) * kDh, xv = (2 * a.heads + h) * kDh;
-    uint32_t bars[3] = {bar_k0, bar_k1, bar_v}, issued[3] = {0, 0, 0}, consumed[3] = {0, 0, 0};
+    const int xq = a.q_col + h * kDh, xk = a.k_col + h * kDh, xv = a.v_col + h * kDh;
+    uint32_t pending = 0, parity = 0;   // loads in flight per barrier (k0, k1, v), phase parities
     tc::mbar_arrive_expect_tx(bar_k0, 2 * kImg64);
-    tc::tma_load_2d(sb + kFwdQ, &tm_qkv, xq, s0 + q0, bar_k0);
-    tc::tma_load_2d(sb + kFwdK, &tm_qkv, xk, s0, bar_k0);
-    issued[0] = 1;
+    tc::tma_load_2d(sb + kFwdQ, &tm_q, xq, sq0 + q0, bar_k0);
+    tc::tma_load_2d(sb + kFwdK, &tm_kv, xk, sk0, bar_k0);
+    pending |= 1u;
     tc::mbar_arrive_expect_tx(bar_v, kImg64);
-    tc::tma_load_2d(sb + kFwdV, &tm_qkv, xv, s0, bar_v);
-    issued[2] = 1;
+    tc::tma_load_2d(sb + kFwdV, &tm_kv, xv, sk0, bar_v);
+    pending |= 4u;
     if (nkb > 1) {
       tc::mbar_arrive_expect_tx(bar_k1, kImg64);
-      tc::tma_load_2d(sb + kFwdK + kImg64, &tm_qkv, xk, s0 + kBlk, bar_k1);
-      issued[1] = 1;
+      tc::tma_load_2d(sb + kFwdK + kImg64, &tm_kv, xk, sk0 + kBlk, bar_k1);
+      pending |= 2u;
     }
     const uint32_t id_s = tc::idesc_bf16(kBlk, kBlk, false, false);
     const uint32_t id_o = tc::idesc_bf16(kBlk, kDh, false, true);
     bool ok = wait_or_fail(bar_k0, 0, a, s_fail, kBitFwd);
     if (ok) {
-      consumed[0] = 1;
+      pending &= ~1u;
+      parity ^= 1u;
       tc::tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < kDh / 16; ++ks)
@@ -219,8 +239,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
       tc::tc_fence_after();
       if (kb + 1 < nkb) {   // next block's scores overlap this block's output update
         const int r = (kb + 1) & 1;
-        if (!(ok = wait_or_fail(bars[r], ((kb + 1) >> 1) & 1, a, s_fail, kBitFwd))) break;
-        consumed[r]++;
+        if (!(ok = wait_or_fail(bar_k0 + 8u * r, ((kb + 1) >> 1) & 1, a, s_fail, kBitFwd))) break;
+        pending &= ~(1u << r);
+        parity ^= 1u << r;
         tc::tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < kDh / 16; ++ks)
@@ -229,7 +250,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
         tc::mma_commit(s_full);
       }
       if (!(ok = wait_or_fail(bar_v, kb & 1, a, s_fail, kBitFwd))) break;
-      consumed[2]++;
+      pending &= ~4u;
+      parity ^= 4u;
       tc::tc_fence_after();
 #pragma unroll
       for (int ks = 0; ks < kBlk / 16; ++ks)
@@ -237,18 +259,19 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
                      ks > 0);
       tc::mma_commit(o_full);
       if (kb + 2 < nkb) {   // K slot kb & 1 was read by S_kb, which completed before P_kb was written
-        tc::mbar_arrive_expect_tx(bars[kb & 1], kImg64);
-        tc::tma_load_2d(sb + kFwdK + (kb & 1) * kImg64, &tm_qkv, xk, s0 + (kb + 2) * kBlk, bars[kb & 1]);
-        issued[kb & 1]++;
+        const uint32_t bk = bar_k0 + 8u * (kb & 1);
+        tc::mbar_arrive_expect_tx(bk, kImg64);
+        tc::tma_load_2d(sb + kFwdK + (kb & 1) * kImg64, &tm_kv, xk, sk0 + (kb + 2) * kBlk, bk);
+        pending |= 1u << (kb & 1);
       }
       if (kb + 1 < nkb) {   // the value block is reloaded once P V has read it
         if (!(ok = wait_or_fail(o_full, kb & 1, a, s_fail, kBitFwd))) break;
         tc::mbar_arrive_expect_tx(bar_v, kImg64);
-        tc::tma_load_2d(sb + kFwdV, &tm_qkv, xv, s0 + (kb + 1) * kBlk, bar_v);
-        issued[2]++;
+        tc::tma_load_2d(sb + kFwdV, &tm_kv, xv, sk0 + (kb + 1) * kBlk, bar_v);
+        pending |= 4u;
       }
     }
-    if (!ok) drain_after_failure(drain, bars, issued, consumed, 3, a);
+    if (!ok) drain_after_failure(drain, bar_k0, pending, parity, 3, a);
   } else if (t < kCompute) {
     // ---- softmax warps: thread t owns query row q0 + t ----
     const uint32_t lane = (uint32_t)(32 * warp) << 16;
@@ -260,7 +283,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
     for (int kb = 0; kb < nkb; ++kb) {
       if (!(ok = wait_or_fail(s_full, kb & 1, a, s_fail, kBitFwd))) break;
       tc::tc_fence_after();
-      const int kvalid = L - kb * kBlk;
+      const int kvalid = Lk - kb * kBlk;
       float mb = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -277,16 +300,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
       if (kb > 0) {   // previous block's P V: into the output row, then P may be overwritten
         if (!(ok = wait_or_fail(o_full, (kb - 1) & 1, a, s_fail, kBitFwd))) break;
         tc::tc_fence_after();
-        float pv[2][32];
-        tc::tmem_ld32_issue(tmem + lane + 128, pv[0]);
-        tc::tmem_ld32_issue(tmem + lane + 160, pv[1]);
-        tc::tmem_ld_wait();
-        tc::tmem_regs_ready(pv[0]);
-        tc::tmem_regs_ready(pv[1]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o[i] = o[i] * alpha_prev + pv[0][i];
-          o[32 + i] = o[32 + i] * alpha_prev + pv[1][i];
+        for (int half = 0; half < 2; ++half) {   // 32 columns at a time keeps the register peak low
+          float pv[32];
+          tc::tmem_ld32_issue(tmem + lane + 128 + 32 * half, pv);
+          tc::tmem_ld_wait();
+          tc::tmem_regs_ready(pv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[32 * half + i] = o[32 * half + i] * alpha_prev + pv[i];
         }
       }
       float sum = 0.f;
@@ -313,28 +334,31 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
     }
     if (ok && wait_or_fail(o_full, (nkb - 1) & 1, a, s_fail, kBitFwd)) {
       tc::tc_fence_after();
-      float pv[2][32];
-      tc::tmem_ld32_issue(tmem + lane + 128, pv[0]);
-      tc::tmem_ld32_issue(tmem + lane + 160, pv[1]);
-      tc::tmem_ld_wait();
-      tc::tmem_regs_ready(pv[0]);
-      tc::tmem_regs_ready(pv[1]);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float pv[32];
+        tc::tmem_ld32_issue(tmem + lane + 128 + 32 * half, pv);
+        tc::tmem_ld_wait();
+        tc::tmem_regs_ready(pv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[32 * half + i] = o[32 * half + i] * alpha_prev + pv[i];
+      }
       const int row = q0 + t;
-      if (row < L) {
+      if (row < Lq) {
         const float inv = 1.f / l;
-        uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)(s0 + row) * (a.heads * kDh) + h * kDh);
+        uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)(sq0 + row) * (a.heads * kDh) + h * kDh);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float y[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int i = 8 * j + e;
-            y[e] = (o[i] * alpha_prev + pv[i >> 5][i & 31]) * inv;
+            y[e] = o[i] * inv;
           }
           dst[j] = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
                               pack_bf16x2(y[6], y[7]));
         }
-        a.lse[(int64_t)h * a.total + s0 + row] = m + log2f(l);
+        a.lse[(int64_t)h * a.total_q + sq0 + row] = m + log2f(l);
       }
     }
   }
@@ -347,12 +371,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a, in
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_dout,
-                const AttnArgs a) {
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
+                const __grid_constant__ CUtensorMap tm_dout, const AttnArgs a) {
   const int h = blockIdx.x % a.heads, seq = blockIdx.x / a.heads;
-  const int s0 = a.cu[seq];
-  const int L = a.cu[seq + 1] - s0;
-  if (L <= 0) return;
+  const int sq0 = a.cu_q[seq], Lq = a.cu_q[seq + 1] - sq0;
+  const int sk0 = a.cu_k[seq], Lk = a.cu_k[seq + 1] - sk0;
+  if (Lq <= 0 || Lk <= 0) {   // no attention pairs: zero gradients
+    for (int i = threadIdx.x; i < Lq * 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(a.dq + (int64_t)(sq0 + (i >> 3)) * a.ldq + a.dq_col + h * kDh)[i & 7] =
+          make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < Lk * 8; i += blockDim.x) {
+      const int64_t r = (int64_t)(sk0 + (i >> 3)) * a.ldkv;
+      reinterpret_cast<uint4*>(a.dkv + r + a.dk_col + h * kDh)[i & 7] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(a.dkv + r + a.dv_col + h * kDh)[i & 7] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -369,8 +403,8 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(misc + 64);
   int* s_fail = reinterpret_cast<int*>(misc + 72);
   const int t = threadIdx.x, warp = t >> 5;
-  const int nb = (L + kBlk - 1) / kBlk;
-  const int npairs = nb * nb;
+  const int nbq = (Lq + kBlk - 1) / kBlk, nbk = (Lk + kBlk - 1) / kBlk;
+  const int npairs = nbk * nbq;
   const int dm = a.heads * kDh;
 
   if (t == kCompute) {
@@ -397,21 +431,23 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
 
   if (t == kCompute) {
     // ---- control: TMA loads, two MMA groups per (key block, query block) pair ----
-    const int xq = h * kDh, xk = (a.heads + h) * kDh, xv = (2 * a.heads + h) * kDh;
-    uint32_t bars[4] = {bar_q0, bar_q1, bar_kv0, bar_kv1}, issued[4] = {0, 0, 0, 0}, consumed[4] = {0, 0, 0, 0};
+    const int xq = a.q_col + h * kDh, xk = a.k_col + h * kDh, xv = a.v_col + h * kDh;
+    uint32_t pending = 0, parity = 0;   // loads in flight per barrier (q0, q1, kv0, kv1), phase parities
     auto load_q = [&](int p) {
-      const int r = p & 1, q0 = (p % nb) * kBlk;
-      tc::mbar_arrive_expect_tx(bars[r], 2 * kImg64);
-      tc::tma_load_2d(sb + kBwdQ + r * kImg64, &tm_qkv, xq, s0 + q0, bars[r]);
-      tc::tma_load_2d(sb + kBwdDO + r * kImg64, &tm_dout, h * kDh, s0 + q0, bars[r]);
-      issued[r]++;
+      const int r = p & 1, q0 = (p % nbq) * kBlk;
+      const uint32_t bq = bar_q0 + 8u * r;
+      tc::mbar_arrive_expect_tx(bq, 2 * kImg64);
+      tc::tma_load_2d(sb + kBwdQ + r * kImg64, &tm_q, xq, sq0 + q0, bq);
+      tc::tma_load_2d(sb + kBwdDO + r * kImg64, &tm_dout, h * kDh, sq0 + q0, bq);
+      pending |= 1u << r;
     };
     auto load_kv = [&](int kb) {
       const int r = kb & 1;
-      tc::mbar_arrive_expect_tx(bars[2 + r], 2 * kImg64);
-      tc::tma_load_2d(sb + kBwdK + r * kImg64, &tm_qkv, xk, s0 + kb * kBlk, bars[2 + r]);
-      tc::tma_load_2d(sb + kBwdV + r * kImg64, &tm_qkv, xv, s0 + kb * kBlk, bars[2 + r]);
-      issued[2 + r]++;
+      const uint32_t bkv = bar_kv0 + 8u * r;
+      tc::mbar_arrive_expect_tx(bkv, 2 * kImg64);
+      tc::tma_load_2d(sb + kBwdK + r * kImg64, &tm_kv, xk, sk0 + kb * kBlk, bkv);
+      tc::tma_load_2d(sb + kBwdV + r * kImg64, &tm_kv, xv, sk0 + kb * kBlk, bkv);
+      pending |= 4u << r;
     };
     load_kv(0);
     load_q(0);
@@ -420,18 +456,20 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
     const uint32_t id_q = tc::idesc_bf16(kBlk, kDh, false, true);      // queries x dh over keys
     bool ok = true;
     for (int p = 0; p < npairs && ok; ++p) {
-      const int kb = p / nb, qb = p % nb, r = p & 1, rk = kb & 1;
+      const int kb = p / nbq, qb = p % nbq, r = p & 1, rk = kb & 1;
       if (p > 0) {   // the previous pair's second group read Q / dO slot (p + 1) & 1 and, at a key block's end, K / V
         if (!(ok = wait_or_fail(g2, (p - 1) & 1, a, s_fail, kBitBwd))) break;
         tc::tc_fence_after();
       }
       if (p + 1 < npairs) load_q(p + 1);
-      if (qb == 0 && kb + 1 < nb) load_kv(kb + 1);
-      if (!(ok = wait_or_fail(bars[r], (p >> 1) & 1, a, s_fail, kBitBwd))) break;
-      consumed[r]++;
+      if (qb == 0 && kb + 1 < nbk) load_kv(kb + 1);
+      if (!(ok = wait_or_fail(bar_q0 + 8u * r, (p >> 1) & 1, a, s_fail, kBitBwd))) break;
+      pending &= ~(1u << r);
+      parity ^= 1u << r;
       if (qb == 0) {
-        if (!(ok = wait_or_fail(bars[2 + rk], (kb >> 1) & 1, a, s_fail, kBitBwd))) break;
-        consumed[2 + rk]++;
+        if (!(ok = wait_or_fail(bar_kv0 + 8u * rk, (kb >> 1) & 1, a, s_fail, kBitBwd))) break;
+        pending &= ~(4u << rk);
+        parity ^= 4u << rk;
       }
       tc::tc_fence_after();
       const uint32_t q_img = sb + kBwdQ + r * kImg64, do_img = sb + kBwdDO + r * kImg64;
@@ -453,15 +491,18 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
       }
       tc::mma_commit(g2);
     }
-    if (!ok) drain_after_failure(drain, bars, issued, consumed, 4, a);
+    if (!ok) drain_after_failure(drain, bar_q0, pending, parity, 4, a);
   } else if (t < kCompute) {
     // ---- elementwise warps: thread t owns row t of each query block (S, dP, dQ)
     // and row t of each key block (dK, dV) ----
-    // D = rowsum(dO * O) of rows t, t + 128, ... (the rows this thread owns
-    // in every query block), while the first MMAs run
-    for (int row = t; row < L; row += kCompute) {
-      const uint4* po = reinterpret_cast<const uint4*>(a.out + (int64_t)(s0 + row) * dm + h * kDh);
-      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + (int64_t)(s0 + row) * dm + h * kDh);
+    // D = rowsum(dO * O) and the log-sum-exp of rows t, t + 128, ... (the
+    // rows this thread owns in every query block), while the first MMAs run;
+    // kept in shared memory (only this thread reads them back)
+    float* s_lse = reinterpret_cast<float*>(smem + kBwdStats);
+    float* s_D = s_lse + kStatRows;
+    for (int row = t; row < Lq; row += kCompute) {
+      const uint4* po = reinterpret_cast<const uint4*>(a.out + (int64_t)(sq0 + row) * dm + h * kDh);
+      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + (int64_t)(sq0 + row) * dm + h * kDh);
       float D = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -474,30 +515,33 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
           D += u.x * w.x + u.y * w.y;
         }
       }
-      a.dvec[(int64_t)h * a.total + s0 + row] = D;
+      const float lse2 = a.lse[(int64_t)h * a.total_q + sq0 + row];
+      if (row < kStatRows) {
+        s_D[row] = D;
+        s_lse[row] = lse2;
+      } else {
+        a.dvec[(int64_t)h * a.total_q + sq0 + row] = D;
+      }
     }
+    float acc[kDh];   // running dQ row of the next pair, fetched a pair ahead
     const uint32_t lane = (uint32_t)(32 * warp) << 16;
     for (int p = 0; p < npairs; ++p) {
-      const int kb = p / nb, qb = p % nb;
+      const int kb = p / nbq, qb = p % nbq;
       const int k0 = kb * kBlk, row = qb * kBlk + t;
-      const bool live = row < L;
+      const bool live = row < Lq;
       float D = 0.f, lse2 = 0.f;
-      float acc[kDh];
       if (live) {
-        D = a.dvec[(int64_t)h * a.total + s0 + row];
-        lse2 = a.lse[(int64_t)h * a.total + s0 + row];
-        if (kb > 0) {   // running dQ row, fetched while the MMAs run
-          const float4* src = reinterpret_cast<const float4*>(a.dq_acc + (int64_t)(s0 + row) * dm + h * kDh);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float4 x = src[j];
-            acc[4 * j] = x.x, acc[4 * j + 1] = x.y, acc[4 * j + 2] = x.z, acc[4 * j + 3] = x.w;
-          }
+        if (row < kStatRows) {
+          D = s_D[row];
+          lse2 = s_lse[row];
+        } else {
+          D = a.dvec[(int64_t)h * a.total_q + sq0 + row];
+          lse2 = a.lse[(int64_t)h * a.total_q + sq0 + row];
         }
       }
       if (!wait_or_fail(g1, p & 1, a, s_fail, kBitBwd)) break;
       tc::tc_fence_after();
-      const int kvalid = L - k0;
+      const int kvalid = Lk - k0;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float s[32], dp[32];
@@ -531,15 +575,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
 #pragma unroll
           for (int i = 0; i < kDh; ++i) g[i >> 5][i & 31] += acc[i];
         }
-        if (kb + 1 < nb) {
-          float4* dst = reinterpret_cast<float4*>(a.dq_acc + (int64_t)(s0 + row) * dm + h * kDh);
+        if (kb + 1 < nbk) {
+          float4* dst = reinterpret_cast<float4*>(a.dq_acc + (int64_t)(sq0 + row) * dm + h * kDh);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float* gj = &g[j >> 3][(j & 7) * 4];
             dst[j] = make_float4(gj[0], gj[1], gj[2], gj[3]);
           }
         } else {   // last key block: the finished dQ row
-          uint4* dst = reinterpret_cast<uint4*>(a.dqkv + (int64_t)(s0 + row) * a.ld + h * kDh);
+          uint4* dst = reinterpret_cast<uint4*>(a.dq + (int64_t)(sq0 + row) * a.ldq + a.dq_col + h * kDh);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float* gj = &g[j >> 2][(j & 3) * 8];
@@ -548,7 +592,18 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
           }
         }
       }
-      if (qb + 1 == nb) {   // the key block's dK and dV (TMEM lane t = key row k0 + t)
+      if (p + 1 < npairs) {   // the next pair's running dQ row (written nbq pairs earlier)
+        const int kb2 = (p + 1) / nbq, row2 = ((p + 1) % nbq) * kBlk + t;
+        if (kb2 > 0 && row2 < Lq) {
+          const float4* src = reinterpret_cast<const float4*>(a.dq_acc + (int64_t)(sq0 + row2) * dm + h * kDh);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float4 x = src[j];
+            acc[4 * j] = x.x, acc[4 * j + 1] = x.y, acc[4 * j + 2] = x.z, acc[4 * j + 3] = x.w;
+          }
+        }
+      }
+      if (qb + 1 == nbq) {   // the key block's dK and dV (TMEM lane t = key row k0 + t)
         const int krow = k0 + t;
         float dv[2][32], dk[2][32];
         tc::tmem_ld32_issue(tmem + lane + 256, dv[0]);
@@ -560,9 +615,9 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
         tc::tmem_regs_ready(dv[1]);
         tc::tmem_regs_ready(dk[0]);
         tc::tmem_regs_ready(dk[1]);
-        if (krow < L) {
-          uint4* pk = reinterpret_cast<uint4*>(a.dqkv + (int64_t)(s0 + krow) * a.ld + (a.heads + h) * kDh);
-          uint4* pv = reinterpret_cast<uint4*>(a.dqkv + (int64_t)(s0 + krow) * a.ld + (2 * a.heads + h) * kDh);
+        if (krow < Lk) {
+          uint4* pk = reinterpret_cast<uint4*>(a.dkv + (int64_t)(sk0 + krow) * a.ldkv + a.dk_col + h * kDh);
+          uint4* pv = reinterpret_cast<uint4*>(a.dkv + (int64_t)(sk0 + krow) * a.ldkv + a.dv_col + h * kDh);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float* k8 = &dk[j >> 2][(j & 3) * 8];
@@ -585,27 +640,41 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constan
   }
 }
 
-void check_common(const torch::Tensor& qkv, const torch::Tensor& cu, int64_t heads, const torch::Tensor& status) {
-  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == torch::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1,
-              "attention: qkv must be a CUDA bf16 [total, 3 * heads * 64] matrix with contiguous rows");
-  TORCH_CHECK(heads > 0 && qkv.size(1) == 3 * heads * kDh, "attention: head dimension must be 64");
-  TORCH_CHECK(qkv.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0,
-              "attention: qkv rows must be 16-byte aligned");
-  TORCH_CHECK(cu.is_cuda() && cu.scalar_type() == torch::kInt32 && cu.dim() == 1 && cu.is_contiguous() &&
-                  cu.numel() >= 2, "attention: cu must be CUDA int32 [samples + 1]");
-  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "attention: status must be CUDA int32");
-  TORCH_CHECK(cu.numel() - 1 < (1ll << 31) && heads < 65536, "attention: too many samples or heads");
-  TORCH_CHECK(qkv.size(0) < (1ll << 31), "attention: too many tokens");
+void check_operand(const torch::Tensor& x, const char* what) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 &&
+                  x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                  x.size(0) < (1ll << 31),
+              "attention: ", what, " must be a CUDA bf16 matrix with contiguous, 16-byte aligned rows");
 }
 
-AttnArgs base_args(const torch::Tensor& qkv, const torch::Tensor& cu, int64_t heads, torch::Tensor& status,
+void check_cols(const torch::Tensor& x, int64_t col, int64_t heads, const char* what) {
+  TORCH_CHECK(col >= 0 && col % 8 == 0 && col + heads * kDh <= x.size(1), "attention: ", what,
+              " columns out of range or not a multiple of 8");
+}
+
+AttnArgs base_args(const torch::Tensor& q, int64_t q_col, const torch::Tensor& kv, int64_t k_col, int64_t v_col,
+                   const torch::Tensor& cu_q, const torch::Tensor& cu_k, int64_t heads, torch::Tensor& status,
                    int64_t wait_ns) {
+  check_operand(q, "the query source");
+  check_operand(kv, "the key / value source");
+  TORCH_CHECK(heads > 0 && heads < 65536, "attention: bad head count");
+  check_cols(q, q_col, heads, "query");
+  check_cols(kv, k_col, heads, "key");
+  check_cols(kv, v_col, heads, "value");
+  for (auto* c : {&cu_q, &cu_k})
+    TORCH_CHECK(c->is_cuda() && c->scalar_type() == torch::kInt32 && c->dim() == 1 && c->is_contiguous() &&
+                    c->numel() >= 2 && c->numel() - 1 < (1ll << 31), "attention: cu must be CUDA int32 [samples + 1]");
+  TORCH_CHECK(cu_q.numel() == cu_k.numel(), "attention: query and key offsets differ in sample count");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "attention: status must be CUDA int32");
+  TORCH_CHECK(wait_ns >= 0, "attention: negative wait");
   AttnArgs a{};
-  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr<at::BFloat16>());
-  a.ld = qkv.stride(0);
-  a.cu = cu.data_ptr<int>();
+  a.cu_q = cu_q.data_ptr<int>();
+  a.cu_k = cu_k.data_ptr<int>();
+  a.q_col = (int)q_col;
+  a.k_col = (int)k_col;
+  a.v_col = (int)v_col;
   a.heads = (int)heads;
-  a.total = qkv.size(0);
+  a.total_q = q.size(0);
   a.scale = 0.125f;
   a.scale_log2 = 0.125f * 1.4426950408889634f;
   a.status = status.data_ptr<int>();
@@ -613,19 +682,31 @@ AttnArgs base_args(const torch::Tensor& qkv, const torch::Tensor& cu, int64_t he
   return a;
 }
 
-// out [total, heads * 64] bf16, lse [heads, total] fp32. `max_len` must be at
-// least the longest sample (it sizes the grid of query blocks).
-void attn_fwd(torch::Tensor qkv, torch::Tensor cu, int64_t max_len, int64_t heads, torch::Tensor out,
-              torch::Tensor lse, torch::Tensor status, int64_t wait_ns) {
-  check_common(qkv, cu, heads, status);
-  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.is_contiguous() &&
-                  out.size(0) == qkv.size(0) && out.size(1) == heads * kDh, "attention: out must be [total, heads * 64]");
-  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() &&
-                  lse.numel() == heads * qkv.size(0), "attention: lse must be fp32 [heads, total]");
-  TORCH_CHECK(max_len >= 0 && wait_ns >= 0, "attention: negative max_len or wait");
-  const int64_t samples = cu.numel() - 1;
-  if (qkv.size(0) == 0 || max_len == 0) return;
-  AttnArgs a = base_args(qkv, cu, heads, status, wait_ns);
+void check_rows(const torch::Tensor& x, int64_t rows, int64_t cols, torch::ScalarType type, const char* what) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == type && x.is_contiguous() && x.numel() == rows * cols &&
+                  reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "attention: ", what, " has the wrong shape, type or layout");
+}
+
+// Sample i's queries are rows cu_q[i]..cu_q[i+1] of `q` (head h at column
+// q_col + 64 h), its keys and values rows cu_k[i]..cu_k[i+1] of `kv` (columns
+// k_col + 64 h and v_col + 64 h). out [total_q, heads * 64] bf16, lse
+// [heads, total_q] fp32. `max_q` must be at least the most queries of a
+// sample (it sizes the grid of query blocks).
+void attn_fwd(torch::Tensor q, int64_t q_col, torch::Tensor kv, int64_t k_col, int64_t v_col, torch::Tensor cu_q,
+              torch::Tensor cu_k, int64_t max_q, int64_t heads, torch::Tensor out, torch::Tensor lse,
+              torch::Tensor status, int64_t wait_ns) {
+  AttnArgs a = base_args(q, q_col, kv, k_col, v_col, cu_q, cu_k, heads, status, wait_ns);
+  check_rows(out, q.size(0), heads * kDh, torch::kBFloat16, "out");
+  check_rows(lse, heads, q.size(0), torch::kFloat32, "lse");
+  TORCH_CHECK(max_q >= 0, "attention: negative max_q");
+  const int64_t samples = cu_q.numel() - 1;
+  if (q.size(0) == 0 || max_q == 0) return;
+  if (kv.size(0) == 0) {   // no keys anywhere: zero output
+    out.zero_();
+    lse.fill_(-INFINITY);
+    return;
+  }
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   a.lse = lse.data_ptr<float>();
   static bool configured = false;
@@ -634,41 +715,59 @@ void attn_fwd(torch::Tensor qkv, torch::Tensor cu, int64_t max_len, int64_t head
                     cudaSuccess, "attention: shared-memory attribute");
     configured = true;
   }
-  const int64_t nqb = (max_len + kBlk - 1) / kBlk;
+  const int64_t nqb = (max_q + kBlk - 1) / kBlk;
   const int64_t blocks = samples * heads * nqb;
   TORCH_CHECK(blocks < (1ll << 31), "attention: too many query blocks");
-  const CUtensorMap tm = tma::bf16_sw128(qkv.data_ptr(), qkv.size(0), qkv.size(1), qkv.stride(0), kBlk);
-  attn_fwd_kernel<<<(unsigned)blocks, kThreads, kFwdSmem, c10::cuda::getCurrentCUDAStream().stream()>>>(tm, a, (int)nqb);
+  const CUtensorMap tq = tma::bf16_sw128(q.data_ptr(), q.size(0), q.size(1), q.stride(0), kBlk);
+  const CUtensorMap tkv = tma::bf16_sw128(kv.data_ptr(), kv.size(0), kv.size(1), kv.stride(0), kBlk);
+  attn_fwd_kernel<<<(unsigned)blocks, kThreads, kFwdSmem, c10::cuda::getCurrentCUDAStream().stream()>>>(tq, tkv, a,
+                                                                                                     (int)nqb);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "attention forward launch failed");
 }
 
-// dqkv [total, 3 * heads * 64] bf16 (every row of every sample written).
-void attn_bwd(torch::Tensor qkv, torch::Tensor cu, int64_t max_len, int64_t heads, torch::Tensor out,
-              torch::Tensor dout, torch::Tensor lse, torch::Tensor dqkv, torch::Tensor status, int64_t wait_ns) {
-  check_common(qkv, cu, heads, status);
-  for (auto* x : {&out, &dout})
-    TORCH_CHECK(x->is_cuda() && x->scalar_type() == torch::kBFloat16 && x->is_contiguous() &&
-                    x->size(0) == qkv.size(0) && x->size(1) == heads * kDh,
-                "attention: out and dout must be contiguous bf16 [total, heads * 64]");
-  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == torch::kFloat32 && lse.is_contiguous() &&
-                  lse.numel() == heads * qkv.size(0), "attention: lse must be fp32 [heads, total]");
-  TORCH_CHECK(dqkv.is_cuda() && dqkv.scalar_type() == torch::kBFloat16 && dqkv.sizes() == qkv.sizes() &&
-                  dqkv.strides() == qkv.strides(), "attention: dqkv must match qkv");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(dqkv.data_ptr()) % 16 == 0, "attention: dqkv must be 16-byte aligned");
-  TORCH_CHECK(max_len >= 0 && wait_ns >= 0, "attention: negative max_len or wait");
-  const int64_t samples = cu.numel() - 1;
-  if (qkv.size(0) == 0 || max_len == 0) return;
-  AttnArgs a = base_args(qkv, cu, heads, status, wait_ns);
+// Gradients of attn_fwd: dq has q's shape and strides (head h's gradient at
+// column dq_col + 64 h), dkv kv's (dk_col, dv_col). Every query and key row of
+// every head is written. `max_k` must be at least the most keys of a sample.
+void attn_bwd(torch::Tensor q, int64_t q_col, torch::Tensor kv, int64_t k_col, int64_t v_col, torch::Tensor cu_q,
+              torch::Tensor cu_k, int64_t max_k, int64_t heads, torch::Tensor out, torch::Tensor dout,
+              torch::Tensor lse, torch::Tensor dq, int64_t dq_col, torch::Tensor dkv, int64_t dk_col, int64_t dv_col,
+              torch::Tensor status, int64_t wait_ns) {
+  AttnArgs a = base_args(q, q_col, kv, k_col, v_col, cu_q, cu_k, heads, status, wait_ns);
+  check_rows(out, q.size(0), heads * kDh, torch::kBFloat16, "out");
+  check_rows(dout, q.size(0), heads * kDh, torch::kBFloat16, "dout");
+  check_rows(lse, heads, q.size(0), torch::kFloat32, "lse");
+  check_operand(dq, "dq");
+  check_operand(dkv, "dkv");
+  TORCH_CHECK(dq.sizes() == q.sizes() && dkv.sizes() == kv.sizes(), "attention: gradient shapes differ from inputs");
+  check_cols(dq, dq_col, heads, "dq");
+  check_cols(dkv, dk_col, heads, "dk");
+  check_cols(dkv, dv_col, heads, "dv");
+  TORCH_CHECK(max_k >= 0, "attention: negative max_k");
+  const int64_t samples = cu_q.numel() - 1;
+  if (q.size(0) == 0 || kv.size(0) == 0) {   // no attention pairs at all
+    if (q.size(0)) dq.narrow(1, dq_col, heads * kDh).zero_();
+    if (kv.size(0)) {
+      dkv.narrow(1, dk_col, heads * kDh).zero_();
+      dkv.narrow(1, dv_col, heads * kDh).zero_();
+    }
+    return;
+  }
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr<at::BFloat16>());
   a.lse = lse.data_ptr<float>();
-  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr<at::BFloat16>());
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr<at::BFloat16>());
+  a.ldq = dq.stride(0);
+  a.dq_col = (int)dq_col;
+  a.dkv = reinterpret_cast<__nv_bfloat16*>(dkv.data_ptr<at::BFloat16>());
+  a.ldkv = dkv.stride(0);
+  a.dk_col = (int)dk_col;
+  a.dv_col = (int)dv_col;
   torch::Tensor acc;
-  if (max_len > kBlk) {   // dQ rows summed over several key blocks
-    acc = torch::empty({qkv.size(0), heads * kDh}, qkv.options().dtype(torch::kFloat32));
+  if (max_k > kBlk) {   // dQ rows summed over several key blocks
+    acc = torch::empty({q.size(0), heads * kDh}, q.options().dtype(torch::kFloat32));
     a.dq_acc = acc.data_ptr<float>();
   }
-  torch::Tensor dvec = torch::empty({heads, qkv.size(0)}, qkv.options().dtype(torch::kFloat32));
+  torch::Tensor dvec = torch::empty({heads, q.size(0)}, q.options().dtype(torch::kFloat32));
   a.dvec = dvec.data_ptr<float>();
   static bool configured = false;
   if (!configured) {
@@ -677,10 +776,11 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor cu, int64_t max_len, int64_t head
     configured = true;
   }
   TORCH_CHECK(samples * heads < (1ll << 31), "attention: too many samples");
-  const CUtensorMap tm = tma::bf16_sw128(qkv.data_ptr(), qkv.size(0), qkv.size(1), qkv.stride(0), kBlk);
-  const CUtensorMap tmd = tma::bf16_sw128(dout.data_ptr(), dout.size(0), dout.size(1), dout.stride(0), kBlk);
+  const CUtensorMap tq = tma::bf16_sw128(q.data_ptr(), q.size(0), q.size(1), q.stride(0), kBlk);
+  const CUtensorMap tkv = tma::bf16_sw128(kv.data_ptr(), kv.size(0), kv.size(1), kv.stride(0), kBlk);
+  const CUtensorMap td = tma::bf16_sw128(dout.data_ptr(), dout.size(0), dout.size(1), heads * kDh, kBlk);
   attn_bwd_kernel<<<(unsigned)(samples * heads), kThreads, kBwdSmem, c10::cuda::getCurrentCUDAStream().stream()>>>(
-      tm, tmd, a);
+      tq, tkv, td, a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "attention backward launch failed");
 }
 
@@ -688,9 +788,12 @@ void attn_bwd(torch::Tensor qkv, torch::Tensor cu, int64_t max_len, int64_t head
 
 void register_attention_ops(py::module& m) {
   m.def("attn_fwd", &attn_fwd, "variable-length multi-head attention forward (tcgen05, head dim 64)",
-        py::arg("qkv"), py::arg("cu"), py::arg("max_len"), py::arg("heads"), py::arg("out"), py::arg("lse"),
-        py::arg("status"), py::arg("wait_ns") = 2000000000ll);
+        py::arg("q"), py::arg("q_col"), py::arg("kv"), py::arg("k_col"), py::arg("v_col"), py::arg("cu_q"),
+        py::arg("cu_k"), py::arg("max_q"), py::arg("heads"), py::arg("out"), py::arg("lse"), py::arg("status"),
+        py::arg("wait_ns") = 2000000000ll);
   m.def("attn_bwd", &attn_bwd, "variable-length multi-head attention backward (tcgen05, head dim 64)",
-        py::arg("qkv"), py::arg("cu"), py::arg("max_len"), py::arg("heads"), py::arg("out"), py::arg("dout"),
-        py::arg("lse"), py::arg("dqkv"), py::arg("status"), py::arg("wait_ns") = 2000000000ll);
+        py::arg("q"), py::arg("q_col"), py::arg("kv"), py::arg("k_col"), py::arg("v_col"), py::arg("cu_q"),
+        py::arg("cu_k"), py::arg("max_k"), py::arg("heads"), py::arg("out"), py::arg("dout"), py::arg("lse"),
+        py::arg("dq"), py::arg("dq_col"), py::arg("dkv"), py::arg("dk_col"), py::arg("dv_col"), py::arg("status"),
+        py::arg("wait_ns") = 2000000000ll);
 }

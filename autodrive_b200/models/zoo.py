@@ -42,7 +42,7 @@ from torch.nn import functional as F
 
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
-from ..ops.attention import supported as _tc_attention_supported, varlen_attention
+from ..ops.attention import supported as _tc_attention_supported, varlen_attention, varlen_query_attention
 from ..ops.layernorm import FusedLayerNorm
 from ..ops.tc_linear import _TcLinearFn, tensorize
 
@@ -369,6 +369,8 @@ class SelfAttention(nn.Module):
         kv = _linear(x, self.in_proj_weight[d:], self.in_proj_bias[d:], self.tensor_cores)
         q = _linear(x[rows], self.in_proj_weight[:d], self.in_proj_bias[:d], self.tensor_cores)
         cu_q = torch.arange(rows.numel() + 1, device=x.device, dtype=torch.int32)
+        if self.tensor_cores and kv.is_cuda and self.dim == self.heads * 64:
+            return self.out_proj(varlen_query_attention(q, kv, cu_q, cu, 1, max_len, self.heads))
         return self.out_proj(_VarlenQueryAttention.apply(q, kv, self.heads, cu_q, cu, max_len))
 
     def forward(self, x: Tensor, padding: Tensor) -> Tensor:

@@ -97,3 +97,25 @@ def test_entity_network_uses_the_tensor_core_attention():
         ref = att(pad, mask)
     for i, (a, n) in enumerate(zip([0, 17, 157], lengths)):
         torch.testing.assert_close(y[a:a + n].float(), ref[i, :n].float(), rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("queries", [[1] * 12, [3, 1, 0, 130, 2, 1, 1, 5, 1, 1, 1, 1]])
+def test_query_attention_matches_fp32_reference(queries):
+    from autodrive_b200.ops.attention import reference_query_attention, varlen_query_attention
+    g = torch.Generator().manual_seed(3)
+    keys = LENGTHS
+    q = (torch.randn((sum(queries), HEADS * 64), generator=g) * 1.5).cuda().to(torch.bfloat16).requires_grad_(True)
+    kv = (torch.randn((sum(keys), 2 * HEADS * 64), generator=g) * 1.5).cuda().to(torch.bfloat16).requires_grad_(True)
+    cu_q = torch.tensor([0] + torch.tensor(queries).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    cu_k = torch.tensor([0] + torch.tensor(keys).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    out = varlen_query_attention(q, kv, cu_q, cu_k, max(queries), max(keys), HEADS)
+    qr, kvr = q.detach().float().requires_grad_(True), kv.detach().float().requires_grad_(True)
+    ref = reference_query_attention(qr, kvr, cu_q, cu_k, HEADS)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    dout = torch.randn(out.shape, generator=torch.Generator().manual_seed(4)).cuda()
+    out.backward(dout.to(out.dtype))
+    ref.backward(dout)
+    for got, want in ((q.grad.float(), qr.grad), (kv.grad.float(), kvr.grad)):
+        rel = (got - want).norm() / want.norm().clamp_min(1e-6)
+        assert float(rel) < 2e-2, float(rel)
