@@ -7,7 +7,10 @@ encoder's PPO minibatch (tokens x d = 256, 4 heads, feed-forward 1024).
 Each case is timed with CUDA events over `iters` launches after 3 warm-up
 launches; every operand set is larger than the 126 MB L2 or rotates through
 buffers that together are, so each launch reads from HBM. Prints one JSON line
-per case: time, TFLOP/s, and the same for cuBLAS.
+per case: time, TFLOP/s, and the same for cuBLAS. Two more cases time the
+GELU epilogues (the feed-forward's first forward GEMM with GELU and the kept
+pre-activation; its backward dH GEMM scaled by GELU') against cuBLAS followed
+by PyTorch's GELU kernels.
 """
 from __future__ import annotations
 
@@ -57,6 +60,32 @@ def main(argv=None) -> None:
                           "tc_gemm_ms": round(ours, 4), "tc_gemm_tflops": round(flops / ours / 1e9, 1),
                           "cublas_ms": round(ref, 4), "cublas_tflops": round(flops / ref / 1e9, 1)}), flush=True)
         del a, b, out, out_ref
+    # fused GELU epilogues against cuBLAS + the PyTorch GELU kernels
+    x = [torch.randn((m, 256), device=dev).bfloat16() for _ in range(2)]
+    w1 = torch.randn((1024, 256), device=dev).bfloat16()
+    bias = torch.randn(1024, device=dev)
+    z = torch.empty((m, 1024), device=dev, dtype=torch.bfloat16)
+    h = torch.empty((m, 1024), device=dev, dtype=torch.bfloat16)
+    ours = _time(lambda i: gemm(x[i % 2], w1, bias=bias, act="gelu", aux=z, out=h), args.iters)
+    b16 = bias.bfloat16()
+
+    def ref_fwd(i):
+        zz = torch.addmm(b16, x[i % 2], w1.T)
+        return torch.nn.functional.gelu(zz)
+    ref = _time(ref_fwd, args.iters)
+    print(json.dumps({"case": "ff1 forward + GELU (pre-activation kept)", "M": m, "N": 1024, "K": 256,
+                      "tc_gemm_ms": round(ours, 4), "cublas_plus_gelu_ms": round(ref, 4)}), flush=True)
+    dy = [torch.randn((m, 256), device=dev).bfloat16() for _ in range(2)]
+    w2 = torch.randn((256, 1024), device=dev).bfloat16()
+    dz = torch.empty((m, 1024), device=dev, dtype=torch.bfloat16)
+    ours = _time(lambda i: gemm(dy[i % 2], w2, b_mn=True, act="gelu_grad", aux=z, out=dz), args.iters)
+
+    def ref_bwd(i):
+        dh = torch.mm(dy[i % 2], w2)
+        return torch.ops.aten.gelu_backward(dh, z)
+    ref = _time(ref_bwd, args.iters)
+    print(json.dumps({"case": "ff2 dX x GELU' (backward of the above)", "M": m, "N": 1024, "K": 256,
+                      "tc_gemm_ms": round(ours, 4), "cublas_plus_gelu_backward_ms": round(ref, 4)}), flush=True)
 
 
 if __name__ == "__main__":

@@ -41,6 +41,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "tc_sm100.h"
 #include "tma_map.h"
@@ -64,7 +65,10 @@ struct GemmArgs {
   __nv_bfloat16* c_bf16;
   int64_t ldc;
   const float* bias;   // [N] or null
-  int act;             // 0 none, 1 tanh, 2 relu, 3 gelu (tanh form)
+  int act;             // 0 none, 1 tanh, 2 relu, 3 gelu (tanh form), 4 gelu (erf form),
+                       // 5 times GELU'(aux_in) (erf form; the backward of act 4)
+  __nv_bfloat16* aux_out;        // act 4: the pre-activation, bf16, same layout as C (or null)
+  const __nv_bfloat16* aux_in;   // act 5: the pre-activation the gradient is scaled by
   int accumulate;      // C += result (fp32 output only)
   int k_steps;         // K steps (of kBK) per split-K slice
   int splits;          // split-K slices (1: no split)
@@ -85,6 +89,28 @@ __device__ __forceinline__ float apply_act(float x, int act) {
   }
 }
 
+// GELU (erf form) z Phi(z) and its derivative Phi(z) + z phi(z), with
+// erf from Abramowitz & Stegun, Handbook of Mathematical Functions, formula
+// 7.1.26: erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),
+// t = 1 / (1 + p x), x >= 0, |error| <= 1.5e-7 (odd extension for x < 0).
+// For x = |z| / sqrt(2) the factor exp(-x^2) = exp(-z^2 / 2) is also the
+// normal density's, so the backward takes one exponential and one reciprocal.
+struct PhiParts { float cdf, pdf; };   // Phi(z), phi(z)
+__device__ __forceinline__ PhiParts normal_parts(float z) {
+  const float x = fabsf(z) * 0.7071067811865476f;
+  const float t = __fdividef(1.f, fmaf(0.3275911f, x, 1.f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, 1.061405429f, -1.453152027f), 1.421413741f),
+                                      -0.284496736f), 0.254829592f);
+  const float e = exp2f(-0.7213475204444817f * z * z);   // exp(-z^2 / 2) = 2^(-z^2 / (2 ln 2))
+  const float erf_x = 1.f - poly * e;
+  return PhiParts{0.5f * (1.f + copysignf(erf_x, z)), 0.3989422804014327f * e};
+}
+__device__ __forceinline__ float gelu_erf(float x) { return x * normal_parts(x).cdf; }
+__device__ __forceinline__ float gelu_erf_grad(float z) {
+  const PhiParts q = normal_parts(z);
+  return q.cdf + z * q.pdf;
+}
+
 // Work item w -> (m0, n0, split slice z); N tiles fastest.
 struct TileCoord { int m0, n0, z; };
 __device__ __forceinline__ TileCoord tile_of(int w, int tiles_n, int tiles_m) {
@@ -98,10 +124,72 @@ __device__ __forceinline__ TileCoord tile_of(int w, int tiles_n, int tiles_m) {
 
 // One accumulator's 32 x 32 chunk of this thread's row: bias, activation and
 // the store (16-byte vectors for a full aligned chunk, scalars otherwise).
-__device__ __forceinline__ void store_chunk(const GemmArgs& g, float (&v)[32], int row, int c0, int z) {
+// The GELU (erf) epilogues, compiled into their own kernel instantiations so
+// the plain GEMM keeps its register budget: act 4 adds the bias, keeps the
+// pre-activation in aux_out and applies GELU; act 5 scales the product by
+// GELU' of the pre-activation aux_in. Then the common store.
+__device__ __forceinline__ void gelu_epilogue(const GemmArgs& g, float (&v)[32], int row, int c0) {
+  const int64_t off0 = (int64_t)row * g.ldc + c0;
+// GELU (erf) forward with the pre-activation kept, or its backward
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i] + (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f), g.act);
+  for (int i = 0; i < 32; ++i) v[i] += (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f);
+  const bool vec_aux = c0 + 32 <= g.N && (g.ldc % 8) == 0;   // aux bases are 16-byte aligned (host check)
+  if (g.act == 4) {
+    if (g.aux_out) {
+      if (vec_aux) {
+        uint4* dst = reinterpret_cast<uint4*>(g.aux_out + off0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 u;
+          uint32_t* w = &u.x;
+#pragma unroll
+          for (int hh = 0; hh < 4; ++hh) {
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * j + 2 * hh], v[8 * j + 2 * hh + 1]);
+            w[hh] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          dst[j] = u;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < g.N) g.aux_out[off0 + i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+  } else {
+    float zv[32];
+    if (vec_aux) {
+      const uint4* src = reinterpret_cast<const uint4*>(g.aux_in + off0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = src[j];
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int hh = 0; hh < 4; ++hh) {
+          const float2 f = __bfloat1622float2(b2[hh]);
+          zv[8 * j + 2 * hh] = f.x;
+          zv[8 * j + 2 * hh + 1] = f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) zv[i] = c0 + i < g.N ? __bfloat162float(g.aux_in[off0 + i]) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(zv[i]);
+  }
+}
+
+template <bool GELU>
+__device__ __forceinline__ void store_chunk(const GemmArgs& g, float (&v)[32], int row, int c0, int z) {
   const int64_t off0 = (int64_t)z * g.split_stride + (int64_t)row * g.ldc + c0;
+  if constexpr (GELU) {
+    gelu_epilogue(g, v, row, c0);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i] + (g.bias && c0 + i < g.N ? g.bias[c0 + i] : 0.f), g.act);
+  }
   // each thread owns one output row: a full in-bounds 32-column chunk goes
   // out as 16-byte vector stores (64 B bf16 / 128 B fp32 per row)
   const bool vec = c0 + 32 <= g.N && (g.ldc % 8) == 0 &&
@@ -141,7 +229,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& g, float (&v)[32], i
   }
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool GELU>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
@@ -299,7 +387,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       tc::mbar_arrive(tempty0 + 8 * acc);   // accumulator read out: the MMA warp may reuse it
       if (row < g.M) {
 #pragma unroll
-        for (int k = 0; k < kChunks; ++k) store_chunk(g, v[k], row, t.n0 + 32 * (2 * k + half), t.z);
+        for (int k = 0; k < kChunks; ++k) store_chunk<GELU>(g, v[k], row, t.n0 + 32 * (2 * k + half), t.z);
       }
     }
   }
@@ -326,11 +414,11 @@ int sm_count() {
   return counts[dev];
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool GELU = false>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN, GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
     configured = true;
   }
@@ -338,7 +426,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cud
   const int64_t total = (int64_t)((g.N + kBN - 1) / kBN) * ((g.M + kBM - 1) / kBM) * g.splits;
   TORCH_CHECK(total < (1ll << 31), "tc_gemm: too many output tiles");
   const int grid = (int)std::min<int64_t>(total, sm_count());
-  tc_gemm_kernel<A_MN, B_MN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
+  tc_gemm_kernel<A_MN, B_MN, GELU><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "tc_gemm launch failed");
 }
 
@@ -347,7 +435,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cud
 // elements and the base pointers 16-byte aligned (TMA rules).
 void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tensor c,
              c10::optional<torch::Tensor> bias, int64_t act, bool accumulate, torch::Tensor status,
-             int64_t wait_ns) {
+             int64_t wait_ns, c10::optional<torch::Tensor> aux) {
   for (auto* t : {&a, &b, &c, &status})
     TORCH_CHECK(t->is_cuda() && t->dim() >= 1, "tc_gemm operands must be CUDA tensors");
   TORCH_CHECK(a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
@@ -383,17 +471,45 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
     g.bias = bias->data_ptr<float>();
   }
   g.act = (int)act;
+  TORCH_CHECK(act >= 0 && act <= 5, "tc_gemm: unknown activation");
   g.accumulate = accumulate ? 1 : 0;
+  if (act >= 4) {
+    TORCH_CHECK(!accumulate, "tc_gemm: GELU epilogues do not accumulate");
+    TORCH_CHECK(act == 4 || (aux && aux->defined()), "tc_gemm: the GELU backward epilogue needs the pre-activation");
+  }
+  if (aux && aux->defined()) {
+    TORCH_CHECK(act >= 4, "tc_gemm: an auxiliary tensor goes with the GELU epilogues only");
+    TORCH_CHECK(aux->is_cuda() && aux->scalar_type() == torch::kBFloat16 && aux->dim() == 2 && aux->size(0) == M &&
+                    aux->size(1) == N && aux->stride(1) == 1 && aux->stride(0) == c.stride(0) &&
+                    reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 == 0,
+                "tc_gemm: aux must be bf16 [M, N] with C's row stride, 16-byte aligned");
+    if (act == 4) g.aux_out = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr<at::BFloat16>());
+    else g.aux_in = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr<at::BFloat16>());
+  }
   g.status = status.data_ptr<int>();
   g.wait_ns = (uint64_t)wait_ns;
+  // Epilogue of a result computed outside the kernel (empty contraction, split-K sums).
+  auto finish = [&](torch::Tensor z) {
+    if (act == 4) {
+      if (aux && aux->defined()) aux->copy_(z);
+      z = torch::gelu(z);
+    } else if (act == 5) {
+      const auto p = aux->to(torch::kFloat32);
+      z = z * (0.5 * (1 + torch::erf(p * M_SQRT1_2)) + p * (0.5 * M_2_SQRTPI * M_SQRT1_2) * torch::exp(-0.5 * p * p));
+    } else if (act == 1) {
+      z = z.tanh();
+    } else if (act == 2) {
+      z = z.relu();
+    } else if (act == 3) {
+      z = torch::gelu(z, "tanh");
+    }
+    if (accumulate) c.add_(z);
+    else c.copy_(z);
+  };
   if (K == 0) {  // empty contraction: C = act(bias) (or unchanged when accumulating zero)
     auto z = torch::zeros({M, N}, c.options().dtype(torch::kFloat32));
     if (g.bias) z += *bias;
-    if (act == 1) z = z.tanh();
-    else if (act == 2) z = z.relu();
-    else if (act == 3) z = torch::gelu(z, "tanh");
-    if (accumulate) c.add_(z);
-    else c.copy_(z);
+    finish(z);
     return;
   }
   // A: K-major [M][K] -> box 64 K x 128 rows; MN-major [K][M] -> box 64 M x 64 K rows
@@ -420,19 +536,41 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
     g.bias = nullptr;
     g.act = 0;
     g.accumulate = 0;
+    g.aux_out = nullptr;
+    g.aux_in = nullptr;
   }
-  if (!a_mn && !b_mn) launch<false, false>(ta, tb, g, st);
+  // GELU epilogues exist for the two layouts a feed-forward layer uses them
+  // in (forward: both K-major; backward dX: B MN-major); other layouts run
+  // the plain GEMM and the activation afterwards.
+  const bool gelu = g.act >= 4;
+  const bool gelu_fused = gelu && !a_mn && ((g.act == 4 && !b_mn) || (g.act == 5 && b_mn));
+  if (gelu && !gelu_fused) {
+    partial = torch::empty({M, N}, c.options().dtype(torch::kFloat32));
+    g.c_f32 = partial.data_ptr<float>();
+    g.c_bf16 = nullptr;
+    g.ldc = N;
+    g.split_stride = 0;
+    g.bias = nullptr;
+    g.act = 0;
+    g.aux_out = nullptr;
+    g.aux_in = nullptr;
+  }
+  if (gelu_fused && !a_mn && !b_mn) launch<false, false, true>(ta, tb, g, st);
+  else if (gelu_fused) launch<false, true, true>(ta, tb, g, st);
+  else if (!a_mn && !b_mn) launch<false, false>(ta, tb, g, st);
   else if (!a_mn && b_mn) launch<false, true>(ta, tb, g, st);
   else if (a_mn && !b_mn) launch<true, false>(ta, tb, g, st);
   else launch<true, true>(ta, tb, g, st);
+  if (gelu && !gelu_fused) {
+    torch::Tensor z = partial;
+    if (bias && bias->defined()) z += *bias;
+    finish(z);
+    return;
+  }
   if (splits > 1) {
     auto z = partial.sum(0);
     if (bias && bias->defined()) z += *bias;
-    if (act == 1) z = z.tanh();
-    else if (act == 2) z = z.relu();
-    else if (act == 3) z = torch::gelu(z, "tanh");
-    if (accumulate) c.add_(z);
-    else c.copy_(z);
+    finish(z);
   }
 }
 
@@ -441,5 +579,6 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
 void register_tc_gemm_ops(py::module& m) {
   m.def("tc_gemm", &tc_gemm, "bf16 tcgen05 GEMM C = op(A) op(B)^T (+bias, activation), TMA-fed, fp32 accumulate",
         py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("c"), py::arg("bias"),
-        py::arg("act"), py::arg("accumulate"), py::arg("status"), py::arg("wait_ns") = 2000000000ll);
+        py::arg("act"), py::arg("accumulate"), py::arg("status"), py::arg("wait_ns") = 2000000000ll,
+        py::arg("aux") = py::none());
 }

@@ -22,7 +22,7 @@ from torch.nn import functional as F
 from ..utils import launches
 from .ext import require_extension
 
-ACTS = {None: 0, "none": 0, "tanh": 1, "relu": 2}
+ACTS = {None: 0, "none": 0, "tanh": 1, "relu": 2, "gelu": 4, "gelu_grad": 5}
 
 
 def _pad8(n: int) -> int:
@@ -146,9 +146,12 @@ def check_gemm_status(device=None, block: bool = True) -> None:
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = False, bias=None, act=None,
          out: torch.Tensor | None = None, accumulate: bool = False, out_dtype=torch.float32,
-         wait_ns: int = 2_000_000_000) -> torch.Tensor:
+         wait_ns: int = 2_000_000_000, aux: torch.Tensor | None = None) -> torch.Tensor:
     """C = op(A) op(B)^T on the tensor cores; A is [M,K] (or [K,M] when a_mn),
     B is [N,K] (or [K,N] when b_mn); both bf16 with row strides % 8 == 0.
+    `act` "gelu" (erf form) also writes the pre-activation into `aux` (bf16,
+    C's layout) when given; "gelu_grad" multiplies the product by GELU' of
+    the pre-activation `aux` (the backward of "gelu").
     `wait_ns` bounds every pipeline wait inside the kernel (tests shorten it
     to make a wait run out); timeouts surface through `check_gemm_status`."""
     ext = require_extension()
@@ -156,7 +159,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn: bool = False, b_mn: bool = F
     n = b.shape[1] if b_mn else b.shape[0]
     if out is None:
         out = torch.empty((m, n), dtype=out_dtype, device=a.device)
-    ext.tc_gemm(a, a_mn, b, b_mn, out, bias, ACTS[act], accumulate, _Status.get(a.device), int(wait_ns))
+    ext.tc_gemm(a, a_mn, b, b_mn, out, bias, ACTS[act], accumulate, _Status.get(a.device), int(wait_ns), aux)
     launches.add(1)
     _Status.after_launch(a.device)
     return out
@@ -176,13 +179,17 @@ class _TcLinearFn(torch.autograd.Function):
         xb = _bf16_padded(x2, in_p)
         wb = _bf16_padded(weight.detach(), in_p, rows=out_p)
         target = _result_dtype(x)
+        y_dtype = torch.bfloat16 if target == torch.bfloat16 else torch.float32
+        # "gelu": the epilogue also keeps the pre-activation (bf16) for the backward
+        z = torch.empty((xb.shape[0], out_f), dtype=torch.bfloat16, device=x.device) if act == "gelu" else None
         y = gemm(xb, wb[:out_f], bias=None if bias is None else bias.detach().float().contiguous(), act=act,
-                 out_dtype=torch.bfloat16 if target == torch.bfloat16 else torch.float32)
+                 out_dtype=y_dtype, aux=z)
         ctx.act = act
         ctx.shapes = (in_f, out_f, in_p, out_p, lead)
         ctx.x_dtype = x.dtype
         ctx.has_bias = bias is not None
-        ctx.save_for_backward(xb, wb, y if act in ("tanh", "relu") else torch.empty(0, device=x.device))
+        keep = y if act in ("tanh", "relu") else (z if act == "gelu" else torch.empty(0, device=x.device))
+        ctx.save_for_backward(xb, wb, keep)
         y = y.reshape(*lead, out_f)
         return y if y.dtype == target else y.to(target)
 
@@ -195,6 +202,8 @@ class _TcLinearFn(torch.autograd.Function):
             g = g.float() * (1 - y.float().square())
         elif ctx.act == "relu":
             g = g.float() * (y > 0)
+        elif ctx.act == "gelu":   # y holds the pre-activation
+            g = torch.ops.aten.gelu_backward(g.float(), y.float())
         gb = _bf16_padded(g, out_p)
         gx = gw = gbias = None
         if ctx.needs_input_grad[0]:
@@ -208,7 +217,8 @@ class _TcLinearFn(torch.autograd.Function):
 
 
 class TcLinear(nn.Linear):
-    """nn.Linear on the tensor-core GEMM (CUDA), optional fused activation."""
+    """nn.Linear on the tensor-core GEMM (CUDA), optional fused activation
+    ("tanh", "relu", or "gelu" in its exact erf form, like nn.GELU())."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True, act: str | None = None,
                  device=None, dtype=None):
@@ -220,21 +230,105 @@ class TcLinear(nn.Linear):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.device.type != "cuda":
             y = F.linear(x, self.weight, self.bias)
+            if self.act == "gelu":
+                return F.gelu(y)
             return torch.tanh(y) if self.act == "tanh" else (F.relu(y) if self.act == "relu" else y)
         return _TcLinearFn.apply(x, self.weight, self.bias, self.act)
 
 
+def _plain_gelu(m: nn.Module) -> bool:
+    return type(m) is nn.GELU and m.approximate == "none"
+
+
+def _as_tc_linear(child: nn.Linear, act=None) -> TcLinear:
+    tl = TcLinear.__new__(TcLinear)
+    nn.Module.__init__(tl)
+    tl.in_features, tl.out_features, tl.act = child.in_features, child.out_features, act
+    tl.weight = child.weight
+    tl.bias = child.bias
+    return tl
+
+
 def tensorize(module: nn.Module) -> nn.Module:
     """Replace every nn.Linear in `module` (recursively) with a TcLinear that
-    shares its parameters. Returns the module."""
-    for name, child in list(module.named_children()):
+    shares its parameters; a Linear -> GELU -> Linear sequence becomes a
+    `TcFeedForward` (GELU fused into both GEMM epilogues) and a Linear
+    followed by a GELU a TcLinear with the GELU in its epilogue (the GELU
+    module becomes an Identity). Parameters and state-dict keys are kept.
+    Returns the module."""
+    if type(module) is nn.Sequential and len(module) == 3 and type(module[0]) is nn.Linear \
+            and _plain_gelu(module[1]) and type(module[2]) is nn.Linear:
+        module.__class__ = TcFeedForward
+        module[0] = _as_tc_linear(module[0])
+        module[2] = _as_tc_linear(module[2])
+        return module
+    children = list(module.named_children())
+    for k, (name, child) in enumerate(children):
         if type(child) is nn.Linear:
-            tl = TcLinear.__new__(TcLinear)
-            nn.Module.__init__(tl)
-            tl.in_features, tl.out_features, tl.act = child.in_features, child.out_features, None
-            tl.weight = child.weight
-            tl.bias = child.bias
-            setattr(module, name, tl)
+            fuse = isinstance(module, nn.Sequential) and k + 1 < len(children) and _plain_gelu(children[k + 1][1])
+            setattr(module, name, _as_tc_linear(child, "gelu" if fuse else None))
+            if fuse:
+                setattr(module, children[k + 1][0], nn.Identity())
         else:
             tensorize(child)
     return module
+
+
+class _TcFeedForwardFn(torch.autograd.Function):
+    """Linear -> GELU (erf) -> Linear on three tensor-core GEMMs forward and
+    three backward. The first forward GEMM writes GELU(Z) and keeps Z (bf16);
+    the backward's dH GEMM multiplies by GELU'(Z) in its epilogue, so dZ comes
+    out of it directly: no GELU pass and no dH tensor."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2):
+        hid, in_f = w1.shape
+        out_f = w2.shape[0]
+        lead = x.shape[:-1]
+        xb = _bf16_padded(x.reshape(-1, in_f), in_f)
+        w1b = _bf16_padded(w1.detach(), in_f)
+        w2b = _bf16_padded(w2.detach(), hid)
+        m = xb.shape[0]
+        z = torch.empty((m, hid), dtype=torch.bfloat16, device=x.device)
+        h = gemm(xb, w1b, bias=None if b1 is None else b1.detach().float().contiguous(), act="gelu",
+                 out_dtype=torch.bfloat16, aux=z)
+        target = _result_dtype(x)
+        y = gemm(h, w2b, bias=None if b2 is None else b2.detach().float().contiguous(),
+                 out_dtype=torch.bfloat16 if target == torch.bfloat16 else torch.float32)
+        ctx.save_for_backward(xb, w1b, w2b, z, h)
+        ctx.lead, ctx.x_dtype, ctx.biases = lead, x.dtype, (b1 is not None, b2 is not None)
+        y = y.reshape(*lead, out_f)
+        return y if y.dtype == target else y.to(target)
+
+    @staticmethod
+    def backward(ctx, gy):
+        xb, w1b, w2b, z, h = ctx.saved_tensors
+        out_f, hid = w2b.shape
+        in_f = w1b.shape[1]
+        g = _bf16_padded(gy.reshape(-1, out_f), out_f)
+        dz = gemm(g, w2b, b_mn=True, act="gelu_grad", aux=z, out_dtype=torch.bfloat16)
+        gx = gw1 = gb1 = gw2 = gb2 = None
+        if ctx.needs_input_grad[0]:
+            gx_dtype = torch.bfloat16 if ctx.x_dtype == torch.bfloat16 else torch.float32
+            gx = gemm(dz, w1b, b_mn=True, out_dtype=gx_dtype).reshape(*ctx.lead, in_f)
+        if ctx.needs_input_grad[1]:
+            gw1 = gemm(dz, xb, a_mn=True, b_mn=True)
+        if ctx.biases[0] and ctx.needs_input_grad[2]:
+            gb1 = dz.sum(0, dtype=torch.float32)
+        if ctx.needs_input_grad[3]:
+            gw2 = gemm(g, h, a_mn=True, b_mn=True)
+        if ctx.biases[1] and ctx.needs_input_grad[4]:
+            gb2 = g.sum(0, dtype=torch.float32)
+        return gx, gw1, gb1, gw2, gb2
+
+
+class TcFeedForward(nn.Sequential):
+    """Linear -> GELU -> Linear (children 0, 1, 2, as the nn.Sequential it
+    replaces) whose CUDA forward and backward run as `_TcFeedForwardFn`; on
+    CPU it is the plain sequence."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        l1, l2 = self[0], self[2]
+        if x.device.type != "cuda" or l1.in_features % 8 or l1.out_features % 8 or l2.out_features % 8:
+            return super().forward(x)
+        return _TcFeedForwardFn.apply(x, l1.weight, l1.bias, l2.weight, l2.bias)

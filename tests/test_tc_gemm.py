@@ -62,6 +62,88 @@ def test_gemm_epilogues():
 
 
 @pytest.mark.gpu
+def test_gelu_epilogues_keep_and_use_the_pre_activation():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(300, 64, device="cuda", generator=g).bfloat16()
+    b = torch.randn(136, 64, device="cuda", generator=g).bfloat16()
+    bias = torch.randn(136, device="cuda", generator=g)
+    z_ref = a.float() @ b.float().T + bias
+    z = torch.empty(300, 136, device="cuda", dtype=torch.bfloat16)
+    y = gemm(a, b, bias=bias, act="gelu", aux=z, out_dtype=torch.bfloat16)
+    torch.testing.assert_close(z.float(), z_ref, rtol=1e-2, atol=5e-2)
+    torch.testing.assert_close(y.float(), torch.nn.functional.gelu(z_ref), rtol=1e-2, atol=5e-2)
+    # backward epilogue: (A B^T) * GELU'(z)
+    dy = torch.randn(300, 96, device="cuda", generator=g).bfloat16()
+    w = torch.randn(96, 136, device="cuda", generator=g).bfloat16()
+    dz = gemm(dy, w, b_mn=True, act="gelu_grad", aux=z)
+    zf = z.float().requires_grad_(True)
+    torch.nn.functional.gelu(zf).backward(dy.float() @ w.float())
+    torch.testing.assert_close(dz, zf.grad, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+def test_gelu_epilogue_precision_in_fp32():
+    """fp32 outputs expose the epilogue's own error: the GELU and GELU' values
+    agree with PyTorch's exact (erf) forms to ~1e-6 over [-8, 8]."""
+    g = torch.Generator(device="cuda").manual_seed(8)
+    a = (torch.rand(512, 16, device="cuda", generator=g) * 2 - 1).bfloat16()
+    b = (torch.rand(64, 16, device="cuda", generator=g) * 2 - 1).bfloat16()
+    bias = torch.linspace(-6, 6, 64, device="cuda")
+    z_ref = a.float() @ b.float().T + bias
+    z = torch.empty(512, 64, device="cuda", dtype=torch.bfloat16)
+    y = gemm(a, b, bias=bias, act="gelu", aux=z)
+    assert float(z_ref.abs().max()) > 6
+    torch.testing.assert_close(y, torch.nn.functional.gelu(z_ref), rtol=0, atol=2e-6)
+    one = torch.ones(512, 16, device="cuda").bfloat16()
+    w = (torch.rand(16, 64, device="cuda", generator=g) * 2 - 1).bfloat16()
+    dz = gemm(one, w, b_mn=True, act="gelu_grad", aux=z)
+    zf = z.float().requires_grad_(True)
+    torch.nn.functional.gelu(zf).backward((one.float() @ w.float()))
+    torch.testing.assert_close(dz, zf.grad, rtol=0, atol=2e-5)
+
+
+@pytest.mark.gpu
+def test_fused_feed_forward_matches_the_plain_sequence():
+    from autodrive_b200.ops.tc_linear import TcFeedForward
+    torch.manual_seed(4)
+    ref = nn.Sequential(nn.Linear(256, 1024), nn.GELU(), nn.Linear(1024, 256)).cuda()
+    fused = nn.Sequential(nn.Linear(256, 1024), nn.GELU(), nn.Linear(1024, 256)).cuda()
+    fused.load_state_dict(ref.state_dict())
+    tensorize(fused)
+    assert type(fused) is TcFeedForward and set(fused.state_dict()) == set(ref.state_dict())
+    x = torch.randn(3000, 256, device="cuda", requires_grad=True)
+    x2 = x.detach().clone().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y = fused(x)
+    y_ref = ref(x2)
+    assert y.dtype == torch.bfloat16
+    torch.testing.assert_close(y.float(), y_ref, rtol=3e-2, atol=3e-2)
+    w = torch.randn_like(y_ref)
+    (y.float() * w).sum().backward()
+    (y_ref * w).sum().backward()
+    pairs = [(x.grad, x2.grad)] + [(p.grad, q.grad) for p, q in zip(fused.parameters(), ref.parameters())]
+    for got, want in pairs:
+        rel = (got.float() - want).norm().item() / max(want.norm().item(), 1e-12)
+        assert rel < 3e-2, rel
+
+
+@pytest.mark.gpu
+def test_linear_gelu_pairs_fuse():
+    torch.manual_seed(6)
+    ref = nn.Sequential(nn.Linear(40, 136), nn.GELU(), nn.Linear(136, 64), nn.GELU(), nn.Linear(64, 8), nn.Tanh()).cuda()
+    import copy
+    net = copy.deepcopy(ref)
+    tensorize(net)
+    assert isinstance(net[1], nn.Identity) and net[0].act == "gelu" and net[2].act == "gelu"
+    x = torch.randn(500, 40, device="cuda")
+    torch.testing.assert_close(net(x), ref(x), rtol=3e-2, atol=3e-2)
+    net(x).square().sum().backward()
+    ref(x).square().sum().backward()
+    rel = (net[0].weight.grad - ref[0].weight.grad).norm() / ref[0].weight.grad.norm()
+    assert float(rel) < 3e-2, float(rel)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("act", [None, "tanh", "relu"])
 def test_tc_linear_forward_backward(act):
     torch.manual_seed(1)
