@@ -9,13 +9,14 @@
 //   dW       dW = dY^T X     A = dY (MN-major), B = X  (MN-major)
 //
 // Persistent kernel: one CTA per SM (at most one per work item) walks the
-// 128x128 output tiles (x split-K slices) in a static round-robin, N tiles
-// fastest so the CTAs running at the same time share A row blocks in L2.
+// 128 x BN output tiles (BN = 256 for wide outputs of long contractions with
+// A read K-major, 128 otherwise; x split-K slices) in a static round-robin, N tiles fastest so
+// the CTAs running at the same time share A row blocks in L2.
 // 320 threads:
 //   warp 0  TMA producer: 2-D tiled loads (128-byte swizzle) of the A and B
 //           tiles of each 64-deep K step into a 4-stage shared-memory ring
 //           that runs continuously across tiles;
-//   warp 1  allocates 256 TMEM columns (two 128-column fp32 accumulators);
+//   warp 1  allocates 2 BN TMEM columns (two BN-column fp32 accumulators);
 //           one lane issues 4 tcgen05.mma per K step into the accumulator of
 //           the current tile, commits each stage back to the producer and
 //           the finished accumulator to the epilogue;
@@ -50,14 +51,15 @@ namespace py = pybind11;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
+// Output tiles are 128 rows x BN columns, BN = 128 or 256 (a template
+// parameter; 256 halves the A re-reads and tile hand-offs on wide outputs).
+constexpr int kBM = 128, kBK = 64, kStages = 4;
 constexpr int kEpiWarps = 8;                    // two warps per TMEM lane quadrant
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr uint32_t kTileBytes = 128 * 128;        // one 128 x 64 bf16 operand tile
-constexpr uint32_t kStageBytes = 2 * kTileBytes;
+constexpr uint32_t kTileBytes = 128 * 128;        // the 128 x 64 bf16 A tile of one K step
 constexpr uint64_t kDrainNs = 200000000ull;       // 200 ms for in-flight copies / MMAs after a failure
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
-constexpr uint32_t kAccCols = 128;                // one fp32 accumulator: 128 lanes x 128 columns
+template <int BN> __host__ __device__ constexpr uint32_t stage_bytes() { return kTileBytes + (uint32_t)BN * 128u; }
+template <int BN> __host__ __device__ constexpr uint32_t smem_bytes() { return kStages * stage_bytes<BN>() + 1024 + 256; }
 
 struct GemmArgs {
   int M, N, K;
@@ -113,9 +115,9 @@ __device__ __forceinline__ float gelu_erf_grad(float z) {
 
 // Work item w -> (m0, n0, split slice z); N tiles fastest.
 struct TileCoord { int m0, n0, z; };
-__device__ __forceinline__ TileCoord tile_of(int w, int tiles_n, int tiles_m) {
+__device__ __forceinline__ TileCoord tile_of(int w, int tiles_n, int tiles_m, int bn) {
   TileCoord t;
-  t.n0 = (w % tiles_n) * kBN;
+  t.n0 = (w % tiles_n) * bn;
   const int r = w / tiles_n;
   t.m0 = (r % tiles_m) * kBM;
   t.z = r / tiles_m;
@@ -229,9 +231,11 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& g, float (&v)[32], i
   }
 }
 
-template <bool A_MN, bool B_MN, bool GELU>
+template <bool A_MN, bool B_MN, bool GELU, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, const GemmArgs g) {
+  constexpr uint32_t kStageBytes = stage_bytes<BN>();
+  constexpr uint32_t kAccCols = BN;               // one fp32 accumulator: 128 lanes x BN columns
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* misc = smem + kStages * kStageBytes;
@@ -245,7 +249,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
   volatile int* fail = s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_n = (g.N + kBN - 1) / kBN, tiles_m = (g.M + kBM - 1) / kBM;
+  const int tiles_n = (g.N + BN - 1) / BN, tiles_m = (g.M + kBM - 1) / kBM;
   const int total = tiles_n * tiles_m * g.splits;
   const int KT_all = (g.K + kBK - 1) / kBK;
 
@@ -275,7 +279,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     // ---- TMA producer: one ring position per K step, across all tiles ----
     uint32_t it = 0;
     for (int w = blockIdx.x; w < total && !*fail; w += gridDim.x) {
-      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const TileCoord t = tile_of(w, tiles_n, tiles_m, BN);
       const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
       for (int kt = kb; kt < ke; ++kt, ++it) {
         const uint32_t s = it % kStages;
@@ -296,9 +300,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
         } else {
           tc::tma_load_2d(sa, &ta, k0, t.m0, full);
         }
-        if (B_MN) {
-          tc::tma_load_2d(sb, &tb, t.n0, k0, full);
-          tc::tma_load_2d(sb + kTileBytes / 2, &tb, t.n0 + 64, k0, full);
+        if (B_MN) {   // BN / 64 boxes of 64 N columns x 64 K rows
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(sb + j * (kTileBytes / 2), &tb, t.n0 + 64 * j, k0, full);
         } else {
           tc::tma_load_2d(sb, &tb, k0, t.n0, full);
         }
@@ -312,11 +316,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer: tile lt accumulates into TMEM columns (lt & 1) * 128 ----
-    const uint32_t id = tc::idesc_bf16(kBM, kBN, A_MN, B_MN);
+    const uint32_t id = tc::idesc_bf16(kBM, BN, A_MN, B_MN);
     uint32_t it = 0;
     int lt = 0;
     for (int w = blockIdx.x; w < total && !*fail; w += gridDim.x, ++lt) {
-      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const TileCoord t = tile_of(w, tiles_n, tiles_m, BN);
       const int kb = t.z * g.k_steps, ke = min(KT_all, kb + g.k_steps);
       const int acc = lt & 1;
       if (lt >= 2 && !tc::mbar_wait(tempty0 + 8 * acc, ((lt >> 1) - 1) & 1, g.wait_ns)) {
@@ -341,7 +345,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
 #pragma unroll
         for (int ks = 0; ks < kBK / 16; ++ks) {
           const uint64_t da = A_MN ? tc::desc_mnmajor(sa, kBK, ks) : tc::desc_kmajor(sa, kBM, ks);
-          const uint64_t db = B_MN ? tc::desc_mnmajor(sb, kBK, ks) : tc::desc_kmajor(sb, kBN, ks);
+          const uint64_t db = B_MN ? tc::desc_mnmajor(sb, kBK, ks) : tc::desc_kmajor(sb, BN, ks);
           tc::mma_bf16(d, da, db, id, kt > kb || ks > 0);
         }
         tc::mma_commit(empty0 + 8 * s);   // stage free once these MMAs have read it
@@ -363,10 +367,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
     // MMA warp before the stores
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    constexpr int kChunks = kBN / 32 / 2;  // chunks per warp
+    constexpr int kChunks = BN / 32 / 2;  // chunks per warp (2 or 4)
+    static_assert(kChunks % 2 == 0, "epilogue reads chunks in pairs");
     int lt = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++lt) {
-      const TileCoord t = tile_of(w, tiles_n, tiles_m);
+      const TileCoord t = tile_of(w, tiles_n, tiles_m, BN);
       const int acc = lt & 1;
       const bool got = tc::mbar_wait(tfull0 + 8 * acc, (lt >> 1) & 1, g.wait_ns);
       if (!got) {
@@ -376,18 +381,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ C
       if (!got || *fail) break;
       tc::tc_fence_after();
       const int row = t.m0 + 32 * q + lane;
-      float v[kChunks][32];
       const uint32_t base = tmem + acc * kAccCols + ((uint32_t)(32 * q) << 16);
+      // two chunks in flight at a time (a 256-wide tile's four would spill);
+      // the accumulator is handed back once its last chunks are read
 #pragma unroll
-      for (int k = 0; k < kChunks; ++k) tc::tmem_ld32_issue(base + 32 * (2 * k + half), v[k]);
-      tc::tmem_ld_wait();
+      for (int k0 = 0; k0 < kChunks; k0 += 2) {
+        float v[2][32];
 #pragma unroll
-      for (int k = 0; k < kChunks; ++k) tc::tmem_regs_ready(v[k]);
-      tc::tc_fence_before();
-      tc::mbar_arrive(tempty0 + 8 * acc);   // accumulator read out: the MMA warp may reuse it
-      if (row < g.M) {
+        for (int k = 0; k < 2; ++k) tc::tmem_ld32_issue(base + 32 * (2 * (k0 + k) + half), v[k]);
+        tc::tmem_ld_wait();
 #pragma unroll
-        for (int k = 0; k < kChunks; ++k) store_chunk<GELU>(g, v[k], row, t.n0 + 32 * (2 * k + half), t.z);
+        for (int k = 0; k < 2; ++k) tc::tmem_regs_ready(v[k]);
+        if (k0 + 2 >= kChunks) {
+          tc::tc_fence_before();
+          tc::mbar_arrive(tempty0 + 8 * acc);   // accumulator read out: the MMA warp may reuse it
+        }
+        if (row < g.M) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            store_chunk<GELU>(g, v[k], row, t.n0 + 32 * (2 * (k0 + k) + half), t.z);
+        }
       }
     }
   }
@@ -414,19 +427,20 @@ int sm_count() {
   return counts[dev];
 }
 
-template <bool A_MN, bool B_MN, bool GELU = false>
+template <bool A_MN, bool B_MN, bool GELU, int BN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
+  constexpr uint32_t kSmemBytes = smem_bytes<BN>();
   static bool configured = false;
   if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN, GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN, GELU, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
     configured = true;
   }
   // persistent: one CTA per SM, never more CTAs than work items
-  const int64_t total = (int64_t)((g.N + kBN - 1) / kBN) * ((g.M + kBM - 1) / kBM) * g.splits;
+  const int64_t total = (int64_t)((g.N + BN - 1) / BN) * ((g.M + kBM - 1) / kBM) * g.splits;
   TORCH_CHECK(total < (1ll << 31), "tc_gemm: too many output tiles");
   const int grid = (int)std::min<int64_t>(total, sm_count());
-  tc_gemm_kernel<A_MN, B_MN, GELU><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
+  tc_gemm_kernel<A_MN, B_MN, GELU, BN><<<grid, kThreads, kSmemBytes, st>>>(ta, tb, g);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "tc_gemm launch failed");
 }
 
@@ -514,13 +528,18 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
   }
   // A: K-major [M][K] -> box 64 K x 128 rows; MN-major [K][M] -> box 64 M x 64 K rows
   const CUtensorMap ta = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), kBK) : make_map(a.data_ptr(), M, K, a.stride(0), kBM);
-  const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), kBK) : make_map(b.data_ptr(), N, K, b.stride(0), kBN);
+  // 256-wide output tiles where the main loop dominates: wide outputs, A read
+  // K-major, long contractions (K >= 512), plain epilogue. On the K = 256
+  // layers the output stores bound the kernel and 128-wide tiles are as fast;
+  // the GELU epilogue is slower with 256-wide tiles.
+  const int bn = (!a_mn && N >= 256 && K >= 512 && act < 4) ? 256 : 128;
+  const CUtensorMap tb = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), kBK) : make_map(b.data_ptr(), N, K, b.stride(0), bn);
   auto st = c10::cuda::getCurrentCUDAStream().stream();
   // Few output tiles over a long contraction (weight gradients: K = tokens)
   // leave most SMs idle; split K into about two work items per SM, each over
   // at least 8 K steps, into fp32 partials that are summed afterwards.
   const int64_t KT = (K + kBK - 1) / kBK;
-  const int64_t tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+  const int64_t tiles = ((N + bn - 1) / bn) * ((M + kBM - 1) / kBM);
   int64_t splits = 1;
   if (tiles < 148 && KT >= 16) splits = std::min<int64_t>(KT / 8, (296 + tiles - 1) / tiles);
   g.k_steps = (int)((KT + splits - 1) / splits);
@@ -555,12 +574,15 @@ void tc_gemm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, torch::Tens
     g.aux_out = nullptr;
     g.aux_in = nullptr;
   }
-  if (gelu_fused && !a_mn && !b_mn) launch<false, false, true>(ta, tb, g, st);
-  else if (gelu_fused) launch<false, true, true>(ta, tb, g, st);
-  else if (!a_mn && !b_mn) launch<false, false>(ta, tb, g, st);
-  else if (!a_mn && b_mn) launch<false, true>(ta, tb, g, st);
-  else if (a_mn && !b_mn) launch<true, false>(ta, tb, g, st);
-  else launch<true, true>(ta, tb, g, st);
+  if (bn == 256) {
+    if (!b_mn) launch<false, false, false, 256>(ta, tb, g, st);
+    else launch<false, true, false, 256>(ta, tb, g, st);
+  } else if (gelu_fused && !a_mn && !b_mn) launch<false, false, true, 128>(ta, tb, g, st);
+  else if (gelu_fused) launch<false, true, true, 128>(ta, tb, g, st);
+  else if (!a_mn && !b_mn) launch<false, false, false, 128>(ta, tb, g, st);
+  else if (!a_mn && b_mn) launch<false, true, false, 128>(ta, tb, g, st);
+  else if (a_mn && !b_mn) launch<true, false, false, 128>(ta, tb, g, st);
+  else launch<true, true, false, 128>(ta, tb, g, st);
   if (gelu && !gelu_fused) {
     torch::Tensor z = partial;
     if (bias && bias->defined()) z += *bias;

@@ -29,7 +29,9 @@ def test_tc_linear_cpu_matches_linear():
 @pytest.mark.parametrize("mnk", [(128, 128, 64), (300, 200, 152), (1000, 72, 1024), (64, 520, 40),
                                  (256, 136, 40000),    # split-K
                                  (4096, 1024, 256),    # 256 tiles: two per persistent CTA
-                                 (20000, 384, 136)])   # 471 tiles: both accumulators reused
+                                 (20000, 384, 136),    # 471 tiles: both accumulators reused
+                                 (3000, 520, 1024),    # 256-wide tiles (K >= 512), ragged N
+                                 (700, 256, 600)])     # 256-wide tiles, ragged K
 def test_gemm_majors_match_fp32(a_mn, b_mn, mnk):
     m, n, k = mnk
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
