@@ -13,6 +13,7 @@ world's alliance scores and per-robot FUEL acquisitions at fixed checkpoints.
     python -m autodrive_b200.bench.match_outcomes run --impl reference --device cpu --seeds 827104 \
         --envs 4 --ticks 8000 --output ref.json
     python -m autodrive_b200.bench.match_outcomes summarize outcomes.json ref.json
+    python -m autodrive_b200.bench.match_outcomes compare --ours outcomes.json --reference ref*.json
 
 `--impl reference` imports the unmodified reference package installed in
 ``baseline/_ref`` and drives it through its public ``TensorThreeVsThreeEnv``
@@ -128,6 +129,65 @@ def summarize(paths, tick=None) -> dict:
     return result
 
 
+def _t975(dof: float) -> float:
+    table = {1: 12.706, 2: 4.303, 3: 3.182, 4: 2.776, 5: 2.571, 6: 2.447, 7: 2.365, 8: 2.306, 9: 2.262,
+             10: 2.228, 11: 2.201, 12: 2.179, 13: 2.160, 14: 2.145, 15: 2.131, 20: 2.086, 25: 2.060, 30: 2.042}
+    if dof > 30:
+        return 1.96
+    return table[max(k for k in table if k <= max(1, int(dof)))]
+
+
+def _pooled(paths, tick):
+    """Per-world red scores and per-robot acquisitions of all seeds of `paths` at `tick`."""
+    score, acq = [], [[] for _ in range(3)]
+    for path in paths:
+        with open(path) as f:
+            for r in json.load(f)["seeds"].values():
+                cp = next((c for c in r["checkpoints"] if c["tick"] == tick), None)
+                if cp is None:
+                    continue
+                for world_score, world_acq in zip(cp["score_by_team"], cp["acquisitions_by_robot"]):
+                    score.append(world_score[0])
+                    for k in range(3):
+                        acq[k].append(world_acq[k])
+    return score, acq
+
+
+def _welch(a, b) -> dict:
+    """Difference of means a - b with a Welch 95 % interval (Welch-Satterthwaite dof)."""
+    na, nb = len(a), len(b)
+    ma, mb = sum(a) / na, sum(b) / nb
+    va = sum((x - ma) ** 2 for x in a) / max(1, na - 1)
+    vb = sum((x - mb) ** 2 for x in b) / max(1, nb - 1)
+    se2 = va / na + vb / nb
+    if se2 == 0:
+        return {"difference": ma - mb, "ci95": [ma - mb, ma - mb], "dof": None}
+    dof = se2 ** 2 / ((va / na) ** 2 / max(1, na - 1) + (vb / nb) ** 2 / max(1, nb - 1) + 1e-300)
+    half = _t975(dof) * math.sqrt(se2)
+    return {"difference": ma - mb, "ci95": [ma - mb - half, ma - mb + half], "dof": dof}
+
+
+def compare(ours, reference, tick=None) -> dict:
+    """Our simulator's outcome files against the reference's at one checkpoint
+    tick (default: the last tick every seed of both sides reached): pooled
+    means with 95 % intervals and the Welch difference of means for the red
+    score per world and each offense robot's acquisitions."""
+    def reached(paths):
+        ticks = []
+        for path in paths:
+            with open(path) as f:
+                ticks += [r["checkpoints"][-1]["tick"] for r in json.load(f)["seeds"].values() if r["checkpoints"]]
+        return min(ticks) if ticks else 0
+    at = tick or min(reached(ours), reached(reference))
+    (so, ao), (sr, ar) = _pooled(ours, at), _pooled(reference, at)
+    if not so or not sr:
+        raise ValueError(f"no worlds reached tick {at} on both sides")
+    return {"tick": at,
+            "red_score_per_world": {"ours": _mean_ci(so), "reference": _mean_ci(sr), "ours_minus_reference": _welch(so, sr)},
+            "acquisitions_per_robot": [{"ours": _mean_ci(ao[k]), "reference": _mean_ci(ar[k]),
+                                        "ours_minus_reference": _welch(ao[k], ar[k])} for k in range(3)]}
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = p.add_subparsers(dest="cmd")
@@ -146,9 +206,15 @@ def main():
     s = sub.add_parser("summarize")
     s.add_argument("files", nargs="+")
     s.add_argument("--tick", type=int)
+    c = sub.add_parser("compare")
+    c.add_argument("--ours", nargs="+", required=True)
+    c.add_argument("--reference", nargs="+", required=True)
+    c.add_argument("--tick", type=int)
     args = p.parse_args()
     if args.cmd == "summarize":
         print(json.dumps(summarize(args.files, args.tick), indent=1))
+    elif args.cmd == "compare":
+        print(json.dumps(compare(args.ours, args.reference, args.tick), indent=1))
     else:
         if args.cmd is None:
             p.error("choose run or summarize")
