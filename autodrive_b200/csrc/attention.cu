@@ -286,14 +286,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const int kvalid = Lk - kb * kBlk;
       float mb = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32_issue(tmem + lane + 32 * c, v);
+      for (int c0 = 0; c0 < 4; c0 += 2) {   // two 32-column loads in flight
+        float v[2][32];
+        tc::tmem_ld32_issue(tmem + lane + 32 * c0, v[0]);
+        tc::tmem_ld32_issue(tmem + lane + 32 * c0 + 32, v[1]);
         tc::tmem_ld_wait();
-        tc::tmem_regs_ready(v);
+        tc::tmem_regs_ready(v[0]);
+        tc::tmem_regs_ready(v[1]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i < kvalid) mb = fmaxf(mb, v[i] * a.scale_log2);
+        for (int i = 0; i < 64; ++i)
+          if (32 * c0 + i < kvalid) mb = fmaxf(mb, v[i >> 5][i & 31] * a.scale_log2);
       }
       const float mn = fmaxf(m, mb);
       const float alpha = exp2f(m - mn);   // 0 on the first block (m = -inf)
@@ -312,18 +314,23 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32_issue(tmem + lane + 32 * c, v);
+      for (int c0 = 0; c0 < 4; c0 += 2) {
+        float v[2][32];
+        tc::tmem_ld32_issue(tmem + lane + 32 * c0, v[0]);
+        tc::tmem_ld32_issue(tmem + lane + 32 * c0 + 32, v[1]);
         tc::tmem_ld_wait();
-        tc::tmem_regs_ready(v);
+        tc::tmem_regs_ready(v[0]);
+        tc::tmem_regs_ready(v[1]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p = (32 * c + i < kvalid) ? exp2f(v[i] * a.scale_log2 - mn) : 0.f;
-          v[i] = p;
-          sum += p;
+        for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p = (32 * (c0 + h2) + i < kvalid) ? exp2f(v[h2][i] * a.scale_log2 - mn) : 0.f;
+            v[h2][i] = p;
+            sum += p;
+          }
+          store_row32(smem + kFwdP, t, 32 * (c0 + h2), v[h2]);
         }
-        store_row32(smem + kFwdP, t, 32 * c, v);
       }
       l = l * alpha + sum;
       m = mn;
@@ -457,12 +464,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     bool ok = true;
     for (int p = 0; p < npairs && ok; ++p) {
       const int kb = p / nbq, qb = p % nbq, r = p & 1, rk = kb & 1;
-      if (p > 0) {   // the previous pair's second group read Q / dO slot (p + 1) & 1 and, at a key block's end, K / V
-        if (!(ok = wait_or_fail(g2, (p - 1) & 1, a, s_fail, kBitBwd))) break;
-        tc::tc_fence_after();
+      if (p == 0) {
+        if (npairs > 1) load_q(1);
+        if (nbk > 1) load_kv(1);
       }
-      if (p + 1 < npairs) load_q(p + 1);
-      if (qb == 0 && kb + 1 < nbk) load_kv(kb + 1);
       if (!(ok = wait_or_fail(bar_q0 + 8u * r, (p >> 1) & 1, a, s_fail, kBitBwd))) break;
       pending &= ~(1u << r);
       parity ^= 1u << r;
@@ -480,6 +485,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         tc::mma_bf16(tmem + 128, tc::desc_kmajor(do_img, kBlk, ks), tc::desc_kmajor(v_img, kBlk, ks), id_sq, ks > 0);
       }
       tc::mma_commit(g1);
+      // S / dP of this pair are queued behind the previous pair's gradient MMAs;
+      // once those finish, slot (p + 1) & 1 (and at a key block's start the K / V
+      // slot of the key block after next) is free for the next loads
+      if (p > 0) {
+        if (!(ok = wait_or_fail(g2, (p - 1) & 1, a, s_fail, kBitBwd))) break;
+        tc::tc_fence_after();
+        if (p + 1 < npairs) load_q(p + 1);
+        if (qb == 0 && kb + 1 < nbk) load_kv(kb + 1);
+      }
       if (!(ok = wait_or_fail(ds_full, p & 1, a, s_fail, kBitBwd))) break;
       tc::tc_fence_after();
 #pragma unroll
