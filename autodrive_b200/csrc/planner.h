@@ -22,6 +22,7 @@ namespace ad {
 
 struct PlanScratch {
   uint8_t* blocked;   // [nx*ny]
+  uint16_t* moves;    // [nx*ny]: per cell, bit k = move k allowed (k < 8), bit 8 = on a bump, bit 9 = blocked
   float* value;       // [nx*ny]
   float* path;        // [plan_lattice_cap * 2]: lattice route of the greedy descent
   float* tmp;         // [4 + plan_lattice_cap * 2]: resolved goal, then the simplified corners
@@ -270,7 +271,27 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   SERIAL_END
   BARRIER();
   const int gcell = cell_index(sp, ps.misc[2], ps.misc[3]);
-  PAR_FOR(c, nc) { ps.value[c] = c == gcell ? 0.f : 1.e6f; }
+  const int dxs[8] = {1, -1, 0, 0, 1, 1, -1, -1};
+  const int dys[8] = {0, 0, 1, -1, 1, -1, 1, -1};
+  // per-cell move table, built once per plan for the sweeps: a move is
+  // allowed into an in-bounds free cell, diagonally only when both corner
+  // cells are free; a blocked target would never lower a value (it keeps
+  // 1e6 while every value starts at 1e6 and only decreases), so leaving it
+  // out changes nothing
+  PAR_FOR(c, nc) {
+    ps.value[c] = c == gcell ? 0.f : 1.e6f;
+    const int ix = c / ny, iy = c % ny;
+    unsigned m = ps.blocked[c] ? 512u : 0u;
+    for (int k = 0; k < 8; ++k) {
+      const int jx = ix + dxs[k], jy = iy + dys[k];
+      if (jx < 0 || jx >= nx || jy < 0 || jy >= ny) continue;
+      if (ps.blocked[cell_index(sp, jx, jy)]) continue;
+      if (k >= 4 && (ps.blocked[cell_index(sp, jx, iy)] || ps.blocked[cell_index(sp, ix, jy)])) continue;
+      m |= 1u << k;
+    }
+    if (cell_on_bump(sp, cell_x(sp, ix), cell_y(sp, iy))) m |= 256u;
+    ps.moves[c] = (uint16_t)m;
+  }
   BARRIER();
   // Bellman value iteration by alternating directional line sweeps (the fast
   // sweeping method, Zhao, Math. Comp. 2005): sweep k walks every grid line in
@@ -281,36 +302,47 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   // Jacobi solution) once one sweep changes no cell, in any update order: the
   // GPU (one line per thread, racing reads of neighbouring lines) and the
   // serial host twin return the same values.
-  const int dxs[8] = {1, -1, 0, 0, 1, 1, -1, -1};
-  const int dys[8] = {0, 0, 1, -1, 1, -1, 1, -1};
   volatile float* vv = ps.value;
+  int offs[8];   // cell index step of move k
+  for (int k = 0; k < 8; ++k) offs[k] = dxs[k] * ny + dys[k];
   int sweeps_run = 0;
   bool converged = false;
   for (int sweep = 0; sweep < sp.plan_sweeps; ++sweep) {
     const int dir = sweep & 3;
     const bool along_x = dir < 2;
     const int lines = along_x ? ny : nx, len = along_x ? nx : ny;
+    // the neighbour just behind in sweep order was updated by this thread
+    // in the previous step: its value comes from a register
+    const int behind = along_x ? ((dir & 1) ? 0 : 1) : ((dir & 1) ? 2 : 3);
     int changed = 0;
     PAR_FOR(line, lines) {
+      float prev = 1.e6f;
       for (int step = 0; step < len; ++step) {
         const int t = (dir & 1) ? len - 1 - step : step;
         const int ix = along_x ? t : line, iy = along_x ? line : t;
         const int c = cell_index(sp, ix, iy);
-        if (ps.blocked[c]) continue;
-        const float bc = cell_on_bump(sp, cell_x(sp, ix), cell_y(sp, iy)) ? 1.f + sp.bump_cost : 1.f;
+        const unsigned m = ps.moves[c];
+        if (m & 512u) {   // blocked: never updated, holds 1e6
+          prev = 1.e6f;
+          continue;
+        }
+        const float bc = (m & 256u) ? 1.f + sp.bump_cost : 1.f;
         const float wd = mul_rn(1.41421356237f, bc);
         const float cur = vv[c];
         float best = cur;
+#if defined(__CUDA_ARCH__)
+#pragma unroll
+#endif
         for (int k = 0; k < 8; ++k) {
-          const int jx = ix + dxs[k], jy = iy + dys[k];
-          if (jx < 0 || jx >= nx || jy < 0 || jy >= ny) continue;
-          if (k >= 4 && (ps.blocked[cell_index(sp, jx, iy)] || ps.blocked[cell_index(sp, ix, jy)])) continue;
-          best = fminf(best, vv[cell_index(sp, jx, jy)] + (k >= 4 ? wd : bc));
+          if (!((m >> k) & 1u)) continue;
+          const float v = k == behind ? prev : vv[c + offs[k]];
+          best = fminf(best, v + (k >= 4 ? wd : bc));
         }
         if (best < cur) {
           vv[c] = best;
           changed = 1;
         }
+        prev = best;
       }
     }
 #if defined(__CUDA_ARCH__)

@@ -445,7 +445,8 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
   ps.path = f + nc;
   ps.tmp = ps.path + cap * 2;
   ps.misc = reinterpret_cast<int*>(ps.tmp + cap * 2 + 4);
-  ps.blocked = reinterpret_cast<uint8_t*>(ps.misc + 8);
+  ps.moves = reinterpret_cast<uint16_t*>(ps.misc + 8);
+  ps.blocked = reinterpret_cast<uint8_t*>(ps.moves + nc);
   __shared__ PlanRequest q;
   __shared__ unsigned long long s_best[2];
   ps.best = s_best;
@@ -508,7 +509,7 @@ std::vector<unsigned long long> sense_profile_read() {
 
 size_t plan_smem_bytes(const SimParams& sp) {
   const int nc = sp.plan_nx * sp.plan_ny;
-  return (size_t)(nc + plan_lattice_cap(sp) * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc + 16;
+  return (size_t)(nc + plan_lattice_cap(sp) * 4 + 4) * sizeof(float) + 8 * sizeof(int) + (size_t)nc * 3 + 16;
 }
 
 void validate_params(const SimParams& sp) {
@@ -625,9 +626,11 @@ void host_plan(World w, const SimParams& sp, int force) {
     const int cap = plan_lattice_cap(sp);
     std::vector<float> fbuf(nc + cap * 4 + 4);
     std::vector<uint8_t> blocked(nc);
+    std::vector<uint16_t> moves(nc);
     int misc[8];
     unsigned long long best[2];
-    PlanScratch ps{blocked.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc, best};
+    PlanScratch ps{blocked.data(), moves.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc,
+                   best};
     for (int row = b; row < end; ++row) {
       const int e = row / sp.R, r = row % sp.R;
       if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;
