@@ -77,6 +77,7 @@ def stages(args):
         ext = require_extension()
         ext.phase_profile_read()
         ext.sense_profile_read()
+        ext.plan_profile_read()
         ext.phase_profile_enable(True)
         for _ in range(args.ticks):
             sim.control(env._actions_buf)
@@ -87,6 +88,10 @@ def stages(args):
         ext.phase_profile_enable(False)
         cyc = ext.phase_profile_read()
         scyc = ext.sense_profile_read()
+        pcyc = ext.plan_profile_read()
+        pnames = ("occupancy_grid", "endpoint_projection", "move_table_init", "sweeps", "greedy_descent",
+                  "line_of_sight", "smoothing_resample", "speed_profile")
+        plan_phases = {n: round(c / max(1, sum(pcyc)), 4) for n, c in zip(pnames, pcyc)}
         snames = ("load", "lens_visibility", "lens_geometry_sort", "lens_depth_buffer", "lens_objects",
                   "stereo_fusion", "packing", "association")
         sense_phases = {n: round(c / max(1, sum(scyc)), 4) for n, c in zip(snames, scyc)}
@@ -108,6 +113,7 @@ def stages(args):
     print(json.dumps({"mode": "stages", "envs": args.envs, "ticks": args.ticks, "actions": args.actions,
                       "awake_fuel_per_world": awake, "planner_sweeps": sweep_stats, "phase_share": phases,
                       "sense_phase_share": sense_phases if args.phases else None,
+                      "plan_phase_share": plan_phases if args.phases else None,
                       "ms_per_tick": per_tick, "env_ticks_per_s": args.envs / (total / 1e3),
                       "threads": sim.threads}))
 

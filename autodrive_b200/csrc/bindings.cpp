@@ -226,6 +226,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         for (int j = 0; j < n; ++j) out[j] = (int64_t)order[j];
         return out;
       }, "stable ascending order of keys in [-pi, pi] by the sensor stage's rank sort (host)");
+  m.def("plan_profile_read", &plan_profile_read,
+        "read and reset the plan kernel's per-phase cycle counters (grid, endpoints, move table, sweeps, "
+        "descent, line of sight, smoothing, speed profile)");
   m.def("sense_profile_read", &sense_profile_read,
         "read and reset the sense kernel's 8 per-phase cycle totals (summed over rows; counted while the "
         "phase profile is enabled): load, lens visibility, lens geometry+sort, lens depth buffer, lens "

@@ -20,6 +20,23 @@
 
 namespace ad {
 
+// Opt-in per-phase cycle accounting of a plan (sim_bench --phases): thread 0
+// adds the clock64() time since the previous mark to bucket k; the marks sit
+// after CTA barriers (or inside the final serial section, which thread 0 runs).
+constexpr int kPlanPhases = 8;
+#if defined(__CUDA_ARCH__)
+#define PLAN_MARK(ps, k)                                           \
+  do {                                                             \
+    if ((ps).prof && threadIdx.x == 0) {                           \
+      const unsigned long long t_ = clock64();                     \
+      (ps).prof[(k)] += t_ - (ps).prof[kPlanPhases];               \
+      (ps).prof[kPlanPhases] = t_;                                 \
+    }                                                              \
+  } while (0)
+#else
+#define PLAN_MARK(ps, k) ((void)0)
+#endif
+
 struct PlanScratch {
   uint8_t* blocked;   // [nx*ny]
   uint16_t* moves;    // [nx*ny]: per cell, bit k = move k allowed (k < 8), bit 8 = on a bump, bit 9 = blocked
@@ -28,6 +45,7 @@ struct PlanScratch {
   float* tmp;         // [4 + plan_lattice_cap * 2]: resolved goal, then the simplified corners
   int* misc;          // [8]
   unsigned long long* best;  // [2] packed endpoint-projection minima
+  unsigned long long* prof;  // [kPlanPhases + 1] cycle buckets and the last mark, or null
 };
 
 // Lattice points the descent may walk: four times the grid's half perimeter
@@ -220,6 +238,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     ps.blocked[c] = b ? 1 : 0;
   }
   BARRIER();
+  PLAN_MARK(ps, 0);   // occupancy grid
   // project blocked endpoints to the nearest free cell: a block-wide minimum
   // of packed (squared distance, cell index) keys, i.e. the nearest free cell
   // with ties to the lower index (the serial scan's choice)
@@ -270,6 +289,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   ps.tmp[1] = pts[3];
   SERIAL_END
   BARRIER();
+  PLAN_MARK(ps, 1);   // endpoint projection
   const int gcell = cell_index(sp, ps.misc[2], ps.misc[3]);
   const int dxs[8] = {1, -1, 0, 0, 1, 1, -1, -1};
   const int dys[8] = {0, 0, 1, -1, 1, -1, 1, -1};
@@ -293,56 +313,75 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     ps.moves[c] = (uint16_t)m;
   }
   BARRIER();
-  // Bellman value iteration by alternating directional line sweeps (the fast
-  // sweeping method, Zhao, Math. Comp. 2005): sweep k walks every grid line in
-  // direction k % 4 (+x, -x, +y, -y) and updates its cells in place, so a value
-  // crosses a whole line in one sweep instead of one cell per Jacobi sweep.
-  // Values only decrease and each is the cost of an actual path, so the
-  // iteration stops at the unique fixed point v(c) = min_k v(n_k) + w_k (the
-  // Jacobi solution) once one sweep changes no cell, in any update order: the
-  // GPU (one line per thread, racing reads of neighbouring lines) and the
-  // serial host twin return the same values.
+  PLAN_MARK(ps, 2);   // move table, value initialisation
+  // Bellman value iteration by directional line sweeps (the fast sweeping
+  // method, Zhao, Math. Comp. 2005): a line sweep walks one grid line and
+  // updates its cells in place, so a value crosses a whole line in one sweep
+  // instead of one cell per Jacobi sweep. Pass k runs, at the same time, every
+  // row (x line, nx cells) in direction +x (k even) or -x (k odd) and every
+  // column (y line, ny cells) in direction +y and then -y: the rows are about
+  // twice as long as the columns, so the two thread groups finish together.
+  // Values only decrease (on the GPU a cell updated by its row and its column
+  // takes the smaller value through an atomic minimum) and each is the cost of
+  // an actual path, so the iteration stops at the unique fixed point
+  // v(c) = min_k v(n_k) + w_k (the Jacobi solution) once a pass changes no
+  // cell, in any update order: the GPU (racing reads of neighbouring lines)
+  // and the serial host twin return the same values.
   volatile float* vv = ps.value;
   int offs[8];   // cell index step of move k
   for (int k = 0; k < 8; ++k) offs[k] = dxs[k] * ny + dys[k];
-  int sweeps_run = 0;
-  bool converged = false;
-  for (int sweep = 0; sweep < sp.plan_sweeps; ++sweep) {
-    const int dir = sweep & 3;
-    const bool along_x = dir < 2;
-    const int lines = along_x ? ny : nx, len = along_x ? nx : ny;
-    // the neighbour just behind in sweep order was updated by this thread
-    // in the previous step: its value comes from a register
-    const int behind = along_x ? ((dir & 1) ? 0 : 1) : ((dir & 1) ? 2 : 3);
+  auto sweep_line = [&](bool along_x, int line, bool reverse) -> int {
+    const int len = along_x ? nx : ny;
+    // the neighbour just behind in sweep order was updated by this thread in
+    // the previous step: its value comes from a register (a smaller value
+    // written there meanwhile by the crossing line only delays convergence)
+    const int behind = along_x ? (reverse ? 0 : 1) : (reverse ? 2 : 3);
     int changed = 0;
-    PAR_FOR(line, lines) {
-      float prev = 1.e6f;
-      for (int step = 0; step < len; ++step) {
-        const int t = (dir & 1) ? len - 1 - step : step;
-        const int ix = along_x ? t : line, iy = along_x ? line : t;
-        const int c = cell_index(sp, ix, iy);
-        const unsigned m = ps.moves[c];
-        if (m & 512u) {   // blocked: never updated, holds 1e6
-          prev = 1.e6f;
-          continue;
-        }
-        const float bc = (m & 256u) ? 1.f + sp.bump_cost : 1.f;
-        const float wd = mul_rn(1.41421356237f, bc);
-        const float cur = vv[c];
-        float best = cur;
+    float prev = 1.e6f;
+    for (int step = 0; step < len; ++step) {
+      const int t = reverse ? len - 1 - step : step;
+      const int ix = along_x ? t : line, iy = along_x ? line : t;
+      const int c = cell_index(sp, ix, iy);
+      const unsigned m = ps.moves[c];
+      if (m & 512u) {   // blocked: never updated, holds 1e6
+        prev = 1.e6f;
+        continue;
+      }
+      const float bc = (m & 256u) ? 1.f + sp.bump_cost : 1.f;
+      const float wd = mul_rn(1.41421356237f, bc);
+      const float cur = vv[c];
+      float best = cur;
 #if defined(__CUDA_ARCH__)
 #pragma unroll
 #endif
-        for (int k = 0; k < 8; ++k) {
-          if (!((m >> k) & 1u)) continue;
-          const float v = k == behind ? prev : vv[c + offs[k]];
-          best = fminf(best, v + (k >= 4 ? wd : bc));
-        }
-        if (best < cur) {
-          vv[c] = best;
-          changed = 1;
-        }
-        prev = best;
+      for (int k = 0; k < 8; ++k) {
+        if (!((m >> k) & 1u)) continue;
+        const float v = k == behind ? prev : vv[c + offs[k]];
+        best = fminf(best, v + (k >= 4 ? wd : bc));
+      }
+      if (best < cur) {
+#if defined(__CUDA_ARCH__)
+        atomicMin(reinterpret_cast<int*>(ps.value) + c, __float_as_int(best));   // values are >= 0
+#else
+        ps.value[c] = best;
+#endif
+        changed = 1;
+      }
+      prev = best;
+    }
+    return changed;
+  };
+  int sweeps_run = 0;
+  bool converged = false;
+  for (int sweep = 0; sweep < sp.plan_sweeps; ++sweep) {
+    const bool reverse = (sweep & 1) != 0;
+    int changed = 0;
+    PAR_FOR(item, ny + nx) {
+      if (item < ny) {
+        changed |= sweep_line(true, item, reverse);
+      } else {
+        changed |= sweep_line(false, item - ny, false);
+        changed |= sweep_line(false, item - ny, true);
       }
     }
 #if defined(__CUDA_ARCH__)
@@ -356,8 +395,9 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
       break;
     }
   }
+  PLAN_MARK(ps, 3);   // value iteration sweeps
   SERIAL_BEGIN
-  // sweeps used; negative when the budget ran out before a sweep changed nothing
+  // passes used; negative when the budget ran out before a pass changed nothing
   w.p_sweeps[er] = converged ? sweeps_run : -sweeps_run;
   // greedy descent
   int px = ps.misc[0], py = ps.misc[1];
@@ -394,6 +434,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   ps.misc[6] = len;
   SERIAL_END
   BARRIER();
+  PLAN_MARK(ps, 4);   // greedy descent
   // line-of-sight simplification (PathPlanner): a lattice point is kept only
   // when the last kept point cannot see the point after it. Round by round:
   // every thread tests the sight line from the current anchor to one later
@@ -448,6 +489,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     SERIAL_END
     BARRIER();
   }
+  PLAN_MARK(ps, 5);   // line-of-sight simplification
   SERIAL_BEGIN
   const int m = ps.misc[7];
   // smoothed route: cubic Bezier corners with the longest handle (0.4, 0.28,
@@ -483,6 +525,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   }
   // a one-cell route from start==goal still counts as a single point
   w.p_len[er] = len > 1 ? kPathPoints : 1;
+  PLAN_MARK(ps, 6);   // smoothing and resampling
   // speed profile: curvature caps then backward braking envelope
   float* prof = w.p_profile + er * kPathPoints;
   const float mu = fmaxf(q.lat_mu, .1f), acc = fmaxf(q.accel, .2f), vcap = fmaxf(q.speed, .1f);
@@ -507,10 +550,15 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     if (k == L - 1) cap = 0.f;
     prof[k] = cap;
   }
-  for (int k = 0; k < kPathPoints; ++k) {
-    float best = kInf;
-    for (int j = k; j < L; ++j) best = fminf(best, sqrtf(prof[j] * prof[j] + 2.f * acc * fmaxf(station[j] - station[k], 0.f)));
-    ps.tmp[k] = best;
+  // backward braking envelope v_k = min over j >= k of sqrt(cap_j^2 + 2 a (s_j - s_k)),
+  // as the recursion v_k^2 = min(cap_k^2, v_{k+1}^2 + 2 a (s_{k+1} - s_k))
+  for (int k = L; k < kPathPoints; ++k) ps.tmp[k] = kInf;
+  float next2 = kInf;
+  for (int k = L - 1; k >= 0; --k) {
+    float v2 = prof[k] * prof[k];
+    if (k < L - 1) v2 = fminf(v2, next2 + 2.f * acc * fmaxf(station[k + 1] - station[k], 0.f));
+    next2 = v2;
+    ps.tmp[k] = sqrtf(v2);
   }
   for (int k = 0; k < kPathPoints; ++k) prof[k] = ps.tmp[k] < kInf ? ps.tmp[k] : vcap;
   w.p_progress[er] = 0.f;
@@ -520,6 +568,7 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   w.p_start[er * 2 + 1] = ps.path[1];
   w.p_heading[er] = heading;
   w.p_trench[er] = trench ? 1 : 0;
+  PLAN_MARK(ps, 7);   // speed profile and route state
   SERIAL_END
   BARRIER();
 }

@@ -381,6 +381,7 @@ __global__ void observe_kernel(World w, SimParams sp) {
 
 __device__ int g_prof_on = 0;
 __device__ unsigned long long g_prof[18];
+__device__ unsigned long long g_plan_prof[kPlanPhases];
 __device__ unsigned long long g_sense_prof[kSensePhases];
 
 __global__ void __launch_bounds__(256, 3) tick_kernel(World w, SimParams sp, uint32_t tick, int run_game) {
@@ -449,10 +450,21 @@ __global__ void plan_kernel(World w, SimParams sp, int force) {
   ps.blocked = reinterpret_cast<uint8_t*>(ps.moves + nc);
   __shared__ PlanRequest q;
   __shared__ unsigned long long s_best[2];
+  __shared__ unsigned long long s_prof[kPlanPhases + 1];
   ps.best = s_best;
-  if (threadIdx.x == 0) q = make_plan_request(w, sp, e, r);
+  const bool prof = g_prof_on != 0;
+  ps.prof = prof ? s_prof : nullptr;
+  if (threadIdx.x == 0) {
+    q = make_plan_request(w, sp, e, r);
+    if (prof) {
+      for (int k = 0; k < kPlanPhases; ++k) s_prof[k] = 0ull;
+      s_prof[kPlanPhases] = clock64();
+    }
+  }
   __syncthreads();
   plan_route(w, sp, e, r, q, ps);
+  if (prof && threadIdx.x == 0)
+    for (int k = 0; k < kPlanPhases; ++k) atomicAdd(&g_plan_prof[k], s_prof[k]);
 }
 
 // Fuel-only microbenchmark kernel: `ticks` ticks of robot + FUEL substeps
@@ -494,6 +506,16 @@ std::vector<unsigned long long> phase_profile_read() {
   check(cudaMemcpyFromSymbol(out.data(), g_prof, sizeof(unsigned long long) * 18), "phase profile read");
   std::vector<unsigned long long> zero(18, 0ull);
   check(cudaMemcpyToSymbol(g_prof, zero.data(), sizeof(unsigned long long) * 18), "phase profile reset");
+  return out;
+}
+
+std::vector<unsigned long long> plan_profile_read() {
+  std::vector<unsigned long long> out(kPlanPhases, 0ull);
+  check(cudaMemcpyFromSymbol(out.data(), g_plan_prof, sizeof(unsigned long long) * kPlanPhases),
+        "plan profile read");
+  std::vector<unsigned long long> zero(kPlanPhases, 0ull);
+  check(cudaMemcpyToSymbol(g_plan_prof, zero.data(), sizeof(unsigned long long) * kPlanPhases),
+        "plan profile reset");
   return out;
 }
 
@@ -630,7 +652,7 @@ void host_plan(World w, const SimParams& sp, int force) {
     int misc[8];
     unsigned long long best[2];
     PlanScratch ps{blocked.data(), moves.data(), fbuf.data(), fbuf.data() + nc, fbuf.data() + nc + cap * 2, misc,
-                   best};
+                   best, nullptr};
     for (int row = b; row < end; ++row) {
       const int e = row / sp.R, r = row % sp.R;
       if (!w.active[e] || sp.mode[r] == MODE_NONE) continue;

@@ -14,6 +14,7 @@ size_t tick_smem_bytes();
 void phase_profile_enable(bool on);
 std::vector<unsigned long long> phase_profile_read();
 std::vector<unsigned long long> sense_profile_read();
+std::vector<unsigned long long> plan_profile_read();
 size_t plan_smem_bytes(const SimParams& sp);
 size_t sense_smem_bytes(const SimParams& sp);
 void validate_params(const SimParams& sp);
