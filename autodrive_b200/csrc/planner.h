@@ -350,15 +350,23 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
       const float bc = (m & 256u) ? 1.f + sp.bump_cost : 1.f;
       const float wd = mul_rn(1.41421356237f, bc);
       const float cur = vv[c];
-      float best = cur;
+      // all eight candidates without branches: a move that is not allowed
+      // reads the cell itself and contributes +inf, so every load can issue
+      // at once; the minimum is the same as over the allowed moves alone
+      float cand[8];
 #if defined(__CUDA_ARCH__)
 #pragma unroll
 #endif
       for (int k = 0; k < 8; ++k) {
-        if (!((m >> k) & 1u)) continue;
-        const float v = k == behind ? prev : vv[c + offs[k]];
-        best = fminf(best, v + (k >= 4 ? wd : bc));
+        const bool ok = (m >> k) & 1u;
+        const float v = vv[ok ? c + offs[k] : c];
+        cand[k] = ok ? (k == behind ? prev : v) + (k >= 4 ? wd : bc) : kInf;
       }
+      float best = cur;
+#if defined(__CUDA_ARCH__)
+#pragma unroll
+#endif
+      for (int k = 0; k < 8; ++k) best = fminf(best, cand[k]);
       if (best < cur) {
 #if defined(__CUDA_ARCH__)
         atomicMin(reinterpret_cast<int*>(ps.value) + c, __float_as_int(best));   // values are >= 0
