@@ -51,6 +51,7 @@
 
 #include "tc_sm100.h"
 #include "tma_map.h"
+#include "smem_opt_in.h"
 
 namespace py = pybind11;
 
@@ -723,12 +724,9 @@ void attn_fwd(torch::Tensor q, int64_t q_col, torch::Tensor kv, int64_t k_col, i
   }
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   a.lse = lse.data_ptr<float>();
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmem) ==
-                    cudaSuccess, "attention: shared-memory attribute");
-    configured = true;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};
+  TORCH_CHECK(dynsmem::opt_in(attn_fwd_kernel, kFwdSmem, configured) == cudaSuccess,
+              "attention: shared-memory attribute");
   const int64_t nqb = (max_q + kBlk - 1) / kBlk;
   const int64_t blocks = samples * heads * nqb;
   TORCH_CHECK(blocks < (1ll << 31), "attention: too many query blocks");
@@ -783,12 +781,9 @@ void attn_bwd(torch::Tensor q, int64_t q_col, torch::Tensor kv, int64_t k_col, i
   }
   torch::Tensor dvec = torch::empty({heads, q.size(0)}, q.options().dtype(torch::kFloat32));
   a.dvec = dvec.data_ptr<float>();
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem) ==
-                    cudaSuccess, "attention: shared-memory attribute");
-    configured = true;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};
+  TORCH_CHECK(dynsmem::opt_in(attn_bwd_kernel, kBwdSmem, configured) == cudaSuccess,
+              "attention: shared-memory attribute");
   TORCH_CHECK(samples * heads < (1ll << 31), "attention: too many samples");
   const CUtensorMap tq = tma::bf16_sw128(q.data_ptr(), q.size(0), q.size(1), q.stride(0), kBlk);
   const CUtensorMap tkv = tma::bf16_sw128(kv.data_ptr(), kv.size(0), kv.size(1), kv.stride(0), kBlk);

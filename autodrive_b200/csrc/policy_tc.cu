@@ -35,6 +35,7 @@
 
 #include "common.h"
 #include "tc_sm100.h"
+#include "smem_opt_in.h"
 
 namespace py = pybind11;
 
@@ -654,13 +655,9 @@ void check_cuda(const torch::Tensor& t, const char* name) {
 template <bool TRAIN>
 void launch(const TcArgs& a, cudaStream_t st) {
   const uint32_t smem = smem_bytes(TRAIN);
-  static bool configured[2] = {false, false};
-  // attribute set once per process; device-agnostic for a single-architecture build
-  if (!configured[TRAIN]) {
-    TORCH_CHECK(cudaFuncSetAttribute(policy_tc_kernel<TRAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem) == cudaSuccess, "policy kernel shared-memory attribute");
-    configured[TRAIN] = true;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};   // one table per instantiation
+  TORCH_CHECK(dynsmem::opt_in(policy_tc_kernel<TRAIN>, smem, configured) == cudaSuccess,
+              "policy kernel shared-memory attribute");
   const int grid = (a.B + kRows - 1) / kRows;
   policy_tc_kernel<TRAIN><<<grid, kThreads, smem, st>>>(a);
   TORCH_CHECK(cudaGetLastError() == cudaSuccess, "policy_tc_kernel launch failed");

@@ -16,6 +16,7 @@
 // The host twins run the same __host__ __device__ routines serially per
 // environment across OpenMP threads; CPU tests and CPU training use them.
 #include "sim.h"
+#include "smem_opt_in.h"
 
 #include <algorithm>
 #include <cstdio>
@@ -550,12 +551,8 @@ void launch_control(const World& w, const SimParams& sp, const int32_t* actions,
 
 void launch_plan(const World& w, const SimParams& sp, int force, cudaStream_t st) {
   size_t smem = plan_smem_bytes(sp);
-  static size_t configured = 0;
-  if (smem > configured) {
-    check(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-          "plan_kernel smem attribute");
-    configured = smem;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};
+  check(dynsmem::opt_in(plan_kernel, smem, configured), "plan_kernel smem attribute");
   plan_kernel<<<sp.n * sp.R, 256, smem, st>>>(w, sp, force);
   check(cudaGetLastError(), "plan_kernel");
 }
@@ -564,28 +561,19 @@ size_t sense_smem_bytes(const SimParams& sp) { return sense_carve(nullptr, sp.P,
 
 void launch_sense(const World& w, const SimParams& sp, int force, cudaStream_t st) {
   const size_t smem = sense_smem_bytes(sp);
-  static size_t configured = 0;
-  if (smem > configured) {
-    check(cudaFuncSetAttribute(sense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-          "sense_kernel smem attribute");
-    configured = smem;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};
+  check(dynsmem::opt_in(sense_kernel, smem, configured), "sense_kernel smem attribute");
   sense_kernel<<<sp.n * sp.R, 256, smem, st>>>(w, sp, force);
   check(cudaGetLastError(), "sense_kernel");
 }
 
 void launch_tick(const World& w, const SimParams& sp, uint32_t tick, int run_game, int threads, cudaStream_t st) {
-  static bool configured = false;
+  static size_t tick_done[dynsmem::kMaxDevices] = {}, physics_done[dynsmem::kMaxDevices] = {},
+                perceive_done[dynsmem::kMaxDevices] = {};
   const size_t smem = tick_smem_bytes();
-  if (!configured) {
-    check(cudaFuncSetAttribute(tick_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-          "tick_kernel smem attribute");
-    check(cudaFuncSetAttribute(physics_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-          "physics_kernel smem attribute");
-    check(cudaFuncSetAttribute(perceive_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-          "perceive_kernel smem attribute");
-    configured = true;
-  }
+  check(dynsmem::opt_in(tick_kernel, smem, tick_done), "tick_kernel smem attribute");
+  check(dynsmem::opt_in(physics_kernel, smem, physics_done), "physics_kernel smem attribute");
+  check(dynsmem::opt_in(perceive_kernel, smem, perceive_done), "perceive_kernel smem attribute");
   if (run_game < 0) return;
   tick_kernel<<<sp.n, threads, smem, st>>>(w, sp, tick, run_game);
   check(cudaGetLastError(), "tick_kernel");

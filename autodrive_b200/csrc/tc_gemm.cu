@@ -46,6 +46,7 @@
 
 #include "tc_sm100.h"
 #include "tma_map.h"
+#include "smem_opt_in.h"
 
 namespace py = pybind11;
 
@@ -430,12 +431,9 @@ int sm_count() {
 template <bool A_MN, bool B_MN, bool GELU, int BN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
   constexpr uint32_t kSmemBytes = smem_bytes<BN>();
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<A_MN, B_MN, GELU, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kSmemBytes) == cudaSuccess, "tc_gemm shared-memory attribute");
-    configured = true;
-  }
+  static size_t configured[dynsmem::kMaxDevices] = {};
+  TORCH_CHECK(dynsmem::opt_in(tc_gemm_kernel<A_MN, B_MN, GELU, BN>, kSmemBytes, configured) == cudaSuccess,
+              "tc_gemm shared-memory attribute");
   // persistent: one CTA per SM, never more CTAs than work items
   const int64_t total = (int64_t)((g.N + BN - 1) / BN) * ((g.M + kBM - 1) / kBM) * g.splits;
   TORCH_CHECK(total < (1ll << 31), "tc_gemm: too many output tiles");
