@@ -80,6 +80,8 @@ struct SenseScratch {
   int32_t* misc;     // [64] warp scratch, profile counters, occluder counts
   float* occ;        // [4 (kMaxBoxes + kMaxRobots)] occluder table of the current lens
   uint8_t* occ_on;   // [kMaxBoxes + kMaxRobots] occluders that can touch its view
+  uint8_t* occ_list; // [kMaxBoxes + kMaxRobots] those occluders' indices, boxes first
+                     // (misc[kOccBoxes] boxes, misc[kOccAll] in all)
   // bucketed rank sort
   int32_t* sbucket;  // [kSortBuckets + 1] bucket counts, then bucket starts
   int16_t *stmp, *sslot;  // [2P] bucket-ordered elements, slot within the bucket
@@ -142,6 +144,7 @@ AD_HD size_t sense_carve(uint8_t* base, int P, SenseScratch* s) {
   t.sbucket = (int32_t*)take((kSortBuckets + 1) * 4);
   t.occ = (float*)take(4 * (kMaxBoxes + kMaxRobots) * 4);
   t.occ_on = take(kMaxBoxes + kMaxRobots);
+  t.occ_list = take(kMaxBoxes + kMaxRobots);
   t.stmp = (int16_t*)take(P2 * 2);
   t.sslot = (int16_t*)take(P2 * 2);
   if (s) *s = t;
@@ -156,6 +159,7 @@ constexpr int SM_WARP = 0;  // misc[0, 32): per-warp counts of a compaction
 // 3 lens depth buffer, 4 lens objects, 5 stereo fusion, 6 packing,
 // 7 association.
 constexpr int kSenseProfOn = 32, kSenseProfAcc = 34, kSensePhases = 8;
+constexpr int kOccBoxes = 56, kOccAll = 57;   // misc slots: lengths of the near-occluder list
 #if defined(__CUDA_ARCH__)
 #define SENSE_MARK(s, k)                                                                       \
   do {                                                                                         \
@@ -366,17 +370,42 @@ AD_HD void sense_build_occluders(const World& w, const SimParams& sp, SenseScrat
     }
     s.occ_on[k] = near ? 1 : 0;
   }
+  BARRIER();
+  // compact the near occluders (at most kMaxBoxes + kMaxRobots <= 32: one warp)
+  const int nall = sp.num_boxes + sp.R;
+#if defined(__CUDA_ARCH__)
+  if (threadIdx.x < 32) {
+    const int k = threadIdx.x;
+    const bool on = k < nall && s.occ_on[k];
+    const unsigned bal = __ballot_sync(0xffffffffu, on);
+    if (on) s.occ_list[__popc(bal & ((1u << k) - 1u))] = (uint8_t)k;
+    if (k == 0) {
+      s.misc[kOccBoxes] = __popc(bal & ((1u << sp.num_boxes) - 1u));
+      s.misc[kOccAll] = __popc(bal);
+    }
+  }
+#else
+  int m = 0, mb = 0;
+  for (int k = 0; k < nall; ++k) {
+    if (!s.occ_on[k]) continue;
+    s.occ_list[m++] = (uint8_t)k;
+    if (k < sp.num_boxes) mb = m;
+  }
+  s.misc[kOccBoxes] = mb;
+  s.misc[kOccAll] = m;
+#endif
 }
 
-// Segment lens -> lens + (dx, dy) blocked by a flagged box (ignoring the
-// first and last 2 % of the segment) or passing within a flagged robot's
-// radius (closest point strictly inside the 2..98 % window).
-AD_HD bool sense_occluded(const SenseScratch& s, float lx, float ly, float dx, float dy, int nbox, int nall) {
+// Segment lens -> lens + (dx, dy) blocked by a near box (ignoring the
+// first and last 2 % of the segment) or passing within a near robot's
+// radius (closest point strictly inside the 2..98 % window); the near
+// occluders are the compacted list of sense_build_occluders.
+AD_HD bool sense_occluded(const SenseScratch& s, float lx, float ly, float dx, float dy) {
   const bool par_x = fabsf(dx) < 1e-8f, par_y = fabsf(dy) < 1e-8f;
   const float ix = par_x ? 0.f : 1.f / dx, iy = par_y ? 0.f : 1.f / dy;
-  for (int b = 0; b < nbox; ++b) {
-    if (!s.occ_on[b]) continue;
-    const float* o = s.occ + 4 * b;
+  const int nbox = s.misc[kOccBoxes], nall = s.misc[kOccAll];
+  for (int u = 0; u < nbox; ++u) {
+    const float* o = s.occ + 4 * s.occ_list[u];
     if ((par_x && (lx < o[0] || lx > o[1])) || (par_y && (ly < o[2] || ly > o[3]))) continue;
     const float tx0 = (o[0] - lx) * ix, tx1 = (o[1] - lx) * ix;
     const float ty0 = (o[2] - ly) * iy, ty1 = (o[3] - ly) * iy;
@@ -385,9 +414,8 @@ AD_HD bool sense_occluded(const SenseScratch& s, float lx, float ly, float dx, f
     if (fminf(fminf(fx, fy), .98f) >= fmaxf(fmaxf(nx, ny), .02f)) return true;
   }
   const float inv_den = 1.f / fmaxf(dx * dx + dy * dy, 1e-8f);
-  for (int q = nbox; q < nall; ++q) {
-    if (!s.occ_on[q]) continue;
-    const float* o = s.occ + 4 * q;
+  for (int u = nbox; u < nall; ++u) {
+    const float* o = s.occ + 4 * s.occ_list[u];
     const float t = ((o[0] - lx) * dx + (o[1] - ly) * dy) * inv_den;
     if (!(t > .02f && t < .98f)) continue;
     const float cx = lx + t * dx - o[0], cy = ly + t * dy - o[1];
@@ -410,7 +438,6 @@ AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e
   sense_build_occluders(w, sp, s, e, r, lx, ly, hx, hy, hf, full_fov);
   PAR_FOR(b, kDepthBins) { s.bins[b] = float_bits(kInf); }
   BARRIER();
-  const int nb = sp.num_boxes, nr = sp.num_boxes + sp.R;
   const float range2 = sp.perception_range * sp.perception_range, cos_hf = cosf(hf);
   PAR_FOR(i, P) {
     bool vis = s.pfree[i] != 0;
@@ -419,7 +446,7 @@ AD_HD int sense_lens(const World& w, const SimParams& sp, SenseScratch& s, int e
       const float d2 = dx * dx + dy * dy;
       vis = d2 <= range2;
       if (vis && !full_fov) vis = hx * dx + hy * dy >= cos_hf * sqrtf(d2);
-      if (vis) vis = !sense_occluded(s, lx, ly, dx, dy, nb, nr);
+      if (vis) vis = !sense_occluded(s, lx, ly, dx, dy);
     }
     s.flag[i] = vis ? 1 : 0;
   }
