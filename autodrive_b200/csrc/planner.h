@@ -220,15 +220,6 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
     int ix = c / ny, iy = c % ny;
     float x = cell_x(sp, ix), y = cell_y(sp, iy);
     bool b = x < ex || x > sp.field_length - ex || y < ey || y > sp.field_width - ey;
-    for (int k = 0; k < sp.num_boxes && !b; ++k) {
-      const Box& bx = sp.boxes[k];
-      float dx = x - bx.cx, dy = y - bx.cy;
-      if (fabsf(dx) > bx.hx + ex || fabsf(dy) > bx.hy + ey) continue;
-      float fwd = dx * ch + dy * sh, lat = -dx * sh + dy * ch;
-      float sf = q.length * .5f + bx.hx * ac + bx.hy * as;
-      float sl = q.width * .5f + bx.hx * as + bx.hy * ac;
-      b = fabsf(fwd) <= sf && fabsf(lat) <= sl;
-    }
     for (int k = 0; k < q.num_obst && !b; ++k) {
       float rr = q.obst[k * 3 + 2];
       if (!(rr > 0.f)) continue;
@@ -236,6 +227,28 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
       b = sqr(x - q.obst[k * 3]) + sqr(y - q.obst[k * 3 + 1]) <= cl * cl;
     }
     ps.blocked[c] = b ? 1 : 0;
+  }
+  BARRIER();
+  // solid boxes: each box tests only the cells of its inflated bounding
+  // rectangle (one cell of margin; the exact per-cell test decides) and
+  // marks the ones its rotated footprint covers, instead of every cell
+  // testing every box
+  for (int k = 0; k < sp.num_boxes; ++k) {
+    const Box& bx = sp.boxes[k];
+    const float sf = q.length * .5f + bx.hx * ac + bx.hy * as;
+    const float sl = q.width * .5f + bx.hx * as + bx.hy * ac;
+    const int ix0 = clampi((int)floorf((bx.cx - bx.hx - ex) / sp.plan_res) - 1, 0, nx - 1);
+    const int ix1 = clampi((int)floorf((bx.cx + bx.hx + ex) / sp.plan_res) + 1, 0, nx - 1);
+    const int iy0 = clampi((int)floorf((bx.cy - bx.hy - ey) / sp.plan_res) - 1, 0, ny - 1);
+    const int iy1 = clampi((int)floorf((bx.cy + bx.hy + ey) / sp.plan_res) + 1, 0, ny - 1);
+    const int span = iy1 - iy0 + 1;
+    PAR_FOR(u, (ix1 - ix0 + 1) * span) {
+      const int ix = ix0 + u / span, iy = iy0 + u % span;
+      const float dx = cell_x(sp, ix) - bx.cx, dy = cell_y(sp, iy) - bx.cy;
+      if (fabsf(dx) > bx.hx + ex || fabsf(dy) > bx.hy + ey) continue;
+      const float fwd = dx * ch + dy * sh, lat = -dx * sh + dy * ch;
+      if (fabsf(fwd) <= sf && fabsf(lat) <= sl) ps.blocked[cell_index(sp, ix, iy)] = 1;
+    }
   }
   BARRIER();
   PLAN_MARK(ps, 0);   // occupancy grid
