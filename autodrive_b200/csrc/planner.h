@@ -314,12 +314,18 @@ AD_HD void plan_route(World& w, const SimParams& sp, int e, int r, const PlanReq
   PAR_FOR(c, nc) {
     ps.value[c] = c == gcell ? 0.f : 1.e6f;
     const int ix = c / ny, iy = c % ny;
-    unsigned m = ps.blocked[c] ? 512u : 0u;
+    // the 3 x 3 neighbourhood's free flags, read once (outside the grid: not free)
+    bool fr[3][3];
+    for (int a = 0; a < 3; ++a)
+      for (int b = 0; b < 3; ++b) {
+        const int jx = ix + a - 1, jy = iy + b - 1;
+        fr[a][b] = jx >= 0 && jx < nx && jy >= 0 && jy < ny && !ps.blocked[cell_index(sp, jx, jy)];
+      }
+    unsigned m = fr[1][1] ? 0u : 512u;
     for (int k = 0; k < 8; ++k) {
-      const int jx = ix + dxs[k], jy = iy + dys[k];
-      if (jx < 0 || jx >= nx || jy < 0 || jy >= ny) continue;
-      if (ps.blocked[cell_index(sp, jx, jy)]) continue;
-      if (k >= 4 && (ps.blocked[cell_index(sp, jx, iy)] || ps.blocked[cell_index(sp, ix, jy)])) continue;
+      const int a = dxs[k] + 1, b = dys[k] + 1;
+      if (!fr[a][b]) continue;
+      if (k >= 4 && (!fr[a][1] || !fr[1][b])) continue;
       m |= 1u << k;
     }
     if (cell_on_bump(sp, cell_x(sp, ix), cell_y(sp, iy))) m |= 256u;
